@@ -1,0 +1,395 @@
+#!/usr/bin/env python3
+"""Benchmark of the block-128 4-bit LLaMA token loop on B200.
+
+Workload (one "step" = one greedy decode token of one sequence per GPU): the LLaMA-3.2-1B shape
+(16 layers, dim 2048, ffn 8192, vocab 128256, 32/8 heads) with seeded random-init weights
+quantised to the LLM4S128 block-128 4-bit format; a 32-token prompt is prefilled, then the
+128-token greedy generation at positions 31..158 is repeated until K steps are timed.  Every
+step streams all 657 MB of weights, far more than the 126 MB L2, so no flush is needed between
+steps.  With N GPUs every rank decodes its own sequence (independent replicas, weak scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  ``value`` is device-resident throughput (CUDA events around K
+graph steps fed by the on-device argmax), ``e2e`` is the same loop through the reference C ABI
+(forward_token + sample per step from the host).  ``--impl reference`` times the reference
+engine itself (compiled from its own source) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib.util
+import json
+import math
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "llama3-signed-4bit_b200"
+METRIC = "decode tok/s (1B, 4-bit b128) at batch 1 and 64; GEMV HBM GB/s vs peak"
+PROMPT_LEN = 32
+GEN_LEN = 128
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_package():
+    name = "llama3_signed_4bit_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, PKG_DIR / "__init__.py",
+                                                  submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def cache_dir() -> Path:
+    d = Path(os.environ.get("LLAMA_B200_CACHE", Path(tempfile.gettempdir()) / "llama3_b200_cache"))
+    d.mkdir(parents=True, exist_ok=True)
+    return d
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        v = float(json.loads(p.read_text())["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# algorithmic bytes (weights + activations + KV actually required by the math)
+# ---------------------------------------------------------------------------------------------
+def phase_bytes(shape, pos: int) -> dict:
+    d, f, kv, v = shape.dim, shape.ffn, shape.kv_dim, shape.vocab
+    mat = lambda n, k: n * (k // 128) * 68  # noqa: E731
+    return {
+        "qkv": mat(d + 2 * kv, d) + 4 * (3 * d + d + 2 * kv),          # W, x + norm, out
+        "attn": 2 * 4 * kv * (pos + 1) + 4 * (d + 2 * kv + d),          # K/V rows, q/k/v in, out
+        "oproj": mat(d, d) + 4 * (d + 2 * d),                           # W, attn in, x rw
+        "gateup": 2 * mat(f, d) + 4 * (2 * d + f),                       # Wg+Wu, x + norm, act
+        "down": mat(d, f) + 4 * (f + 2 * d),                            # W, act, x rw
+        "lmhead": mat(v, d) + 4 * (2 * d + v),                           # W, x + norm, logits
+    }
+
+
+def token_bytes(shape, pos: int) -> int:
+    """Weights + norms + KV read (pos+1 rows incl. the new one) + KV write, per token."""
+    kv_row = shape.layers * shape.kv_dim * 4 * 2
+    return shape.weight_bytes() + kv_row * (pos + 1) + kv_row
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        self.out.flush()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) in self.gpus:
+                    rows.append(parts)
+            except ValueError:
+                pass
+        os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------
+# reference / oracle on the host (CPU baseline)
+# ---------------------------------------------------------------------------------------------
+def _cpu_decode_worker(args):
+    model_path, n_tokens, n_warm, use_ref = args
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    if use_ref:
+        lib = oracle.load_ref_engine()
+        h = lib.llama_engine_create(str(model_path).encode())
+        fwd = lambda t, p: lib.llama_engine_forward_token(h, t, p, 1)  # noqa: E731
+        smp = lambda: lib.llama_engine_sample(h, ctypes.c_float(0.0), ctypes.c_float(0.9))  # noqa: E731
+    else:
+        lib = oracle.load_oracle()
+        h = lib.orc_create(str(model_path).encode())
+        fwd = lambda t, p: lib.orc_forward_token(h, t, p, 1)  # noqa: E731
+        smp = lambda: lib.orc_sample_engine(h, ctypes.c_float(0.0), ctypes.c_float(0.9))  # noqa: E731
+    tok = 128000
+    for p in range(n_warm):
+        fwd(tok, p)
+        tok = smp()
+    t0 = time.perf_counter()
+    for p in range(n_warm, n_warm + n_tokens):
+        fwd(tok, p)
+        tok = smp()
+    return time.perf_counter() - t0
+
+
+def cpu_decode_rate(model_path, n_proc, n_tokens, n_warm):
+    import oracle
+    oracle.build()
+    use_ref = oracle.have_reference()
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(n_proc) as pool:
+        times = pool.map(_cpu_decode_worker, [(str(model_path), n_tokens, n_warm, use_ref)] * n_proc)
+    rate = n_proc * n_tokens / max(times)
+    return rate, ("reference" if use_ref else "port")
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    pkg = load_package()
+    shape = pkg.model_file.LLAMA_3_2_1B
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+    if rank == 0:
+        pkg.build.build_all()
+        model = pkg.model_file.cached_model(cache_dir(), shape, seed=0, sigma=0.02)
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        model = pkg.model_file.cached_model(cache_dir(), shape, seed=0, sigma=0.02)
+    import numpy as np
+
+    bindings = pkg.LlamaEngineBindings()
+    eng = pkg.LlamaEngine(str(model), bindings, device=local_rank, max_batch=1, max_seq_len=0)
+    lib = bindings.lib
+    stream = torch.cuda.ExternalStream(lib.llama_engine_get_stream(eng.handle))
+    prompt = np.random.default_rng(1000 + rank).integers(0, shape.vocab, PROMPT_LEN).astype(np.int32)
+    eng.prefill([int(t) for t in prompt[:-1]], 0, False)
+    first, start = int(prompt[-1]), PROMPT_LEN - 1
+
+    def device_steps(n):
+        """n greedy steps in chunks of the 128-token generation (positions 31..158)."""
+        done = 0
+        while done < n:
+            c = min(GEN_LEN, n - done)
+            eng.generate_greedy(first, start, c)
+            done += c
+
+    device_steps(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(range(world) if world > 1 else [local_rank]) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        device_steps(args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    clocks = clk.summary() if rank == 0 else None
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * args.steps / (ms / 1e3)
+
+    # e2e through the reference ABI: forward_token + sample(0) per step, from the host
+    def host_steps(n):
+        done = 0
+        while done < n:
+            tok, pos = first, start
+            for _ in range(min(GEN_LEN, n - done)):
+                lib.llama_engine_forward_token(eng.handle, tok, pos, 1)
+                tok = lib.llama_engine_sample(eng.handle, ctypes.c_float(0.0), ctypes.c_float(0.9))
+                pos += 1
+                done += 1
+
+    host_steps(min(args.warmup, GEN_LEN))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    w0 = time.perf_counter()
+    host_steps(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms, wall * 1e3], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms, wall = float(t[0].item()), float(t[1].item()) / 1e3
+    e2e_value = world * args.steps / max(e2e_ms / 1e3, wall)
+
+    # per-phase live timing for the roofline of the dominant kernel
+    peak, peak_kind = hbm_peak()
+    avg_pos = start + (GEN_LEN - 1) / 2.0
+    pb = phase_bytes(shape, int(avg_pos))
+    launches = {"qkv": shape.layers, "attn": shape.layers, "oproj": shape.layers, "gateup": shape.layers,
+                "down": shape.layers, "lmhead": 1}
+    phase_ms = {}
+    for ph in launches:
+        out = ctypes.c_float(0.0)
+        iters = 64 if ph != "lmhead" else 16
+        lib.llama_engine_profile_phase(eng.handle, ph.encode(), 4, ctypes.byref(out))
+        rc = lib.llama_engine_profile_phase(eng.handle, ph.encode(), iters, ctypes.byref(out))
+        phase_ms[ph] = float(out.value) if rc == 0 else float("nan")
+    share = {ph: phase_ms[ph] * launches[ph] for ph in launches}
+    dom = max(share, key=share.get)
+    achieved = pb[dom] / (phase_ms[dom] / 1e3) / 1e9
+    traffic = read_traffic(dom)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": pb[dom], "launch_ms": round(phase_ms[dom], 5),
+                "phase_ms": {k: round(v, 5) for k, v in phase_ms.items()},
+                "phase_share": {k: round(v / sum(share.values()), 4) for k, v in share.items()}}
+    bytes_tok = sum(token_bytes(shape, p) for p in range(start, start + GEN_LEN)) / GEN_LEN
+    step_gbs = bytes_tok * (value / world) / 1e9
+    step_roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(step_gbs / peak, 4), "bytes_per_token": int(bytes_tok),
+                     "ideal_tok_s_per_gpu": round(peak * 1e9 / bytes_tok, 1)}
+
+    result = None
+    if rank == 0:
+        kernels_per_token = 1 + 5 * shape.layers + 2
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            rate, kind = cpu_decode_rate(model, 1, args.cpu_tokens, 1)
+            cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": 1, "kind": kind,
+                   "sample": f"{args.cpu_tokens} greedy decode tokens (forward_token + sample) of the same model "
+                             f"after 1 warm-up token, one process, 1 thread"}
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "decode-b1: LLaMA-3.2-1B shape, LLM4S128 block-128 4-bit, seeded random-init "
+                                   "N(0,0.02) weights, batch 1 per GPU, greedy, 128-token generation at positions "
+                                   "31..158 repeated",
+                       "global_batch": world, "seq_len": start + GEN_LEN, "parallelism": f"dp{world} (replicas)",
+                       "l2": "no flush: 657 MB of weights streamed per step > 126 MB L2"},
+            "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4,
+                    "api": "llama_engine_forward_token + llama_engine_sample per step (C ABI via ctypes)",
+                    "wall_s": round(wall, 4)},
+            "gpu_launches": kernels_per_token * args.steps, "clocks": clocks,
+        }
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def read_traffic(kernel_phase: str):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic_per_launch.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel_phase:
+            try:
+                return int(float(parts[1]))
+            except ValueError:
+                return None
+    return None
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    pkg = load_package()
+    shape = pkg.model_file.LLAMA_3_2_1B
+    model = pkg.model_file.cached_model(cache_dir(), shape, seed=0, sigma=0.02)
+    n_proc = max(1, min(host_cores(), 32))
+    steps = max(1, min(args.steps, args.ref_max_steps))
+    warm = max(1, min(args.warmup, 2))
+    rate, kind = cpu_decode_rate(model, n_proc, steps, warm)
+    sample = (f"{n_proc} concurrent processes (one sequence each, 1 thread each; the reference is serial on "
+              f"Linux), {warm} warm-up + {steps} timed greedy decode tokens per process")
+    return {"impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s", "n_gpus": 0,
+            "steps": steps, "warmup": warm, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "decode-b1: LLaMA-3.2-1B shape, LLM4S128 block-128 4-bit, seeded random-init, "
+                                   "greedy, one sequence per process"},
+            "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": n_proc, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3840)
+    ap.add_argument("--warmup", type=int, default=256)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-tokens", type=int, default=12)
+    ap.add_argument("--ref-max-steps", type=int, default=12)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+    else:
+        res = run_ours(args, rank, world, local_rank)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

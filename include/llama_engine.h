@@ -1,0 +1,154 @@
+/*
+ * llama_engine.h — C ABI of the B200 (sm_100a) engine for the llama3-signed-4bit token loop.
+ *
+ * Part 1 is the reference's ABI, unchanged in names, argument meaning and error behaviour, so
+ * that the reference's callers (src/main.py ctypes bindings at :57-140, src/main.cpp,
+ * tests/lm_eval_adapter.py) can load this library in place of the reference build.  Each entry
+ * point cites the declaration it replaces (src/llama_engine.h) and the reference implementation
+ * (src/llama_engine.cpp).
+ *
+ * Part 2 holds additive extensions (device selection, batched decode over independent
+ * sequences, a device-resident greedy loop, the isolated block-128 GEMV).  No reference caller
+ * needs them.
+ *
+ * Device residency: weights, KV caches, activations and logits live in GPU memory.
+ * llama_engine_get_logits() returns a host pointer to a pinned mirror that is refreshed on
+ * each call when the device logits are newer; the pointer stays valid until llama_engine_free(),
+ * and its contents are current as of the last get_logits() call.
+ *
+ * Threading: one engine handle must not be used from two host threads at once (the reference
+ * shares scratch buffers per handle in the same way).  Separate handles are independent.
+ */
+#ifndef LLAMA_ENGINE_H
+#define LLAMA_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* llama_engine_t;     /* src/llama_engine.h:12 */
+typedef void* llama_tokenizer_t;  /* src/llama_engine.h:13 */
+
+/* ---------------------------------------------------------------------------------------- */
+/* Part 1: the reference ABI                                                                 */
+/* ---------------------------------------------------------------------------------------- */
+
+/* src/llama_engine.h:20, impl src/llama_engine.cpp:1051-1059.  Loads an LLM4S128 file onto
+ * CUDA device 0 (or $LLAMA_ENGINE_DEVICE).  Returns NULL on any failure: missing file, bad
+ * magic, a file shorter than its header implies, unsupported geometry, or a CUDA error. */
+llama_engine_t llama_engine_create(const char* model_path);
+
+/* src/llama_engine.h:23, impl :1061-1065.  NULL is a no-op. */
+void llama_engine_free(llama_engine_t engine);
+
+/* src/llama_engine.h:26, impl :1067-1071 and :930-933.  A no-op: KV positions are simply
+ * overwritten from pos 0 by the next sequence, as in the reference. */
+void llama_engine_reset(llama_engine_t engine);
+
+/* src/llama_engine.h:29-36, impl :1073-1110.  0 for a NULL handle; get_max_seq_len ignores
+ * the handle and returns 8192 (MAX_SEQ_LEN, src/llama_engine.cpp:26). */
+int32_t llama_engine_get_num_layers(llama_engine_t engine);
+int32_t llama_engine_get_dim(llama_engine_t engine);
+int32_t llama_engine_get_ffn_dim(llama_engine_t engine);
+int32_t llama_engine_get_vocab_size(llama_engine_t engine);
+int32_t llama_engine_get_num_heads(llama_engine_t engine);
+int32_t llama_engine_get_num_kv_heads(llama_engine_t engine);
+int32_t llama_engine_get_head_dim(llama_engine_t engine);
+int32_t llama_engine_get_max_seq_len(llama_engine_t engine);
+
+/* src/llama_engine.h:40, impl :1112-1116 and :935-1042.  Runs one token through all layers
+ * at position pos of sequence slot 0, writing its K/V rows, and the lm_head when
+ * compute_logits != 0.  pos >= 8192 is a silent no-op; an out-of-range token id is replaced by
+ * 0 (both as in the reference).  Returns 0, or -1 for a NULL handle or a CUDA error.  The call
+ * is stream-ordered: it returns once the work is queued on the GPU. */
+int llama_engine_forward_token(llama_engine_t engine, int32_t token_id, size_t pos, int compute_logits);
+
+/* src/llama_engine.h:44, impl :1118-1127.  Same result as count forward_token calls at
+ * start_pos..start_pos+count-1 with logits only for the last one (if compute_last_logits).
+ * Returns -1 for a NULL handle or NULL token_ids. */
+int llama_engine_prefill(llama_engine_t engine, const int32_t* token_ids, size_t count, size_t start_pos, int compute_last_logits);
+
+/* src/llama_engine.h:47, impl :1129-1133 and :784-839.  temperature <= 0.01: greedy argmax
+ * (first index among equal maxima).  Otherwise the logits are overwritten in place with
+ * probabilities (temperature, softmax), the 64 most probable ids are kept in descending order,
+ * and libc rand() draws within the top_p mass, as in the reference.  0 for a NULL handle. */
+int32_t llama_engine_sample(llama_engine_t engine, float temperature, float top_p);
+
+/* src/llama_engine.h:50, impl :1135-1138.  Host pointer to vocab_size floats (see top). */
+const float* llama_engine_get_logits(llama_engine_t engine);
+
+/* src/llama_engine.h:53, impl :1140-1144 and :182-220.  Dequantises embedding row token_id
+ * (of the tied lm_head) into out_x[dim] on the host side.  No-op for NULL arguments or an
+ * out-of-range token id. */
+void llama_engine_dequantize_embedding(llama_engine_t engine, size_t token_id, float* out_x);
+
+/* src/llama_engine.h:59-62, impl :1146-1178.  Byte-level BPE tokenizer over a HF
+ * tokenizer.json (host code; not on the GPU path).  encode returns the number of ids written
+ * (0 on bad arguments); decode returns a string owned by the tokenizer, valid until the next
+ * decode call on it ("" for unknown ids). */
+llama_tokenizer_t llama_tokenizer_create(const char* tokenizer_path);
+void llama_tokenizer_free(llama_tokenizer_t tokenizer);
+int llama_tokenizer_encode(llama_tokenizer_t tokenizer, const char* text, int32_t* out_tokens, int max_tokens);
+const char* llama_tokenizer_decode(llama_tokenizer_t tokenizer, int32_t token_id);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Part 2: extensions (no counterpart in the reference ABI)                                  */
+/* ---------------------------------------------------------------------------------------- */
+
+/* Like llama_engine_create, on CUDA device `device`, with KV caches for `max_batch`
+ * independent sequence slots of `max_seq_len` positions each (max_seq_len <= 8192; 0 means
+ * 8192).  Slot 0 is the sequence used by the Part-1 calls.  NULL on failure. */
+llama_engine_t llama_engine_create_ex(const char* model_path, int device, int max_batch, int max_seq_len);
+
+/* Message of the last failure on this handle (or of the last failed create when engine is
+ * NULL).  Never NULL. */
+const char* llama_engine_last_error(llama_engine_t engine);
+
+/* Device-resident greedy loop, equal to n_steps x { forward_token(tok, pos, 1); tok =
+ * sample(0, .) ; pos++ } starting from (first_token, start_pos) on slot 0.  Writes the n_steps
+ * sampled ids to out_tokens (host memory).  Returns 0, or -1 on error / pos overflow. */
+int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_token, size_t start_pos,
+                                 int32_t n_steps, int32_t* out_tokens);
+
+/* Batched decode: one step for n independent sequences.  Row i feeds tokens[i] at positions[i]
+ * into sequence slot slots[i] (slots distinct, < max_batch; positions < max_seq_len).  Host
+ * arrays.  compute_logits != 0 also runs the lm_head for every row.  Returns 0 or -1. */
+int llama_engine_forward_batch(llama_engine_t engine, const int32_t* tokens, const int32_t* positions,
+                               const int32_t* slots, int n, int compute_logits);
+
+/* Greedy ids (first index among equal maxima) of the n rows of the last forward_batch. */
+int llama_engine_argmax_batch(llama_engine_t engine, int32_t* out_tokens, int n);
+
+/* Host pointer to the logits of row `row` of the last forward_batch (vocab_size floats,
+ * refreshed by this call).  NULL on error. */
+const float* llama_engine_get_logits_batch(llama_engine_t engine, int row);
+
+/* Isolated block-128 GEMV, y[m][n] = sum_k w[n][k] * x[m][k] with w = min + q*step, for the M
+ * rows of x (1 <= M <= 8), all pointers in device memory with the LLM4S128 matrix layout
+ * (nibbles[N*K/2], step_bf16[N*K/128], min_bf16[N*K/128]).  K % 128 == 0.  `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  Counterpart of the reference's file-local
+ * signed_4bit_b128_gemv (src/llama_engine.cpp:233-357), which receives the block sums of x
+ * precomputed; here they are computed inside the kernel.  Returns 0, or -1 on bad arguments /
+ * launch error. */
+int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
+                    int N, int K, const float* x, int M, float* y, void* stream);
+
+/* The cudaStream_t on which the engine enqueues all of its work (for CUDA-event timing and
+ * stream ordering by the caller).  NULL for a NULL handle. */
+void* llama_engine_get_stream(llama_engine_t engine);
+
+/* Diagnostics: enqueues `iters` launches of one phase of the token step on the engine stream,
+ * cycling through the layers (so consecutive launches read different weights), between two
+ * CUDA events, and returns the average time per launch in *avg_ms.  Phases: "qkv", "attn",
+ * "oproj", "gateup", "down", "lmhead", "step" (one whole token, graph launch).  Returns 0 or -1.
+ * Activations are whatever the last step left; the numbers are timings only. */
+int llama_engine_profile_phase(llama_engine_t engine, const char* phase, int iters, float* avg_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLAMA_ENGINE_H */

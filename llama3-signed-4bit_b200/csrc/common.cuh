@@ -1,0 +1,72 @@
+// Shared device helpers for the sm_100a kernels of the block-128 4-bit engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define LE_MAX_SEQ_LEN 8192  // MAX_SEQ_LEN, src/llama_engine.cpp:26
+#define LE_HEAD_DIM 64       // head_dim fixed by the reference's attention loops (:978, :1010, :1017)
+
+// One quantised matrix on the device, in the LLM4S128 layout: row n owns K/128 consecutive
+// blocks; a block is 64 bytes of nibbles (low nibble = even element) and one bf16 step and
+// one bf16 min (src/llama_engine.cpp:156-180).
+struct QMat {
+  const uint8_t* nib;    // [N][K/2]
+  const uint16_t* step;  // [N][K/128] bf16 bits
+  const uint16_t* mn;    // [N][K/128] bf16 bits
+  int N, K;
+};
+
+// bf16 -> fp32 is a 16-bit shift (src/llama_engine.cpp:28-33).
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Streaming 16-byte load of weights: read once per token, so keep them out of L1.
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Exact float value of a 4-bit code held in the low bits of `q` (q < 16): the bit pattern
+// 0x4B000000 | q is 2^23 + q, and subtracting 2^23 is exact.
+__device__ __forceinline__ float nib_to_f32(uint32_t q) {
+  return __uint_as_float(0x4B000000u | q) - 8388608.0f;
+}
+
+// Block-wide sum for blockDim.x threads (a multiple of 32, at most 1024).  `red` must hold 32
+// floats of shared memory.  Every thread receives the total.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : -INFINITY;
+  t = warp_max(t);
+  return t;
+}

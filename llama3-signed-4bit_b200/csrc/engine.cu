@@ -1,0 +1,781 @@
+// Engine state and the llama_engine.h C ABI for the B200 (sm_100a) build.
+//
+// Host side of the drop-in: parses and validates the LLM4S128 file (the reference does the same
+// parse without validation, src/llama_engine.cpp:865-906), uploads every array into one device
+// arena, builds the RoPE table on the host with the reference's own libm calls (:908-917) so
+// the table is bit-identical, allocates device KV caches, and captures the per-token kernel
+// sequence into CUDA graphs.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "decode_kernels.cuh"
+#include "llama_engine.h"
+
+#define LE_API extern "C" __attribute__((visibility("default")))
+
+namespace le {
+
+static std::mutex g_err_mu;
+static std::string g_create_error = "";
+
+static void set_create_error(const std::string& s) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  g_create_error = s;
+}
+
+// Restores the caller's current CUDA device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+struct FileMatrix {
+  uint32_t N = 0, K = 0, nb = 0;
+  size_t nib_off = 0, step_off = 0, min_off = 0;  // byte offsets into the file
+};
+
+struct FileLayer {
+  size_t in_norm_off = 0, post_norm_off = 0;
+  FileMatrix m[7];  // q k v o gate up down
+};
+
+struct ParsedFile {
+  uint32_t layers, dim, ffn, vocab, heads, kv_heads, block;
+  size_t final_norm_off;
+  std::vector<FileLayer> L;
+  FileMatrix lm_head;
+};
+
+// Parses the header and walks the matrix records, checking every size against the file length.
+static bool parse_file(const uint8_t* base, size_t size, ParsedFile& P, std::string& err) {
+  if (size < 36) { err = "file shorter than the LLM4S128 header"; return false; }
+  if (std::memcmp(base, "LLM4S128", 8) != 0) { err = "bad magic (expected LLM4S128)"; return false; }
+  uint32_t h[7];
+  std::memcpy(h, base + 8, 28);
+  P.layers = h[0]; P.dim = h[1]; P.ffn = h[2]; P.vocab = h[3]; P.heads = h[4]; P.kv_heads = h[5]; P.block = h[6];
+  if (P.block != 128) { err = "block size must be 128"; return false; }
+  if (P.layers == 0 || P.dim == 0 || P.ffn == 0 || P.vocab == 0 || P.heads == 0 || P.kv_heads == 0 ||
+      P.dim % P.heads != 0 || P.heads % P.kv_heads != 0) {
+    err = "inconsistent model dimensions"; return false;
+  }
+  if (P.dim / P.heads != LE_HEAD_DIM) { err = "head_dim must be 64"; return false; }
+  if (P.dim % 1024 != 0 || P.ffn % 1024 != 0) { err = "dim and ffn_dim must be multiples of 1024"; return false; }
+  if (P.dim > 16384 || P.ffn > 65536 || P.layers > 1024) { err = "model dimensions out of supported range"; return false; }
+  size_t off = 36;
+  auto need = [&](size_t n) { return off + n <= size; };
+  auto take_norm = [&](size_t& where) -> bool {
+    if (!need((size_t)P.dim * 4)) return false;
+    where = off; off += (size_t)P.dim * 4; return true;
+  };
+  auto take_mat = [&](FileMatrix& m, uint32_t N, uint32_t K) -> bool {
+    if (!need(12)) return false;
+    uint32_t hh[3];
+    std::memcpy(hh, base + off, 12);
+    off += 12;
+    if (hh[0] != N || hh[1] != K || (uint64_t)hh[2] != (uint64_t)N * (K / 128)) return false;
+    m.N = N; m.K = K; m.nb = hh[2];
+    if (!need((size_t)m.nb * 68)) return false;
+    m.nib_off = off; off += (size_t)m.nb * 64;
+    m.step_off = off; off += (size_t)m.nb * 2;
+    m.min_off = off; off += (size_t)m.nb * 2;
+    return true;
+  };
+  if (!take_norm(P.final_norm_off)) { err = "file truncated (final_norm)"; return false; }
+  const uint32_t kvd = P.kv_heads * LE_HEAD_DIM;
+  const uint32_t shapes[7][2] = {{P.dim, P.dim}, {kvd, P.dim}, {kvd, P.dim}, {P.dim, P.dim},
+                                 {P.ffn, P.dim}, {P.ffn, P.dim}, {P.dim, P.ffn}};
+  P.L.resize(P.layers);
+  for (uint32_t l = 0; l < P.layers; ++l) {
+    if (!take_norm(P.L[l].in_norm_off) || !take_norm(P.L[l].post_norm_off)) {
+      err = "file truncated (layer norms)"; return false;
+    }
+    for (int i = 0; i < 7; ++i)
+      if (!take_mat(P.L[l].m[i], shapes[i][0], shapes[i][1])) {
+        err = "matrix record " + std::to_string(i) + " of layer " + std::to_string(l) +
+              " is truncated or has an unexpected shape";
+        return false;
+      }
+  }
+  if (!take_mat(P.lm_head, P.vocab, P.dim)) { err = "lm_head record truncated or mis-shaped"; return false; }
+  return true;
+}
+
+struct DevLayer {
+  const float* in_norm;
+  const float* post_norm;
+  QMat q, k, v, o, g, u, d;
+};
+
+constexpr int kRing = 64;
+
+struct Engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t layers = 0, dim = 0, ffn = 0, vocab = 0, heads = 0, kv_heads = 0, kv_dim = 0;
+  int max_batch = 1, max_seq = LE_MAX_SEQ_LEN;
+  int num_sms = 148;
+
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  const float* final_norm = nullptr;
+  std::vector<DevLayer> L;
+  QMat lm_head{};
+
+  float* rope_cos = nullptr;  // [LE_MAX_SEQ_LEN][32], bit-identical to the reference table
+  float* rope_sin = nullptr;
+  float* kcache = nullptr;    // [slot][layer][max_seq][kv_dim]
+  float* vcache = nullptr;
+
+  // activations
+  float* x = nullptr;      // [max_batch][dim]   residual stream
+  float* qkv = nullptr;    // [max_batch][dim + 2 kv_dim]
+  float* attn = nullptr;   // [max_batch][dim]
+  float* act = nullptr;    // [max_batch][ffn]
+  float* logits = nullptr; // [max_batch][vocab]
+  float* emb = nullptr;    // [dim] scratch for llama_engine_dequantize_embedding
+  float* red = nullptr;    // [2048] partial reductions of the sampler
+  int32_t* d_misc = nullptr;  // [16] small device scalars (embedding row id)
+  ArgmaxPart* part = nullptr;  // [max_batch][lm_grid]
+  int32_t* am_result = nullptr;  // [max_batch]
+  int32_t* token_log = nullptr;  // [LE_MAX_SEQ_LEN]
+  StepParams* d_params = nullptr;  // [max_batch]
+  int lm_grid = 0;
+
+  // host side
+  StepParams* h_ring = nullptr;  // pinned
+  cudaEvent_t ring_ev[kRing] = {};
+  bool ring_used[kRing] = {};
+  int ring_pos = 0;
+  float* h_logits = nullptr;  // pinned [max_batch][vocab]
+  int32_t* h_small = nullptr; // pinned scratch [LE_MAX_SEQ_LEN]
+  bool logits_on_host_fresh = false;   // slot-0 host mirror matches device
+  bool argmax_valid = false;           // am_result[0] holds greedy of current device logits
+  bool have_logits = false;
+
+  cudaGraphExec_t g_fwd[2] = {nullptr, nullptr};  // [compute_logits]
+  cudaGraphExec_t g_gen = nullptr;                // forward + greedy + advance
+
+  std::string err;
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+#define LE_CK(expr)                                                          \
+  do {                                                                       \
+    cudaError_t e_ = (expr);                                                 \
+    if (e_ != cudaSuccess) {                                                 \
+      E->err = std::string(#expr) + ": " + cudaGetErrorString(e_);           \
+      return false;                                                          \
+    }                                                                        \
+  } while (0)
+
+// ---------------------------------------------------------------------------------------------
+// Kernel sequence of one token for one sequence.
+// ---------------------------------------------------------------------------------------------
+static size_t gemv_smem(int K, int mx = 1) { return (size_t)mx * (K + K / 128) * 4 + 32 * 4 + 64; }
+
+static bool set_smem_attrs(Engine* E) {
+  LE_CK(cudaFuncSetAttribute(k_proj_residual<1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)gemv_smem(E->ffn)));
+  return true;
+}
+
+struct TokenBuffers {
+  const StepParams* prm;  // device params for this row
+  float* x;
+  float* qkv;
+  float* attn;
+  float* act;
+  float* kc;  // KV base of the slot (layer 0)
+  float* vc;
+  float* logits;  // nullptr: no lm_head
+  ArgmaxPart* part;
+  int32_t* result;
+  StepParams* prm_mut;  // for advance
+  int32_t* token_log;
+  int advance;
+};
+
+enum Phase { PH_QKV = 0, PH_ATTN, PH_OPROJ, PH_GATEUP, PH_DOWN, PH_LMHEAD };
+
+// Enqueues one phase of the token step for layer l (PH_LMHEAD ignores l).
+static void enqueue_phase(Engine* E, const TokenBuffers& B, int phase, uint32_t l, cudaStream_t s) {
+  const int dim = E->dim, ffn = E->ffn, kvd = E->kv_dim;
+  const size_t layer_stride = (size_t)E->max_seq * kvd;
+  const DevLayer& Ly = E->L[l];
+  switch (phase) {
+    case PH_QKV: {
+      const int grid = ((dim + 2 * kvd) / 2 + kWarps - 1) / kWarps;
+      k_qkv<2><<<grid, kThreads, gemv_smem(dim), s>>>(B.x, Ly.in_norm, Ly.q, Ly.k, Ly.v, B.qkv);
+      break;
+    }
+    case PH_ATTN: {
+      const size_t att_smem = (size_t)(64 * 3 + 32 + 256 + E->max_seq) * 4;
+      k_attention<<<E->heads, kThreads, att_smem, s>>>(B.qkv, B.kc + l * layer_stride, B.vc + l * layer_stride,
+                                                        E->rope_cos, E->rope_sin, B.prm, E->heads, E->kv_heads,
+                                                        B.attn);
+      break;
+    }
+    case PH_OPROJ:
+      k_proj_residual<1, 2><<<(dim + kWarps - 1) / kWarps, kThreads, gemv_smem(dim), s>>>(B.attn, Ly.o, B.x);
+      break;
+    case PH_GATEUP:
+      k_gateup<2><<<(ffn / 2 + kWarps - 1) / kWarps, kThreads, gemv_smem(dim), s>>>(B.x, Ly.post_norm, Ly.g, Ly.u,
+                                                                                   B.act);
+      break;
+    case PH_DOWN:
+      k_proj_residual<1, 8><<<(dim + kWarps - 1) / kWarps, kThreads, gemv_smem(ffn), s>>>(B.act, Ly.d, B.x);
+      break;
+    case PH_LMHEAD:
+      k_lmhead<2><<<E->lm_grid, kThreads, gemv_smem(dim), s>>>(B.x, E->final_norm, E->lm_head,
+                                                               B.logits ? B.logits : E->logits, B.part);
+      break;
+  }
+}
+
+static void enqueue_token(Engine* E, const TokenBuffers& B, cudaStream_t s) {
+  k_embed<<<1, kThreads, 0, s>>>(E->lm_head, B.prm, nullptr, B.x);
+  for (uint32_t l = 0; l < E->layers; ++l)
+    for (int ph = PH_QKV; ph <= PH_DOWN; ++ph) enqueue_phase(E, B, ph, l, s);
+  if (B.logits) {
+    enqueue_phase(E, B, PH_LMHEAD, 0, s);
+    k_argmax_finish<<<1, 1024, 0, s>>>(B.part, E->lm_grid, B.result, B.prm_mut, B.token_log, B.advance);
+  }
+}
+
+static TokenBuffers row_buffers(Engine* E, int row, int slot, bool logits, int advance) {
+  TokenBuffers B;
+  B.prm = E->d_params + row;
+  B.prm_mut = E->d_params + row;
+  B.x = E->x + (size_t)row * E->dim;
+  B.qkv = E->qkv + (size_t)row * (E->dim + 2 * E->kv_dim);
+  B.attn = E->attn + (size_t)row * E->dim;
+  B.act = E->act + (size_t)row * E->ffn;
+  const size_t slot_stride = (size_t)E->layers * E->max_seq * E->kv_dim;
+  B.kc = E->kcache + (size_t)slot * slot_stride;
+  B.vc = E->vcache + (size_t)slot * slot_stride;
+  B.logits = logits ? E->logits + (size_t)row * E->vocab : nullptr;
+  B.part = E->part + (size_t)row * E->lm_grid;
+  B.result = E->am_result + row;
+  B.token_log = E->token_log;
+  B.advance = advance;
+  return B;
+}
+
+static bool capture(Engine* E, const TokenBuffers& B, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  LE_CK(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
+  enqueue_token(E, B, E->stream);
+  cudaError_t ce = cudaStreamEndCapture(E->stream, &g);
+  if (ce != cudaSuccess) { E->err = std::string("capture: ") + cudaGetErrorString(ce); return false; }
+  ce = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) { E->err = std::string("instantiate: ") + cudaGetErrorString(ce); return false; }
+  return true;
+}
+
+static void destroy(Engine* E);
+
+static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
+  LE_CK(cudaSetDevice(E->device));
+  LE_CK(cudaDeviceGetAttribute(&E->num_sms, cudaDevAttrMultiProcessorCount, E->device));
+  LE_CK(cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking));
+  E->layers = P.layers; E->dim = P.dim; E->ffn = P.ffn; E->vocab = P.vocab;
+  E->heads = P.heads; E->kv_heads = P.kv_heads; E->kv_dim = P.kv_heads * LE_HEAD_DIM;
+
+  // ---- weight arena: every array 256-byte aligned ----
+  auto mat_bytes = [](const FileMatrix& m) {
+    return align_up((size_t)m.nb * 64, 256) + 2 * align_up((size_t)m.nb * 2, 256);
+  };
+  size_t total = align_up((size_t)P.dim * 4, 256);
+  for (const auto& Ly : P.L) {
+    total += 2 * align_up((size_t)P.dim * 4, 256);
+    for (int i = 0; i < 7; ++i) total += mat_bytes(Ly.m[i]);
+  }
+  total += mat_bytes(P.lm_head);
+  E->arena_bytes = total;
+  LE_CK(cudaMalloc(&E->arena, total));
+  size_t off = 0;
+  auto put = [&](size_t n) -> uint8_t* {
+    uint8_t* dst = E->arena + off;
+    off += align_up(n, 256);
+    return dst;
+  };
+  // Copy in large pieces straight from the mapping.
+  std::vector<std::pair<uint8_t*, std::pair<size_t, size_t>>> copies;
+  auto place = [&](size_t src_off, size_t n) -> uint8_t* {
+    uint8_t* d = put(n);
+    copies.push_back({d, {src_off, n}});
+    return d;
+  };
+  auto place_mat = [&](const FileMatrix& m) -> QMat {
+    QMat q;
+    q.N = (int)m.N; q.K = (int)m.K;
+    q.nib = place(m.nib_off, (size_t)m.nb * 64);
+    q.step = reinterpret_cast<const uint16_t*>(place(m.step_off, (size_t)m.nb * 2));
+    q.mn = reinterpret_cast<const uint16_t*>(place(m.min_off, (size_t)m.nb * 2));
+    return q;
+  };
+  E->final_norm = reinterpret_cast<const float*>(place(P.final_norm_off, (size_t)P.dim * 4));
+  E->L.resize(P.layers);
+  for (uint32_t l = 0; l < P.layers; ++l) {
+    DevLayer& D = E->L[l];
+    D.in_norm = reinterpret_cast<const float*>(place(P.L[l].in_norm_off, (size_t)P.dim * 4));
+    D.post_norm = reinterpret_cast<const float*>(place(P.L[l].post_norm_off, (size_t)P.dim * 4));
+    D.q = place_mat(P.L[l].m[0]); D.k = place_mat(P.L[l].m[1]); D.v = place_mat(P.L[l].m[2]);
+    D.o = place_mat(P.L[l].m[3]); D.g = place_mat(P.L[l].m[4]); D.u = place_mat(P.L[l].m[5]);
+    D.d = place_mat(P.L[l].m[6]);
+  }
+  E->lm_head = place_mat(P.lm_head);
+  for (auto& c : copies) LE_CK(cudaMemcpy(c.first, base + c.second.first, c.second.second, cudaMemcpyHostToDevice));
+
+  // ---- RoPE table on the host, same float calls as src/llama_engine.cpp:911-917 ----
+  {
+    const size_t hd2 = LE_HEAD_DIM / 2;
+    std::vector<float> cs((size_t)LE_MAX_SEQ_LEN * hd2), sn((size_t)LE_MAX_SEQ_LEN * hd2);
+    for (size_t pos = 0; pos < LE_MAX_SEQ_LEN; ++pos) {
+      for (size_t i = 0; i < hd2; ++i) {
+        float theta = std::pow(500000.0f, -2.0f * static_cast<float>(i) / static_cast<float>(LE_HEAD_DIM));
+        cs[pos * hd2 + i] = std::cos(static_cast<float>(pos) * theta);
+        sn[pos * hd2 + i] = std::sin(static_cast<float>(pos) * theta);
+      }
+    }
+    LE_CK(cudaMalloc(&E->rope_cos, cs.size() * 4));
+    LE_CK(cudaMalloc(&E->rope_sin, sn.size() * 4));
+    LE_CK(cudaMemcpy(E->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    LE_CK(cudaMemcpy(E->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  }
+
+  // ---- KV caches and activations ----
+  const size_t kv_elems = (size_t)E->max_batch * E->layers * E->max_seq * E->kv_dim;
+  LE_CK(cudaMalloc(&E->kcache, kv_elems * 4));
+  LE_CK(cudaMalloc(&E->vcache, kv_elems * 4));
+  LE_CK(cudaMemsetAsync(E->kcache, 0, kv_elems * 4, E->stream));
+  LE_CK(cudaMemsetAsync(E->vcache, 0, kv_elems * 4, E->stream));
+  const size_t B = (size_t)E->max_batch;
+  E->lm_grid = std::min<int>((int)((E->vocab / 2 + kWarps - 1) / kWarps), E->num_sms * 8);
+  LE_CK(cudaMalloc(&E->x, B * E->dim * 4));
+  LE_CK(cudaMalloc(&E->qkv, B * (E->dim + 2 * E->kv_dim) * 4));
+  LE_CK(cudaMalloc(&E->attn, B * E->dim * 4));
+  LE_CK(cudaMalloc(&E->act, B * E->ffn * 4));
+  LE_CK(cudaMalloc(&E->logits, B * E->vocab * 4));
+  LE_CK(cudaMemsetAsync(E->logits, 0, B * E->vocab * 4, E->stream));
+  LE_CK(cudaMalloc(&E->emb, (size_t)E->dim * 4));
+  LE_CK(cudaMalloc(&E->red, 2048 * 4));
+  LE_CK(cudaMalloc(&E->d_misc, 16 * 4));
+  LE_CK(cudaMalloc(&E->part, B * E->lm_grid * sizeof(ArgmaxPart)));
+  LE_CK(cudaMalloc(&E->am_result, B * 4));
+  LE_CK(cudaMemsetAsync(E->am_result, 0, B * 4, E->stream));
+  LE_CK(cudaMalloc(&E->token_log, (size_t)LE_MAX_SEQ_LEN * 4));
+  LE_CK(cudaMalloc(&E->d_params, B * sizeof(StepParams)));
+  LE_CK(cudaMemsetAsync(E->d_params, 0, B * sizeof(StepParams), E->stream));
+  LE_CK(cudaMallocHost(&E->h_ring, kRing * sizeof(StepParams)));
+  for (int i = 0; i < kRing; ++i) LE_CK(cudaEventCreateWithFlags(&E->ring_ev[i], cudaEventDisableTiming));
+  LE_CK(cudaMallocHost(&E->h_logits, B * E->vocab * 4));
+  LE_CK(cudaMallocHost(&E->h_small, (size_t)LE_MAX_SEQ_LEN * 4));
+  if (!set_smem_attrs(E)) return false;
+
+  // ---- graphs ----
+  if (!capture(E, row_buffers(E, 0, 0, false, 0), &E->g_fwd[0])) return false;
+  if (!capture(E, row_buffers(E, 0, 0, true, 0), &E->g_fwd[1])) return false;
+  if (!capture(E, row_buffers(E, 0, 0, true, 1), &E->g_gen)) return false;
+  LE_CK(cudaStreamSynchronize(E->stream));
+  return true;
+}
+
+static void destroy(Engine* E) {
+  if (!E) return;
+  DeviceGuard dg(E->device);
+  if (E->stream) cudaStreamSynchronize(E->stream);
+  for (auto& g : E->g_fwd) if (g) cudaGraphExecDestroy(g);
+  if (E->g_gen) cudaGraphExecDestroy(E->g_gen);
+  for (auto& ev : E->ring_ev) if (ev) cudaEventDestroy(ev);
+  void* dev_ptrs[] = {E->arena, E->rope_cos, E->rope_sin, E->kcache, E->vcache, E->x, E->qkv, E->attn,
+                      E->act, E->logits, E->emb, E->red, E->d_misc, E->part, E->am_result, E->token_log, E->d_params};
+  for (void* p : dev_ptrs) if (p) cudaFree(p);
+  if (E->h_ring) cudaFreeHost(E->h_ring);
+  if (E->h_logits) cudaFreeHost(E->h_logits);
+  if (E->h_small) cudaFreeHost(E->h_small);
+  if (E->stream) cudaStreamDestroy(E->stream);
+  delete E;
+}
+
+static Engine* create(const char* path, int device, int max_batch, int max_seq) {
+  if (!path) { set_create_error("model path is NULL"); return nullptr; }
+  if (max_batch < 1 || max_batch > 4096) { set_create_error("max_batch out of range"); return nullptr; }
+  if (max_seq == 0) max_seq = LE_MAX_SEQ_LEN;
+  if (max_seq < 1 || max_seq > LE_MAX_SEQ_LEN) { set_create_error("max_seq_len out of range"); return nullptr; }
+  int fd = ::open(path, O_RDONLY);
+  if (fd < 0) { set_create_error(std::string("cannot open ") + path); return nullptr; }
+  struct stat sb;
+  if (fstat(fd, &sb) != 0) { ::close(fd); set_create_error("fstat failed"); return nullptr; }
+  const size_t size = (size_t)sb.st_size;
+  void* map = size ? mmap(nullptr, size, PROT_READ, MAP_SHARED, fd, 0) : MAP_FAILED;
+  ::close(fd);
+  if (map == MAP_FAILED) { set_create_error("mmap failed"); return nullptr; }
+  ParsedFile P;
+  std::string perr;
+  const bool ok = parse_file(static_cast<const uint8_t*>(map), size, P, perr);
+  if (!ok) { munmap(map, size); set_create_error(perr); return nullptr; }
+  Engine* E = new Engine();
+  E->device = device;
+  E->max_batch = max_batch;
+  E->max_seq = max_seq;
+  bool good;
+  {
+    DeviceGuard dg(device);
+    good = init_device(E, static_cast<const uint8_t*>(map), P);
+  }
+  munmap(map, size);
+  if (!good) {
+    set_create_error(E->err);
+    destroy(E);
+    return nullptr;
+  }
+  return E;
+}
+
+static bool queue_params(Engine* E, int32_t token, int32_t pos) {
+  const int slot = E->ring_pos;
+  E->ring_pos = (E->ring_pos + 1) % kRing;
+  if (E->ring_used[slot]) LE_CK(cudaEventSynchronize(E->ring_ev[slot]));
+  E->h_ring[slot] = StepParams{token, pos, 0, 0};
+  LE_CK(cudaMemcpyAsync(E->d_params, &E->h_ring[slot], sizeof(StepParams), cudaMemcpyHostToDevice, E->stream));
+  LE_CK(cudaEventRecord(E->ring_ev[slot], E->stream));
+  E->ring_used[slot] = true;
+  return true;
+}
+
+static bool forward_token(Engine* E, int32_t token, size_t pos, bool logits) {
+  if (pos >= (size_t)E->max_seq) return true;  // silent no-op, src/llama_engine.cpp:936
+  if (token < 0 || token >= (int32_t)E->vocab) token = 0;  // :937
+  if (!queue_params(E, token, (int32_t)pos)) return false;
+  LE_CK(cudaGraphLaunch(E->g_fwd[logits ? 1 : 0], E->stream));
+  if (logits) {
+    E->logits_on_host_fresh = false;
+    E->argmax_valid = true;
+    E->have_logits = true;
+  }
+  return true;
+}
+
+static bool greedy(Engine* E, int32_t* out) {
+  if (!E->argmax_valid) {
+    const int parts = std::min<int>(E->num_sms * 2, (E->vocab + kThreads - 1) / kThreads);
+    k_argmax_rows<<<parts, kThreads, 0, E->stream>>>(E->logits, E->vocab, E->part);
+    k_argmax_finish<<<1, 1024, 0, E->stream>>>(E->part, parts, E->am_result, E->d_params, E->token_log, 0);
+    LE_CK(cudaGetLastError());
+    E->argmax_valid = true;
+  }
+  LE_CK(cudaMemcpyAsync(E->h_small, E->am_result, 4, cudaMemcpyDeviceToHost, E->stream));
+  LE_CK(cudaStreamSynchronize(E->stream));
+  *out = E->h_small[0];
+  return true;
+}
+
+static bool sync_logits(Engine* E) {
+  if (!E->logits_on_host_fresh) {
+    LE_CK(cudaMemcpyAsync(E->h_logits, E->logits, (size_t)E->vocab * 4, cudaMemcpyDeviceToHost, E->stream));
+    LE_CK(cudaStreamSynchronize(E->stream));
+    E->logits_on_host_fresh = true;
+  }
+  return true;
+}
+
+// Temperature / top-p sampling.  The probabilities are formed on the device; the candidate walk of
+// sample_top_p (src/llama_engine.cpp:808-838) runs over the host mirror, with libc rand().
+static int32_t sample_top_p_host(float* p, size_t vocab, float top_p) {
+  const size_t k = std::min<size_t>(64, vocab);
+  int32_t ids[64];
+  float vals[64];
+  for (size_t i = 0; i < k; ++i) { ids[i] = (int32_t)i; vals[i] = p[i]; }
+  for (size_t i = k; i < vocab; ++i) {
+    const float v = p[i];
+    if (v > vals[k - 1]) {
+      size_t q = k - 1;
+      while (q > 0 && v > vals[q - 1]) { vals[q] = vals[q - 1]; ids[q] = ids[q - 1]; --q; }
+      vals[q] = v; ids[q] = (int32_t)i;
+    }
+  }
+  float cum = 0.0f;
+  size_t last = 0;
+  for (size_t i = 0; i < k; ++i) { cum += vals[i]; last = i; if (cum >= top_p) break; }
+  const float r = (static_cast<float>(rand()) / static_cast<float>(RAND_MAX)) * cum;
+  float run = 0.0f;
+  for (size_t i = 0; i <= last; ++i) { run += vals[i]; if (run >= r) return ids[i]; }
+  return ids[0];
+}
+
+}  // namespace le
+
+#include "sampler_kernels.cuh"
+
+using namespace le;
+
+// =============================================================================================
+// C ABI, Part 1 (reference entry points)
+// =============================================================================================
+
+static Engine* H(llama_engine_t e) { return static_cast<Engine*>(e); }
+
+static int default_device() {
+  const char* d = getenv("LLAMA_ENGINE_DEVICE");
+  return d ? atoi(d) : 0;
+}
+
+LE_API llama_engine_t llama_engine_create(const char* model_path) {
+  return create(model_path, default_device(), 1, LE_MAX_SEQ_LEN);
+}
+
+LE_API void llama_engine_free(llama_engine_t engine) { destroy(H(engine)); }
+
+LE_API void llama_engine_reset(llama_engine_t engine) { (void)engine; }
+
+LE_API int32_t llama_engine_get_num_layers(llama_engine_t e) { return e ? (int32_t)H(e)->layers : 0; }
+LE_API int32_t llama_engine_get_dim(llama_engine_t e) { return e ? (int32_t)H(e)->dim : 0; }
+LE_API int32_t llama_engine_get_ffn_dim(llama_engine_t e) { return e ? (int32_t)H(e)->ffn : 0; }
+LE_API int32_t llama_engine_get_vocab_size(llama_engine_t e) { return e ? (int32_t)H(e)->vocab : 0; }
+LE_API int32_t llama_engine_get_num_heads(llama_engine_t e) { return e ? (int32_t)H(e)->heads : 0; }
+LE_API int32_t llama_engine_get_num_kv_heads(llama_engine_t e) { return e ? (int32_t)H(e)->kv_heads : 0; }
+LE_API int32_t llama_engine_get_head_dim(llama_engine_t e) { return e ? (int32_t)LE_HEAD_DIM : 0; }
+LE_API int32_t llama_engine_get_max_seq_len(llama_engine_t e) { (void)e; return LE_MAX_SEQ_LEN; }
+
+LE_API int llama_engine_forward_token(llama_engine_t engine, int32_t token_id, size_t pos, int compute_logits) {
+  if (!engine) return -1;
+  Engine* E = H(engine);
+  DeviceGuard dg(E->device);
+  return forward_token(E, token_id, pos, compute_logits != 0) ? 0 : -1;
+}
+
+LE_API int llama_engine_prefill(llama_engine_t engine, const int32_t* token_ids, size_t count, size_t start_pos,
+                                int compute_last_logits) {
+  if (!engine || !token_ids) return -1;
+  Engine* E = H(engine);
+  DeviceGuard dg(E->device);
+  for (size_t i = 0; i < count; ++i) {
+    const bool last = (i + 1 == count) && compute_last_logits != 0;
+    if (!forward_token(E, token_ids[i], start_pos + i, last)) return -1;
+  }
+  return 0;
+}
+
+LE_API int32_t llama_engine_sample(llama_engine_t engine, float temperature, float top_p) {
+  if (!engine) return 0;
+  Engine* E = H(engine);
+  DeviceGuard dg(E->device);
+  int32_t id = 0;
+  if (temperature <= 0.01f) {
+    if (!greedy(E, &id)) return 0;
+    return id;
+  }
+  if (!softmax_in_place(E, temperature)) return 0;
+  if (!sync_logits(E)) return 0;
+  return sample_top_p_host(E->h_logits, E->vocab, top_p);
+}
+
+LE_API const float* llama_engine_get_logits(llama_engine_t engine) {
+  if (!engine) return nullptr;
+  Engine* E = H(engine);
+  DeviceGuard dg(E->device);
+  if (!sync_logits(E)) return nullptr;
+  return E->h_logits;
+}
+
+LE_API void llama_engine_dequantize_embedding(llama_engine_t engine, size_t token_id, float* out_x) {
+  if (!engine || !out_x) return;
+  Engine* E = H(engine);
+  if (token_id >= E->vocab) return;
+  DeviceGuard dg(E->device);
+  int32_t* tok = E->d_misc;
+  if (cudaStreamSynchronize(E->stream) != cudaSuccess) return;  // h_small may be in use by a copy
+  E->h_small[0] = (int32_t)token_id;
+  if (cudaMemcpyAsync(tok, E->h_small, 4, cudaMemcpyHostToDevice, E->stream) != cudaSuccess) return;
+  k_embed<<<1, kThreads, 0, E->stream>>>(E->lm_head, E->d_params, tok, E->emb);
+  if (cudaMemcpyAsync(out_x, E->emb, (size_t)E->dim * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess) return;
+  cudaStreamSynchronize(E->stream);
+}
+
+// =============================================================================================
+// C ABI, Part 2 (extensions)
+// =============================================================================================
+
+LE_API llama_engine_t llama_engine_create_ex(const char* model_path, int device, int max_batch, int max_seq_len) {
+  return create(model_path, device, max_batch, max_seq_len);
+}
+
+LE_API const char* llama_engine_last_error(llama_engine_t engine) {
+  if (engine) return H(engine)->err.c_str();
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  static thread_local std::string copy;
+  copy = g_create_error;
+  return copy.c_str();
+}
+
+LE_API int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_token, size_t start_pos,
+                                        int32_t n_steps, int32_t* out_tokens) {
+  if (!engine || !out_tokens || n_steps < 0) return -1;
+  Engine* E = H(engine);
+  if (n_steps == 0) return 0;
+  if (start_pos + (size_t)n_steps > (size_t)E->max_seq) { E->err = "generate_greedy: positions exceed max_seq_len"; return -1; }
+  DeviceGuard dg(E->device);
+  if (first_token < 0 || first_token >= (int32_t)E->vocab) first_token = 0;
+  if (!queue_params(E, first_token, (int32_t)start_pos)) return -1;
+  for (int32_t i = 0; i < n_steps; ++i)
+    if (cudaGraphLaunch(E->g_gen, E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
+  if (cudaMemcpyAsync(out_tokens, E->token_log, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess)
+    return -1;
+  cudaError_t ce = cudaStreamSynchronize(E->stream);
+  if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
+  E->logits_on_host_fresh = false;
+  E->argmax_valid = true;
+  E->have_logits = true;
+  return 0;
+}
+
+LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* tokens, const int32_t* positions,
+                                      const int32_t* slots, int n, int compute_logits) {
+  if (!engine || !tokens || !positions || !slots || n < 1) return -1;
+  Engine* E = H(engine);
+  if (n > E->max_batch) { E->err = "forward_batch: n exceeds max_batch"; return -1; }
+  for (int i = 0; i < n; ++i) {
+    if (slots[i] < 0 || slots[i] >= E->max_batch) { E->err = "forward_batch: slot out of range"; return -1; }
+    if (positions[i] < 0 || positions[i] >= E->max_seq) { E->err = "forward_batch: position out of range"; return -1; }
+  }
+  DeviceGuard dg(E->device);
+  std::vector<StepParams> hp(n);
+  for (int i = 0; i < n; ++i) {
+    int32_t t = tokens[i];
+    if (t < 0 || t >= (int32_t)E->vocab) t = 0;
+    hp[i] = StepParams{t, positions[i], 0, 0};
+  }
+  if (cudaMemcpyAsync(E->d_params, hp.data(), n * sizeof(StepParams), cudaMemcpyHostToDevice, E->stream) != cudaSuccess)
+    return -1;
+  for (int i = 0; i < n; ++i) enqueue_token(E, row_buffers(E, i, slots[i], compute_logits != 0, 0), E->stream);
+  cudaError_t ce = cudaStreamSynchronize(E->stream);  // hp goes out of scope
+  if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
+  E->logits_on_host_fresh = false;
+  if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
+  return 0;
+}
+
+LE_API void* llama_engine_get_stream(llama_engine_t engine) { return engine ? (void*)H(engine)->stream : nullptr; }
+
+LE_API int llama_engine_profile_phase(llama_engine_t engine, const char* phase, int iters, float* avg_ms) {
+  if (!engine || !phase || iters < 1 || !avg_ms) return -1;
+  Engine* E = H(engine);
+  static const char* names[] = {"qkv", "attn", "oproj", "gateup", "down", "lmhead"};
+  int ph = -1;
+  for (int i = 0; i < 6; ++i)
+    if (std::strcmp(phase, names[i]) == 0) ph = i;
+  const bool step = std::strcmp(phase, "step") == 0;
+  if (ph < 0 && !step) { E->err = "profile_phase: unknown phase"; return -1; }
+  DeviceGuard dg(E->device);
+  cudaEvent_t a, b;
+  if (cudaEventCreate(&a) != cudaSuccess) return -1;
+  if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return -1; }
+  TokenBuffers B = row_buffers(E, 0, 0, true, 0);
+  cudaEventRecord(a, E->stream);
+  for (int i = 0; i < iters; ++i) {
+    if (step) cudaGraphLaunch(E->g_fwd[1], E->stream);
+    else enqueue_phase(E, B, ph, (uint32_t)(i % E->layers), E->stream);
+  }
+  cudaEventRecord(b, E->stream);
+  cudaError_t ce = cudaEventSynchronize(b);
+  float ms = 0.0f;
+  if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
+  *avg_ms = ms / (float)iters;
+  E->logits_on_host_fresh = false;
+  E->argmax_valid = false;
+  return 0;
+}
+
+LE_API int llama_engine_argmax_batch(llama_engine_t engine, int32_t* out_tokens, int n) {
+  if (!engine || !out_tokens || n < 1) return -1;
+  Engine* E = H(engine);
+  if (n > E->max_batch) return -1;
+  DeviceGuard dg(E->device);
+  if (cudaMemcpyAsync(out_tokens, E->am_result, (size_t)n * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess) return -1;
+  return cudaStreamSynchronize(E->stream) == cudaSuccess ? 0 : -1;
+}
+
+LE_API const float* llama_engine_get_logits_batch(llama_engine_t engine, int row) {
+  if (!engine) return nullptr;
+  Engine* E = H(engine);
+  if (row < 0 || row >= E->max_batch) return nullptr;
+  DeviceGuard dg(E->device);
+  float* h = E->h_logits + (size_t)row * E->vocab;
+  if (cudaMemcpyAsync(h, E->logits + (size_t)row * E->vocab, (size_t)E->vocab * 4, cudaMemcpyDeviceToHost,
+                      E->stream) != cudaSuccess)
+    return nullptr;
+  if (cudaStreamSynchronize(E->stream) != cudaSuccess) return nullptr;
+  if (row == 0) E->logits_on_host_fresh = true;
+  return h;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Isolated GEMV
+// ---------------------------------------------------------------------------------------------
+template <int MX, int R, int CPL>
+static int launch_gemv(const QMat& W, const float* x, float* y, cudaStream_t s, int num_sms) {
+  const size_t smem = (size_t)MX * (W.K + W.K / 128) * 4;
+  if (smem > 200 * 1024) return -1;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k_gemv<MX, R, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return -1;
+  const int groups = W.N / R;
+  const int grid = std::min<int>((groups + kWarps - 1) / kWarps, num_sms * 8);
+  k_gemv<MX, R, CPL><<<grid, kThreads, smem, s>>>(x, W, y);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <int R, int CPL>
+static int launch_gemv_m(int mx, const QMat& W, const float* x, float* y, cudaStream_t s, int num_sms) {
+  switch (mx) {
+    case 1: return launch_gemv<1, R, CPL>(W, x, y, s, num_sms);
+    case 2: return launch_gemv<2, R, CPL>(W, x, y, s, num_sms);
+    case 3: return launch_gemv<3, R, CPL>(W, x, y, s, num_sms);
+    default: return launch_gemv<4, R, CPL>(W, x, y, s, num_sms);
+  }
+}
+
+LE_API int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16, int N, int K,
+                           const float* x, int M, float* y, void* stream) {
+  if (!nibbles || !step_bf16 || !min_bf16 || !x || !y) return -1;
+  if (N < 1 || K < 128 || K % 128 != 0 || M < 1 || M > 8) return -1;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  QMat W{nibbles, step_bf16, min_bf16, N, K};
+  for (int m0 = 0; m0 < M; m0 += 4) {
+    const int mx = std::min(4, M - m0);
+    const float* xm = x + (size_t)m0 * K;
+    float* ym = y + (size_t)m0 * N;
+    int rc;
+    if (N % 2 == 0) rc = K >= 8192 ? launch_gemv_m<2, 8>(mx, W, xm, ym, s, sms) : launch_gemv_m<2, 2>(mx, W, xm, ym, s, sms);
+    else rc = K >= 8192 ? launch_gemv_m<1, 8>(mx, W, xm, ym, s, sms) : launch_gemv_m<1, 2>(mx, W, xm, ym, s, sms);
+    if (rc != 0) return -1;
+  }
+  return 0;
+}
