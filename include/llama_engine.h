@@ -131,8 +131,8 @@ const float* llama_engine_get_logits_batch(llama_engine_t engine, int row);
  * (nibbles[N*K/2], step_bf16[N*K/128], min_bf16[N*K/128]).  K % 128 == 0.  `stream` is a
  * cudaStream_t (NULL = legacy default stream).  Counterpart of the reference's file-local
  * signed_4bit_b128_gemv (src/llama_engine.cpp:233-357), which receives the block sums of x
- * precomputed; here they are computed inside the kernel.  Returns 0, or -1 on bad arguments /
- * launch error. */
+ * precomputed; here they are computed inside the kernel.  `nibbles` and `x` must be 16-byte
+ * aligned.  Returns 0, or -1 on bad arguments / launch error. */
 int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
                     int N, int K, const float* x, int M, float* y, void* stream);
 

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "decode_kernels.cuh"
+#include "mma_gemv.cuh"
 #include "llama_engine.h"
 
 #define LE_API extern "C" __attribute__((visibility("default")))
@@ -164,6 +165,7 @@ struct Engine {
   cudaEvent_t ring_ev[kRing] = {};
   bool ring_used[kRing] = {};
   int ring_pos = 0;
+  int32_t last_pos = 0;  // last position queued for slot 0 (diagnostics re-use it)
   float* h_logits = nullptr;  // pinned [max_batch][vocab]
   int32_t* h_small = nullptr; // pinned scratch [LE_MAX_SEQ_LEN]
   bool logits_on_host_fresh = false;   // slot-0 host mirror matches device
@@ -458,6 +460,7 @@ static bool queue_params(Engine* E, int32_t token, int32_t pos) {
   E->ring_pos = (E->ring_pos + 1) % kRing;
   if (E->ring_used[slot]) LE_CK(cudaEventSynchronize(E->ring_ev[slot]));
   E->h_ring[slot] = StepParams{token, pos, 0, 0};
+  E->last_pos = pos;
   LE_CK(cudaMemcpyAsync(E->d_params, &E->h_ring[slot], sizeof(StepParams), cudaMemcpyHostToDevice, E->stream));
   LE_CK(cudaEventRecord(E->ring_ev[slot], E->stream));
   E->ring_used[slot] = true;
@@ -638,6 +641,7 @@ LE_API int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_tok
   DeviceGuard dg(E->device);
   if (first_token < 0 || first_token >= (int32_t)E->vocab) first_token = 0;
   if (!queue_params(E, first_token, (int32_t)start_pos)) return -1;
+  E->last_pos = (int32_t)(start_pos + n_steps - 1);
   for (int32_t i = 0; i < n_steps; ++i)
     if (cudaGraphLaunch(E->g_gen, E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
   if (cudaMemcpyAsync(out_tokens, E->token_log, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess)
@@ -692,6 +696,12 @@ LE_API int llama_engine_profile_phase(llama_engine_t engine, const char* phase, 
   if (cudaEventCreate(&a) != cudaSuccess) return -1;
   if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return -1; }
   TokenBuffers B = row_buffers(E, 0, 0, true, 0);
+  // device params may have been advanced past the cache by a generation: re-queue a valid one
+  if (!queue_params(E, 0, std::min<int32_t>(E->last_pos, E->max_seq - 1))) {
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return -1;
+  }
   cudaEventRecord(a, E->stream);
   for (int i = 0; i < iters; ++i) {
     if (step) cudaGraphLaunch(E->g_fwd[1], E->stream);
@@ -759,10 +769,36 @@ static int launch_gemv_m(int mx, const QMat& W, const float* x, float* y, cudaSt
   }
 }
 
+template <int NT>
+static int launch_gemv_mma(int mx, const QMat& W, const float* x, float* y, cudaStream_t s, int num_sms) {
+  const size_t smem = (size_t)digit_image_bytes(mx, W.K);
+  if (smem > 200 * 1024) return -1;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k_gemv_mma<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return -1;
+  const int ntiles = (W.N + 15) / 16;
+  const int grid = std::min<int>((ntiles + 7) / 8, num_sms * 4);
+  k_gemv_mma<NT><<<grid, 256, smem, s>>>(x, mx, W, y);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Kernel selection for the isolated GEMV: LLAMA_B128_GEMV=simt forces the CUDA-core kernel,
+// otherwise the integer tensor-core kernel is used (N >= 16).
+static bool gemv_use_mma(int N) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* v = getenv("LLAMA_B128_GEMV");
+    forced = (v && std::strcmp(v, "simt") == 0) ? 0 : 1;
+  }
+  return forced == 1 && N >= 16;
+}
+
 LE_API int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16, int N, int K,
                            const float* x, int M, float* y, void* stream) {
   if (!nibbles || !step_bf16 || !min_bf16 || !x || !y) return -1;
   if (N < 1 || K < 128 || K % 128 != 0 || M < 1 || M > 8) return -1;
+  // 16-byte vector loads of the nibble rows and of x
+  if ((reinterpret_cast<uintptr_t>(nibbles) | reinterpret_cast<uintptr_t>(x)) & 15u) return -1;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -773,8 +809,13 @@ LE_API int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, co
     const float* xm = x + (size_t)m0 * K;
     float* ym = y + (size_t)m0 * N;
     int rc;
-    if (N % 2 == 0) rc = K >= 8192 ? launch_gemv_m<2, 8>(mx, W, xm, ym, s, sms) : launch_gemv_m<2, 2>(mx, W, xm, ym, s, sms);
-    else rc = K >= 8192 ? launch_gemv_m<1, 8>(mx, W, xm, ym, s, sms) : launch_gemv_m<1, 2>(mx, W, xm, ym, s, sms);
+    if (gemv_use_mma(N)) {
+      rc = mx <= 2 ? launch_gemv_mma<1>(mx, W, xm, ym, s, sms) : launch_gemv_mma<2>(mx, W, xm, ym, s, sms);
+    } else if (N % 2 == 0) {
+      rc = K >= 8192 ? launch_gemv_m<2, 8>(mx, W, xm, ym, s, sms) : launch_gemv_m<2, 2>(mx, W, xm, ym, s, sms);
+    } else {
+      rc = K >= 8192 ? launch_gemv_m<1, 8>(mx, W, xm, ym, s, sms) : launch_gemv_m<1, 2>(mx, W, xm, ym, s, sms);
+    }
     if (rc != 0) return -1;
   }
   return 0;

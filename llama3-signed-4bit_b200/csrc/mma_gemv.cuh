@@ -1,0 +1,228 @@
+// Block-128 4-bit GEMV on the integer tensor-core path (mma.sync m16n8k32, u8 x s8 -> s32).
+//
+// The factored form of the reference GEMV (src/llama_engine.cpp:231-232, 315-319),
+//     y_n = sum_b ( min_nb * xs_b + step_nb * sum_{k in b} q_nk * x_k ),
+// needs the exact 4-bit codes q (0..15) times the activations.  Here the codes go into the
+// tensor core unchanged as u8, and each 128-block of the fp32 activation vector is written as a
+// 30-bit fixed-point integer split into four balanced base-256 digits:
+//     x_k ~= 2^-e_b * X_k,   X_k = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3,   d_i in [-128, 127],
+// with e_b chosen so that max_k |x_k| * 2^e_b < 2^29.  The four digit planes are four columns
+// of the MMA's B operand (N = 8 holds two activation vectors), so one MMA returns the exact
+// integer sums  C_i = sum_k q_k d_ik  for a 16-row tile.  Per block the tile's rows then add
+//     step * 2^-e_b * (((C3 * 256 + C2) * 256 + C1) * 256 + C0)  +  min * xs_b
+// in fp32.  The only rounding inside a block is the 2^-30-relative fixed-point step of x and
+// the final fp32 combination, so the result matches an fp32 loop to ~1e-7 relative.
+//
+// Operand layout.  A warp owns a tile of 16 rows.  For block b, lane (g, t) (g = lane/4,
+// t = lane%4) loads bytes [16t, 16t+16) of rows g and g+8 of the block (two coalesced 512-byte
+// warp loads).  Its u32 word i (i = 0..3) holds codes 32t+8i .. 32t+8i+7 of the block:
+//   a0 = word & 0x0F0F0F0F (row g, codes 32t+8i+{0,2,4,6}), a2 = (word >> 4) & 0x0F0F0F0F
+//   (codes +{1,3,5,7}); a1 / a3 likewise from row g+8.  MMA i of the block covers the 32 codes
+// {32t+8i+m}; the B fragments are written in the same permuted K order by stage_digits().
+#pragma once
+
+#include "common.cuh"
+
+namespace le {
+
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory image of MX activation vectors for the MMA path.
+//   bfrag : [nb][4 (MMA i)][NT (n-tile)][32 lanes] uint2, NT = (MX+1)/2
+//   bsum  : [MX][nb]  fp32 block sums (compute_x_block_sums, src/llama_engine.cpp:496-521)
+//   escl  : [MX][nb]  2^-e_b
+struct DigitImage {
+  uint2* bfrag;
+  float* bsum;
+  float* escl;
+};
+
+__host__ __device__ constexpr int digit_image_bytes(int MX, int K) {
+  return (K / 128) * 4 * ((MX + 1) / 2) * 32 * 8 + 2 * MX * (K / 128) * 4;
+}
+
+// Builds the digit image from MX fp32 vectors xs[m*K + k] already in shared memory.
+// Must be called by the whole CTA; ends with __syncthreads().
+__device__ __forceinline__ void stage_digits(const float* xs, int MX, int K, DigitImage img) {
+  const int nb = K / 128, NT = (MX + 1) / 2;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // 1) per-block sum and exponent: one warp per (m, b)
+  for (int mb = wid; mb < MX * nb; mb += nw) {
+    const float4 v = *reinterpret_cast<const float4*>(xs + (size_t)mb * 128 + lane * 4);
+    float s = (v.x + v.y) + (v.z + v.w);
+    float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    s = warp_sum(s);
+    a = warp_max(a);
+    if (lane == 0) {
+      int ex = 0;
+      if (a > 0.0f) frexpf(a, &ex);  // a < 2^ex
+      int e = 29 - ex;
+      if (e > 126) e = 126;
+      img.bsum[mb] = s;
+      img.escl[mb] = (a > 0.0f) ? ldexpf(1.0f, -e) : 0.0f;
+    }
+  }
+  // Zero the unused half of the last n-tile when MX is odd (lanes 16..31 of n-tile NT-1).
+  if (MX & 1) {
+    for (int u = threadIdx.x; u < nb * 4 * 16; u += blockDim.x) {
+      const int bi = u >> 4, l = 16 + (u & 15);
+      img.bfrag[((size_t)bi * NT + (NT - 1)) * 32 + l] = make_uint2(0u, 0u);
+    }
+  }
+  __syncthreads();
+  // 2) digits: one unit = (m, b, i, t, h) covering codes n = 32t + 8i + 2j + h, j = 0..3
+  const int units = MX * nb * 32;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int h = u & 1, t = (u >> 1) & 3, i = (u >> 3) & 3, b = (u >> 5) % nb, m = (u >> 5) / nb;
+    const float es = img.escl[m * nb + b];
+    const int e = es > 0.0f ? -ilogbf(es) : 0;
+    uint32_t plane[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float xv = xs[(size_t)m * K + b * 128 + 32 * t + 8 * i + 2 * j + h];
+      int X = es > 0.0f ? __float2int_rn(ldexpf(xv, e)) : 0;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int d = ((X + 128) & 255) - 128;
+        X = (X - d) >> 8;
+        plane[p] |= (uint32_t)(d & 255) << (8 * j);
+      }
+    }
+    const int jt = m >> 1;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int L = ((m & 1) * 4 + p) * 4 + t;
+      uint32_t* dst = reinterpret_cast<uint32_t*>(&img.bfrag[(((size_t)b * 4 + i) * NT + jt) * 32 + L]);
+      dst[h] = plane[p];
+    }
+  }
+  __syncthreads();
+}
+
+// One output row-pair result per thread: lanes with t in {0, 2} own (rows g, g+8) of sequence
+// 2*j + t/2 for each n-tile j.
+template <int NT>
+struct TileAcc {
+  float y[NT][2];
+};
+
+// Accumulates the tile (16 rows starting at row0 of W) over all K blocks.
+// `scale_rows` loads step/min for rows (row0+g, row0+g+8) at block b.
+template <int NT>
+__device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitImage& img, int MX, TileAcc<NT>& acc) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int nb = W.K >> 7;
+  const uint8_t* ra = W.nib + (size_t)(row0 + g) * (W.K >> 1) + 16 * t;
+  const uint8_t* rb = ra + (size_t)8 * (W.K >> 1);
+  const uint16_t* sa = W.step + (size_t)(row0 + g) * nb;
+  const uint16_t* ma = W.mn + (size_t)(row0 + g) * nb;
+  const uint16_t* sb = sa + (size_t)8 * nb;
+  const uint16_t* mb = ma + (size_t)8 * nb;
+  const bool owner = (t & 1) == 0;
+  const int seq_off = t >> 1;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc.y[j][0] = acc.y[j][1] = 0.0f;
+
+  uint4 wa = ld_stream_u4(ra), wb = ld_stream_u4(rb);
+  for (int b = 0; b < nb; ++b) {
+    uint4 na = wa, nbw = wb;
+    if (b + 1 < nb) {
+      na = ld_stream_u4(ra + (size_t)(b + 1) * 64);
+      nbw = ld_stream_u4(rb + (size_t)(b + 1) * 64);
+    }
+    int c[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0;
+    const uint2* bf = img.bfrag + (size_t)b * 4 * NT * 32 + lane;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t xa = i == 0 ? wa.x : i == 1 ? wa.y : i == 2 ? wa.z : wa.w;
+      const uint32_t xb = i == 0 ? wb.x : i == 1 ? wb.y : i == 2 ? wb.z : wb.w;
+      const uint32_t a0 = xa & 0x0F0F0F0Fu, a2 = (xa >> 4) & 0x0F0F0F0Fu;
+      const uint32_t a1 = xb & 0x0F0F0F0Fu, a3 = (xb >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const uint2 bb = bf[(i * NT + j) * 32];
+        mma_u8s8(c[j], a0, a1, a2, a3, bb.x, bb.y);
+      }
+    }
+    // epilogue of block b: lanes t and t^1 hold digit planes {0,1} and {2,3}
+    float st0 = 0.f, mn0 = 0.f, st1 = 0.f, mn1 = 0.f;
+    if (owner) {
+      st0 = bf16_bits_to_f32(__ldg(sa + b));
+      mn0 = bf16_bits_to_f32(__ldg(ma + b));
+      st1 = bf16_bits_to_f32(__ldg(sb + b));
+      mn1 = bf16_bits_to_f32(__ldg(mb + b));
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int p2 = __shfl_xor_sync(0xffffffffu, c[j][0], 1);
+      const int p3 = __shfl_xor_sync(0xffffffffu, c[j][1], 1);
+      const int q2 = __shfl_xor_sync(0xffffffffu, c[j][2], 1);
+      const int q3 = __shfl_xor_sync(0xffffffffu, c[j][3], 1);
+      const int m = 2 * j + seq_off;
+      if (owner && m < MX) {
+        const float es = img.escl[m * nb + b], xsb = img.bsum[m * nb + b];
+        float v0 = (float)p3;
+        v0 = fmaf(v0, 256.0f, (float)p2);
+        v0 = fmaf(v0, 256.0f, (float)c[j][1]);
+        v0 = fmaf(v0, 256.0f, (float)c[j][0]);
+        float v1 = (float)q3;
+        v1 = fmaf(v1, 256.0f, (float)q2);
+        v1 = fmaf(v1, 256.0f, (float)c[j][3]);
+        v1 = fmaf(v1, 256.0f, (float)c[j][2]);
+        acc.y[j][0] += fmaf(st0 * es, v0, mn0 * xsb);
+        acc.y[j][1] += fmaf(st1 * es, v1, mn1 * xsb);
+      }
+    }
+    wa = na;
+    wb = nbw;
+  }
+}
+
+}  // namespace le
+
+namespace le {
+
+// Isolated GEMV on the MMA path: y[m][n] = W[n,:] . x[m,:] for MX = 1..4 vectors.  Each warp
+// processes 16-row tiles (grid-stride); rows past N are clamped on load and never stored.
+template <int NT>
+__global__ void __launch_bounds__(256) k_gemv_mma(const float* __restrict__ x, int MX, QMat W, float* __restrict__ y) {
+  extern __shared__ float4 smem4[];
+  const int nb = W.K / 128;
+  DigitImage img;
+  img.bfrag = reinterpret_cast<uint2*>(smem4);
+  img.bsum = reinterpret_cast<float*>(img.bfrag + (size_t)nb * 4 * NT * 32);
+  img.escl = img.bsum + MX * nb;
+  stage_digits(x, MX, W.K, img);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int ntiles = (W.N + 15) / 16;
+  const int warps = blockDim.x >> 5;
+  for (int tile = blockIdx.x * warps + (threadIdx.x >> 5); tile < ntiles; tile += gridDim.x * warps) {
+    int row0 = tile * 16;
+    QMat Wt = W;
+    if (row0 + 16 > W.N) row0 = W.N - 16;  // N >= 16 is required by the launcher
+    TileAcc<NT> acc;
+    mma_tile<NT>(Wt, row0, img, MX, acc);
+    if ((t & 1) == 0) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int m = 2 * j + (t >> 1);
+        if (m < MX) {
+          const int r0 = row0 + g, r1 = row0 + g + 8;
+          if (r0 >= tile * 16) y[(size_t)m * W.N + r0] = acc.y[j][0];
+          if (r1 >= tile * 16) y[(size_t)m * W.N + r1] = acc.y[j][1];
+        }
+      }
+    }
+  }
+}
+
+}  // namespace le

@@ -221,12 +221,12 @@ def test_forward_batch_matches_single(pkg, bindings, small_model, oracle_lib):
         for t in range(max(lens)):
             rows = [i for i in range(n) if t < lens[i]]
             eng.forward_batch([int(prompts[i][t]) for i in rows], [t] * len(rows), rows, True)
+            am = eng.argmax_batch(len(rows))
             for j, i in enumerate(rows):
                 oracle_lib.orc_forward_token(orcs[i], int(prompts[i][t]), t, 1)
                 ref = _oracle_logits(oracle_lib, orcs[i], vocab)
                 assert rel_max_err(eng.get_logits_batch(j), ref) <= LOGIT_RTOL
-        am = eng.argmax_batch(1)
-        assert am[0] == int(np.argmax(_oracle_logits(oracle_lib, orcs[0], vocab)))
+                assert am[j] == int(np.argmax(ref))
     finally:
         for o in orcs:
             oracle_lib.orc_free(o)
