@@ -272,9 +272,11 @@ def run_ours(args, rank, world, local_rank):
         e2e_ms, wall = float(t[0].item()), float(t[1].item()) / 1e3
     e2e_value = world * args.steps / max(e2e_ms / 1e3, wall)
 
-    # per-phase live timing for the roofline of the dominant kernel
+    # roofline of the dominant kernel
     peak, peak_kind = hbm_peak()
     avg_pos = start + (GEN_LEN - 1) / 2.0
+    bytes_tok = sum(token_bytes(shape, p) for p in range(start, start + GEN_LEN)) / GEN_LEN
+    persistent = eng.decode_path == "persistent"
     pb = phase_bytes(shape, int(avg_pos))
     launches = {"qkv": shape.layers, "attn": shape.layers, "oproj": shape.layers, "gateup": shape.layers,
                 "down": shape.layers, "lmhead": 1}
@@ -286,23 +288,37 @@ def run_ours(args, rank, world, local_rank):
         rc = lib.llama_engine_profile_phase(eng.handle, ph.encode(), iters, ctypes.byref(out))
         phase_ms[ph] = float(out.value) if rc == 0 else float("nan")
     share = {ph: phase_ms[ph] * launches[ph] for ph in launches}
-    dom = max(share, key=share.get)
-    achieved = pb[dom] / (phase_ms[dom] / 1e3) / 1e9
-    traffic = read_traffic(dom)
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
-                "algorithmic_bytes_per_launch": pb[dom], "launch_ms": round(phase_ms[dom], 5),
-                "phase_ms": {k: round(v, 5) for k, v in phase_ms.items()},
-                "phase_share": {k: round(v / sum(share.values()), 4) for k, v in share.items()}}
-    bytes_tok = sum(token_bytes(shape, p) for p in range(start, start + GEN_LEN)) / GEN_LEN
+    if persistent:
+        # one launch = one 128-token greedy generation (positions 31..158) of the timed region
+        launch_ms = ms / (args.steps / GEN_LEN)
+        launch_bytes = bytes_tok * GEN_LEN
+        achieved = launch_bytes / (launch_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "k_decode_persistent", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": read_traffic("k_decode_persistent"),
+                    "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(launch_bytes),
+                    "launch_ms": round(launch_ms, 5), "tokens_per_launch": GEN_LEN,
+                    "kernel_chain_phase_ms": {k: round(v, 5) for k, v in phase_ms.items()}}
+    else:
+        dom = max(share, key=share.get)
+        achieved = pb[dom] / (phase_ms[dom] / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "traffic": read_traffic(dom), "peak_source": peak_kind,
+                    "algorithmic_bytes_per_launch": pb[dom], "launch_ms": round(phase_ms[dom], 5),
+                    "phase_ms": {k: round(v, 5) for k, v in phase_ms.items()},
+                    "phase_share": {k: round(v / sum(share.values()), 4) for k, v in share.items()}}
     step_gbs = bytes_tok * (value / world) / 1e9
     step_roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(step_gbs / peak, 4), "bytes_per_token": int(bytes_tok),
                      "ideal_tok_s_per_gpu": round(peak * 1e9 / bytes_tok, 1)}
 
+    trace = None
+    if persistent and rank == 0 and args.trace:
+        tr = load_package().trace
+        trace = tr.capture(eng, first, start)
     result = None
     if rank == 0:
         kernels_per_token = 1 + 5 * shape.layers + 2
+        launches_timed = (args.steps + GEN_LEN - 1) // GEN_LEN if persistent else kernels_per_token * args.steps
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             rate, kind = cpu_decode_rate(model, 1, args.cpu_tokens, 1)
@@ -322,7 +338,8 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4,
                     "api": "llama_engine_forward_token + llama_engine_sample per step (C ABI via ctypes)",
                     "wall_s": round(wall, 4)},
-            "gpu_launches": kernels_per_token * args.steps, "clocks": clocks,
+            "gpu_launches": launches_timed, "decode_path": eng.decode_path, "clocks": clocks,
+            **({"phase_trace": trace} if trace else {}),
         }
     eng.close()
     if world > 1:
@@ -377,6 +394,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=12)
     ap.add_argument("--ref-max-steps", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="add the persistent kernel's phase timeline")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

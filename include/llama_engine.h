@@ -136,6 +136,20 @@ const float* llama_engine_get_logits_batch(llama_engine_t engine, int row);
 int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
                     int N, int K, const float* x, int M, float* y, void* stream);
 
+/* Which implementation runs the slot-0 token steps: 1 = the persistent token-step kernel (one
+ * cooperative launch per forward_token, or per whole generate_greedy call; used for dim 2048
+ * and ffn_dim in {2048, 4096, 8192}), 0 = the per-phase kernel chain in a CUDA graph (any other
+ * supported geometry, or LLAMA_B200_PERSISTENT=0 at create time).  -1 for a NULL handle. */
+int llama_engine_decode_path(llama_engine_t engine);
+
+/* Diagnostics for the persistent kernel: enable = 1 starts recording a phase trace of the first
+ * token of each following launch (globaltimer timestamps per CTA at every phase's start, after
+ * its dependency wait, after staging and at its end), 0 stops, 2 copies up to max_entries
+ * (time_ns, tag) pairs laid out as [cta][1024] into `out` and returns the count.  Tags:
+ * (event << 16) | (phase << 8) | layer, event 1..4; 0xFFFF0000 marks a token start.
+ * Returns -1 when the engine does not use the persistent kernel. */
+int llama_engine_trace(llama_engine_t engine, int enable, unsigned long long* out, int max_entries);
+
 /* The cudaStream_t on which the engine enqueues all of its work (for CUDA-event timing and
  * stream ordering by the caller).  NULL for a NULL handle. */
 void* llama_engine_get_stream(llama_engine_t engine);

@@ -15,12 +15,14 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "decode_kernels.cuh"
 #include "mma_gemv.cuh"
+#include "persistent.cuh"
 #include "llama_engine.h"
 
 #define LE_API extern "C" __attribute__((visibility("default")))
@@ -172,6 +174,22 @@ struct Engine {
   bool argmax_valid = false;           // am_result[0] holds greedy of current device logits
   bool have_logits = false;
 
+  // persistent token-step kernel (LLaMA-3.2-1B geometry: dim 2048, ffn 8192)
+  bool persist = false;
+  uint8_t* rec_arena = nullptr;
+  size_t rec_bytes = 0;
+  PCtaSched* d_sched = nullptr;
+  PSeg* d_segs = nullptr;
+  PItem* d_items = nullptr;
+  unsigned long long* d_recs = nullptr;
+  const float** d_norms = nullptr;
+  uint32_t* d_ctr = nullptr;
+  PCtrl* d_ctrl = nullptr;
+  uint32_t* h_err = nullptr;  // pinned mirror of PCtrl::error / err_where
+  unsigned long long* d_trace = nullptr;  // optional phase trace of the persistent kernel
+  PArgs pargs{};
+  int p_grid = 0;
+
   cudaGraphExec_t g_fwd[2] = {nullptr, nullptr};  // [compute_logits]
   cudaGraphExec_t g_gen = nullptr;                // forward + greedy + advance
 
@@ -296,6 +314,200 @@ static bool capture(Engine* E, const TokenBuffers& B, cudaGraphExec_t* out) {
 
 static void destroy(Engine* E);
 
+// ---------------------------------------------------------------------------------------------
+// Persistent kernel set-up: record arena, static schedule, control words.
+// ---------------------------------------------------------------------------------------------
+static bool persistent_supported(const Engine* E) {
+  const char* v = getenv("LLAMA_B200_PERSISTENT");
+  if (v && std::strcmp(v, "0") == 0) return false;
+  return E->dim == 2048 && (E->ffn == 2048 || E->ffn == 4096 || E->ffn == 8192) && E->vocab % 16 == 0 &&
+         E->kv_dim % 16 == 0 &&
+         (E->dim + 2 * E->kv_dim) % 16 == 0;
+}
+
+static size_t persistent_smem() {
+  return (size_t)kRingSlots * kRecBytes + kImageBytes + kMiscFloats * 4 + 2 * kRingSlots * 8;
+}
+
+static bool init_persistent(Engine* E) {
+  if (!persistent_supported(E)) return true;
+  const int L = (int)E->layers, G = E->num_sms;
+  const size_t smem = persistent_smem();
+  LE_CK(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, kPThreads, smem));
+  if (per_sm < 1) return true;  // keep the kernel-chain path
+  // record arena: per layer [q|k|v tiles][o tiles][gate tiles][up tiles][down tiles x 4], lm_head
+  const size_t rec_qkv = (E->dim + 2 * E->kv_dim) / 16, rec_o = E->dim / 16, rec_g = E->ffn / 16;
+  const size_t rec_d = (E->dim / 16) * (E->ffn / 2048), rec_lm = E->vocab / 16;
+  const size_t per_layer = rec_qkv + rec_o + 2 * rec_g + rec_d;
+  const size_t nrec_total = per_layer * L + rec_lm;
+  E->rec_bytes = nrec_total * kRecBytes;
+  LE_CK(cudaMalloc(&E->rec_arena, E->rec_bytes));
+  auto layer_base = [&](int l) { return (size_t)l * per_layer; };
+  auto repack = [&](const QMat& W, size_t rec0) -> bool {
+    k_repack<<<E->num_sms * 8, 256, 0, E->stream>>>(W, E->rec_arena + rec0 * kRecBytes);
+    LE_CK(cudaGetLastError());
+    return true;
+  };
+  for (int l = 0; l < L; ++l) {
+    const DevLayer& D = E->L[l];
+    size_t b = layer_base(l);
+    if (!repack(D.q, b)) return false;
+    if (!repack(D.k, b + E->dim / 16)) return false;
+    if (!repack(D.v, b + (E->dim + E->kv_dim) / 16)) return false;
+    b += rec_qkv;
+    if (!repack(D.o, b)) return false;
+    b += rec_o;
+    if (!repack(D.g, b)) return false;
+    if (!repack(D.u, b + rec_g)) return false;
+    b += 2 * rec_g;
+    if (!repack(D.d, b)) return false;
+  }
+  const size_t lm_base = per_layer * L;
+  if (!repack(E->lm_head, lm_base)) return false;
+
+  // ---- static schedule ----
+  struct CtaLists { std::vector<PSeg> segs; std::vector<PItem> items; std::vector<unsigned long long> recs; };
+  std::vector<CtaLists> C(G);
+  std::vector<int> warp_rr(G, 0);
+  int rot = 0;
+  auto add_phase = [&](uint16_t kind, int layer, int n_items, int nrec_per_item,
+                       const std::function<size_t(int, int)>& rec_of, const std::function<int(int)>& cta_of) {
+    std::vector<std::vector<int>> per(G);
+    for (int i = 0; i < n_items; ++i) per[cta_of(i)].push_back(i);
+    for (int c = 0; c < G; ++c) {
+      if (per[c].empty()) continue;
+      PSeg sg{kind, (uint16_t)layer, (uint32_t)C[c].items.size(), 0};
+      int w = 0;
+      for (int i : per[c]) {
+        PItem it{};
+        it.kind = kind;
+        it.layer = (uint16_t)layer;
+        it.tile = (uint32_t)i;
+        it.rec = (uint32_t)C[c].recs.size();
+        it.nrec = (uint16_t)nrec_per_item;
+        it.warp = (uint16_t)(w++ % kPConsumerWarps);
+        for (int r = 0; r < nrec_per_item; ++r) C[c].recs.push_back((unsigned long long)rec_of(i, r) * kRecBytes);
+        C[c].items.push_back(it);
+      }
+      sg.item_end = (uint32_t)C[c].items.size();
+      C[c].segs.push_back(sg);
+    }
+  };
+  const int n_qkv = (int)rec_qkv, n_o = (int)rec_o, n_gu = (int)rec_g, n_down = (int)(E->dim / 16);
+  const int kq_down = (int)(E->ffn / 2048), n_lm = (int)rec_lm;
+  for (int l = 0; l < L; ++l) {
+    const size_t b = layer_base(l);
+    int r0 = rot;
+    add_phase(PK_QKV, l, n_qkv, 1, [&](int i, int) { return b + i; }, [&](int i) { return (r0 + i) % G; });
+    rot = (rot + n_qkv) % G;
+    add_phase(PK_ATTN, l, (int)E->heads, 0, [&](int, int) { return (size_t)0; },
+              [&](int h) { return (int)(((long long)h * G) / E->heads + G / (2 * (int)E->heads)) % G; });
+    r0 = rot;
+    add_phase(PK_O, l, n_o, 1, [&](int i, int) { return b + rec_qkv + i; }, [&](int i) { return (r0 + i) % G; });
+    rot = (rot + n_o) % G;
+    r0 = rot;
+    add_phase(PK_GATEUP, l, n_gu, 2,
+              [&](int i, int r) { return b + rec_qkv + rec_o + (r == 0 ? 0 : rec_g) + i; },
+              [&](int i) { return (r0 + i) % G; });
+    rot = (rot + n_gu) % G;
+    r0 = rot;
+    add_phase(PK_DOWN, l, n_down, kq_down,
+              [&](int i, int r) { return b + rec_qkv + rec_o + 2 * rec_g + (size_t)i * kq_down + r; },
+              [&](int i) { return (r0 + i) % G; });
+    rot = (rot + n_down) % G;
+  }
+  std::vector<uint32_t> nrec_nolm(G);
+  for (int c = 0; c < G; ++c) nrec_nolm[c] = (uint32_t)C[c].recs.size();
+  {
+    const int r0 = rot;
+    add_phase(PK_LMHEAD, L, n_lm, 1, [&](int i, int) { return lm_base + i; }, [&](int i) { return (r0 + i) % G; });
+  }
+  int n_lm_ctas = 0;
+  for (int c = 0; c < G; ++c)
+    for (const auto& sg : C[c].segs)
+      if (sg.kind == PK_LMHEAD) ++n_lm_ctas;
+  std::vector<PCtaSched> sched(G);
+  std::vector<PSeg> segs;
+  std::vector<PItem> items;
+  std::vector<unsigned long long> recs;
+  for (int c = 0; c < G; ++c) {
+    sched[c].seg_off = (uint32_t)segs.size();
+    sched[c].nseg = (uint32_t)C[c].segs.size();
+    sched[c].item_off = (uint32_t)items.size();
+    sched[c].nitem = (uint32_t)C[c].items.size();
+    sched[c].rec_off = (uint32_t)recs.size();
+    sched[c].nrec = (uint32_t)C[c].recs.size();
+    sched[c].nrec_nolm = nrec_nolm[c];
+    segs.insert(segs.end(), C[c].segs.begin(), C[c].segs.end());
+    items.insert(items.end(), C[c].items.begin(), C[c].items.end());
+    recs.insert(recs.end(), C[c].recs.begin(), C[c].recs.end());
+  }
+  auto upload = [&](void** dst, const void* src, size_t bytes) -> bool {
+    LE_CK(cudaMalloc(dst, std::max<size_t>(bytes, 16)));
+    if (bytes) LE_CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+    return true;
+  };
+  if (!upload((void**)&E->d_sched, sched.data(), sched.size() * sizeof(PCtaSched))) return false;
+  if (!upload((void**)&E->d_segs, segs.data(), segs.size() * sizeof(PSeg))) return false;
+  if (!upload((void**)&E->d_items, items.data(), items.size() * sizeof(PItem))) return false;
+  if (!upload((void**)&E->d_recs, recs.data(), recs.size() * sizeof(unsigned long long))) return false;
+  std::vector<const float*> norms;
+  for (int l = 0; l < L; ++l) { norms.push_back(E->L[l].in_norm); norms.push_back(E->L[l].post_norm); }
+  norms.push_back(E->final_norm);
+  if (!upload((void**)&E->d_norms, norms.data(), norms.size() * sizeof(float*))) return false;
+  LE_CK(cudaMalloc(&E->d_ctr, ctr_count(L) * sizeof(uint32_t)));
+  LE_CK(cudaMemset(E->d_ctr, 0, ctr_count(L) * sizeof(uint32_t)));
+  LE_CK(cudaMalloc(&E->d_ctrl, sizeof(PCtrl)));
+  LE_CK(cudaMemset(E->d_ctrl, 0, sizeof(PCtrl)));
+  LE_CK(cudaMallocHost(&E->h_err, 4 * sizeof(uint32_t)));
+  E->h_err[0] = E->h_err[1] = 0;
+
+  PArgs& A = E->pargs;
+  A.arena = E->rec_arena;
+  A.sched = E->d_sched; A.segs = E->d_segs; A.items = E->d_items; A.recs = E->d_recs;
+  A.norms = E->d_norms;
+  A.rope_cos = E->rope_cos; A.rope_sin = E->rope_sin;
+  A.x = E->x; A.qkv = E->qkv; A.attn = E->attn; A.act = E->act; A.logits = E->logits;
+  A.kcache = E->kcache; A.vcache = E->vcache;
+  A.ctr = E->d_ctr; A.ctrl = E->d_ctrl; A.prm = E->d_params;
+  A.token_log = E->token_log; A.am_result = E->am_result;
+  A.lm_rec_base = (unsigned long long)lm_base * kRecBytes;
+  A.layers = L; A.dim = (int)E->dim; A.ffn = (int)E->ffn; A.vocab = (int)E->vocab;
+  A.heads = (int)E->heads; A.kv_heads = (int)E->kv_heads; A.max_seq = E->max_seq;
+  A.n_qkv_items = n_qkv; A.n_o_items = n_o; A.n_gu_items = n_gu; A.n_down_items = n_down;
+  A.n_lm_ctas = n_lm_ctas;
+  A.n_tokens = 1; A.do_logits = 1;
+  E->p_grid = G;
+  LE_CK(cudaStreamSynchronize(E->stream));
+  E->persist = true;
+  return true;
+}
+
+// One cooperative launch of n_tokens steps on slot 0 (parameters already queued).
+static bool launch_persistent(Engine* E, int n_tokens, bool logits) {
+  PArgs A = E->pargs;
+  A.n_tokens = n_tokens;
+  A.do_logits = logits ? 1 : 0;
+  void* args[] = {&A};
+  LE_CK(cudaLaunchCooperativeKernel((const void*)k_decode_persistent, dim3(E->p_grid), dim3(kPThreads), args,
+                                    persistent_smem(), E->stream));
+  return true;
+}
+
+// Reads the persistent kernel's error word (after the stream has been synchronised).
+static bool persistent_ok(Engine* E) {
+  if (!E->persist) return true;
+  LE_CK(cudaMemcpyAsync(E->h_err, &E->d_ctrl->error, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
+  LE_CK(cudaStreamSynchronize(E->stream));
+  if (E->h_err[0] != 0) {
+    E->err = "persistent decode kernel: a dependency wait timed out (code " + std::to_string(E->h_err[1]) + ")";
+    return false;
+  }
+  return true;
+}
+
 static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   LE_CK(cudaSetDevice(E->device));
   LE_CK(cudaDeviceGetAttribute(&E->num_sms, cudaDevAttrMultiProcessorCount, E->device));
@@ -400,6 +612,7 @@ static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   if (!capture(E, row_buffers(E, 0, 0, true, 0), &E->g_fwd[1])) return false;
   if (!capture(E, row_buffers(E, 0, 0, true, 1), &E->g_gen)) return false;
   LE_CK(cudaStreamSynchronize(E->stream));
+  if (!init_persistent(E)) return false;
   return true;
 }
 
@@ -410,6 +623,9 @@ static void destroy(Engine* E) {
   for (auto& g : E->g_fwd) if (g) cudaGraphExecDestroy(g);
   if (E->g_gen) cudaGraphExecDestroy(E->g_gen);
   for (auto& ev : E->ring_ev) if (ev) cudaEventDestroy(ev);
+  void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_ctr, E->d_ctrl};
+  for (void* p : pdev) if (p) cudaFree(p);
+  if (E->h_err) cudaFreeHost(E->h_err);
   void* dev_ptrs[] = {E->arena, E->rope_cos, E->rope_sin, E->kcache, E->vcache, E->x, E->qkv, E->attn,
                       E->act, E->logits, E->emb, E->red, E->d_misc, E->part, E->am_result, E->token_log, E->d_params};
   for (void* p : dev_ptrs) if (p) cudaFree(p);
@@ -471,7 +687,11 @@ static bool forward_token(Engine* E, int32_t token, size_t pos, bool logits) {
   if (pos >= (size_t)E->max_seq) return true;  // silent no-op, src/llama_engine.cpp:936
   if (token < 0 || token >= (int32_t)E->vocab) token = 0;  // :937
   if (!queue_params(E, token, (int32_t)pos)) return false;
-  LE_CK(cudaGraphLaunch(E->g_fwd[logits ? 1 : 0], E->stream));
+  if (E->persist) {
+    if (!launch_persistent(E, 1, logits)) return false;
+  } else {
+    LE_CK(cudaGraphLaunch(E->g_fwd[logits ? 1 : 0], E->stream));
+  }
   if (logits) {
     E->logits_on_host_fresh = false;
     E->argmax_valid = true;
@@ -490,6 +710,7 @@ static bool greedy(Engine* E, int32_t* out) {
   }
   LE_CK(cudaMemcpyAsync(E->h_small, E->am_result, 4, cudaMemcpyDeviceToHost, E->stream));
   LE_CK(cudaStreamSynchronize(E->stream));
+  if (!persistent_ok(E)) return false;
   *out = E->h_small[0];
   return true;
 }
@@ -498,6 +719,7 @@ static bool sync_logits(Engine* E) {
   if (!E->logits_on_host_fresh) {
     LE_CK(cudaMemcpyAsync(E->h_logits, E->logits, (size_t)E->vocab * 4, cudaMemcpyDeviceToHost, E->stream));
     LE_CK(cudaStreamSynchronize(E->stream));
+    if (!persistent_ok(E)) return false;
     E->logits_on_host_fresh = true;
   }
   return true;
@@ -642,12 +864,17 @@ LE_API int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_tok
   if (first_token < 0 || first_token >= (int32_t)E->vocab) first_token = 0;
   if (!queue_params(E, first_token, (int32_t)start_pos)) return -1;
   E->last_pos = (int32_t)(start_pos + n_steps - 1);
-  for (int32_t i = 0; i < n_steps; ++i)
-    if (cudaGraphLaunch(E->g_gen, E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
+  if (E->persist) {
+    if (!launch_persistent(E, n_steps, true)) return -1;
+  } else {
+    for (int32_t i = 0; i < n_steps; ++i)
+      if (cudaGraphLaunch(E->g_gen, E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
+  }
   if (cudaMemcpyAsync(out_tokens, E->token_log, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess)
     return -1;
   cudaError_t ce = cudaStreamSynchronize(E->stream);
   if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
+  if (!persistent_ok(E)) return -1;
   E->logits_on_host_fresh = false;
   E->argmax_valid = true;
   E->have_logits = true;
@@ -680,6 +907,35 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
   return 0;
 }
 
+LE_API int llama_engine_trace(llama_engine_t engine, int enable, unsigned long long* out, int max_entries) {
+  if (!engine) return -1;
+  Engine* E = H(engine);
+  if (!E->persist) return -1;
+  DeviceGuard dg(E->device);
+  const size_t n = (size_t)E->p_grid * kTraceCap * 2;
+  if (enable == 1) {
+    if (!E->d_trace && cudaMalloc(&E->d_trace, n * 8) != cudaSuccess) return -1;
+    if (cudaMemsetAsync(E->d_trace, 0, n * 8, E->stream) != cudaSuccess) return -1;
+    E->pargs.trace = E->d_trace;
+    return 0;
+  }
+  if (enable == 0) {
+    E->pargs.trace = nullptr;
+    return 0;
+  }
+  // enable == 2: copy out (grid * kTraceCap pairs of (globaltimer ns, tag))
+  if (!E->d_trace || !out) return -1;
+  const size_t m = std::min<size_t>(n, (size_t)std::max(0, max_entries) * 2);
+  if (cudaMemcpyAsync(out, E->d_trace, m * 8, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess) return -1;
+  if (cudaStreamSynchronize(E->stream) != cudaSuccess) return -1;
+  return (int)std::min<size_t>((size_t)E->p_grid * kTraceCap, (size_t)std::max(0, max_entries));
+}
+
+LE_API int llama_engine_decode_path(llama_engine_t engine) {
+  if (!engine) return -1;
+  return H(engine)->persist ? 1 : 0;
+}
+
 LE_API void* llama_engine_get_stream(llama_engine_t engine) { return engine ? (void*)H(engine)->stream : nullptr; }
 
 LE_API int llama_engine_profile_phase(llama_engine_t engine, const char* phase, int iters, float* avg_ms) {
@@ -704,7 +960,10 @@ LE_API int llama_engine_profile_phase(llama_engine_t engine, const char* phase, 
   }
   cudaEventRecord(a, E->stream);
   for (int i = 0; i < iters; ++i) {
-    if (step) cudaGraphLaunch(E->g_fwd[1], E->stream);
+    if (step) {
+      if (E->persist) launch_persistent(E, 1, true);
+      else cudaGraphLaunch(E->g_fwd[1], E->stream);
+    }
     else enqueue_phase(E, B, ph, (uint32_t)(i % E->layers), E->stream);
   }
   cudaEventRecord(b, E->stream);

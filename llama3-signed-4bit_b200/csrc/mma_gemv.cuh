@@ -61,12 +61,11 @@ __device__ __forceinline__ void stage_digits(const float* xs, int MX, int K, Dig
     s = warp_sum(s);
     a = warp_max(a);
     if (lane == 0) {
-      int ex = 0;
-      if (a > 0.0f) frexpf(a, &ex);  // a < 2^ex
-      int e = 29 - ex;
-      if (e > 126) e = 126;
+      // a < 2^ex with ex from the exponent field (denormals bounded by 2^-126)
+      const int ex = max((int)((__float_as_uint(a) >> 23) & 0xFFu), 1) - 126;
+      const int e = min(29 - ex, 126);
       img.bsum[mb] = s;
-      img.escl[mb] = (a > 0.0f) ? ldexpf(1.0f, -e) : 0.0f;
+      img.escl[mb] = (a > 0.0f) ? __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
     }
   }
   // Zero the unused half of the last n-tile when MX is odd (lanes 16..31 of n-tile NT-1).
@@ -82,12 +81,13 @@ __device__ __forceinline__ void stage_digits(const float* xs, int MX, int K, Dig
   for (int u = threadIdx.x; u < units; u += blockDim.x) {
     const int h = u & 1, t = (u >> 1) & 3, i = (u >> 3) & 3, b = (u >> 5) % nb, m = (u >> 5) / nb;
     const float es = img.escl[m * nb + b];
-    const int e = es > 0.0f ? -ilogbf(es) : 0;
+    const int e = es > 0.0f ? 127 - (int)(__float_as_uint(es) >> 23) : 0;
+    const float up = __uint_as_float((uint32_t)(e + 127) << 23);  // 2^e
     uint32_t plane[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float xv = xs[(size_t)m * K + b * 128 + 32 * t + 8 * i + 2 * j + h];
-      int X = es > 0.0f ? __float2int_rn(ldexpf(xv, e)) : 0;
+      int X = es > 0.0f ? __float2int_rn(xv * up) : 0;
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const int d = ((X + 128) & 255) - 128;

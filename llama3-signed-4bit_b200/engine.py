@@ -69,6 +69,14 @@ class LlamaEngineBindings:
         # extensions
         lib.llama_engine_create_ex.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         lib.llama_engine_create_ex.restype = _P
+        lib.llama_engine_decode_path.argtypes = [_P]
+        lib.llama_engine_decode_path.restype = ctypes.c_int
+        lib.llama_engine_trace.argtypes = [_P, ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
+        lib.llama_engine_trace.restype = ctypes.c_int
+        lib.llama_engine_get_stream.argtypes = [_P]
+        lib.llama_engine_get_stream.restype = _P
+        lib.llama_engine_profile_phase.argtypes = [_P, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]
+        lib.llama_engine_profile_phase.restype = ctypes.c_int
         lib.llama_engine_last_error.argtypes = [_P]
         lib.llama_engine_last_error.restype = ctypes.c_char_p
         lib.llama_engine_generate_greedy.argtypes = [_P, ctypes.c_int32, ctypes.c_size_t, ctypes.c_int32, _I32P]
@@ -211,6 +219,10 @@ class LlamaEngine:
         if not ptr:
             raise RuntimeError("get_logits_batch failed")
         return np.ctypeslib.as_array(ptr, shape=(self.vocab_size,)).copy()
+
+    @property
+    def decode_path(self) -> str:
+        return {1: "persistent", 0: "kernel-chain"}.get(self.bindings.lib.llama_engine_decode_path(self.handle), "?")
 
     def close(self):
         if getattr(self, "handle", None):

@@ -81,13 +81,21 @@ def ref_engine():
 
 # Small model with the reference's fixed attention geometry (32 heads of 64, 8 kv heads: the
 # reference hard-codes 4 head groups of 8 and kv_h = h/4, src/llama_engine.cpp:960-966).
-SMALL_SHAPE = dict(layers=2, dim=2048, ffn=1024, vocab=4096, heads=32, kv_heads=8)
+SMALL_SHAPE = dict(layers=2, dim=2048, ffn=2048, vocab=4096, heads=32, kv_heads=8)
+# ffn not a multiple of 2048: served by the per-phase kernel chain
+CHAIN_SHAPE = dict(layers=2, dim=2048, ffn=1024, vocab=4096, heads=32, kv_heads=8)
 
 
 @pytest.fixture(scope="session")
 def small_model(pkg, cache_dir):
     shape = pkg.model_file.ModelShape(**SMALL_SHAPE)
     return pkg.model_file.cached_model(cache_dir, shape, seed=7, sigma=0.02, random_norms=True)
+
+
+@pytest.fixture(scope="session")
+def chain_model(pkg, cache_dir):
+    shape = pkg.model_file.ModelShape(**CHAIN_SHAPE)
+    return pkg.model_file.cached_model(cache_dir, shape, seed=9, sigma=0.02, random_norms=True)
 
 
 @pytest.fixture(scope="session")

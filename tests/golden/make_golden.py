@@ -5,7 +5,7 @@
     python tests/golden/make_golden.py small      # only the small-model fixture
 
 Fixtures:
-* ``small_greedy.npz`` — 2-layer model (dim 2048, 32/8 heads, ffn 1024, vocab 4096, seed 7,
+* ``small_greedy.npz`` — 2-layer model (dim 2048, 32/8 heads, ffn 2048, vocab 4096, seed 7,
   random norm weights), 9-token prompt, prefill 8 + 24 greedy steps: ids, top-2 margins and full
   logits of every step.
 * ``config0_greedy.npz`` — the LLaMA-3.2-1B shape (16 layers, dim 2048, ffn 8192, vocab 128256),
@@ -79,7 +79,7 @@ def run_reference(model_path: Path, prompt: np.ndarray, n_gen: int, full_logit_s
 
 def make_small(cache: Path):
     pkg = _pkg()
-    shape = pkg.model_file.ModelShape(layers=2, dim=2048, ffn=1024, vocab=4096, heads=32, kv_heads=8)
+    shape = pkg.model_file.ModelShape(layers=2, dim=2048, ffn=2048, vocab=4096, heads=32, kv_heads=8)
     model = pkg.model_file.cached_model(cache, shape, seed=7, sigma=0.02, random_norms=True)
     prompt = np.random.default_rng(11).integers(0, shape.vocab, 9).astype(np.int32)
     n_gen = 24

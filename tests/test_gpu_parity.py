@@ -107,6 +107,7 @@ def _oracle_logits(oracle_lib, o, vocab):
 def test_small_model_golden(small_engine):
     g = np.load(GOLDEN / "small_greedy.npz")
     eng = small_engine
+    assert eng.decode_path == "persistent"
     prompt = [int(t) for t in g["prompt"]]
     eng.reset()
     eng.prefill(prompt[:-1], 0, False)
@@ -241,6 +242,7 @@ def test_config0_golden(pkg, bindings, full_model):
     g = np.load(GOLDEN / "config0_greedy.npz")
     assert pkg.model_file.file_sha256(full_model) == str(g["model_sha256"]), "generator output differs"
     eng = pkg.LlamaEngine(str(full_model), bindings)
+    assert eng.decode_path == "persistent"
     try:
         prompt = [int(t) for t in g["prompt"]]
         eng.prefill(prompt[:-1], 0, False)
@@ -265,3 +267,46 @@ def test_config0_golden(pkg, bindings, full_model):
         assert not mismatches, f"greedy id mismatch at (step, top-2 margin) {mismatches}"
     finally:
         eng.close()
+
+
+def test_kernel_chain_path_vs_oracle(pkg, bindings, chain_model, oracle_lib):
+    """Geometries outside the persistent kernel's (here ffn 1024) run the per-phase kernel chain."""
+    eng = pkg.LlamaEngine(str(chain_model), bindings)
+    o = oracle_lib.orc_create(str(chain_model).encode())
+    try:
+        assert eng.decode_path == "kernel-chain"
+        vocab = eng.vocab_size
+        ids = np.random.default_rng(8).integers(0, vocab, 20).astype(np.int32)
+        eng.prefill([int(t) for t in ids], 0, True)
+        oracle_lib.orc_prefill(o, fptr(ids), len(ids), 0, 1)
+        assert rel_max_err(eng.get_logits(), _oracle_logits(oracle_lib, o, vocab)) <= LOGIT_RTOL
+        tok = eng.sample(0.0, 0.9)
+        assert tok == oracle_lib.orc_sample_engine(o, ctypes.c_float(0.0), ctypes.c_float(0.9))
+        for pos in range(20, 24):
+            eng.forward_token(tok, pos, True)
+            oracle_lib.orc_forward_token(o, tok, pos, 1)
+            assert rel_max_err(eng.get_logits(), _oracle_logits(oracle_lib, o, vocab)) <= LOGIT_RTOL
+            tok = eng.sample(0.0, 0.9)
+            assert tok == oracle_lib.orc_sample_engine(o, ctypes.c_float(0.0), ctypes.c_float(0.9))
+    finally:
+        oracle_lib.orc_free(o)
+        eng.close()
+
+
+def test_persistent_matches_kernel_chain(pkg, bindings, small_model, monkeypatch):
+    """Same model, both decode paths: logits agree within the parity tolerance, ids identical."""
+    a = pkg.LlamaEngine(str(small_model), bindings)
+    monkeypatch.setenv("LLAMA_B200_PERSISTENT", "0")
+    b = pkg.LlamaEngine(str(small_model), bindings)
+    try:
+        assert a.decode_path == "persistent" and b.decode_path == "kernel-chain"
+        prompt = [5, 77, 1000, 4095, 12, 0, 9]
+        a.prefill(prompt, 0, True)
+        b.prefill(prompt, 0, True)
+        assert rel_max_err(a.get_logits(), b.get_logits()) <= LOGIT_RTOL
+        ga = a.generate_greedy(a.sample(0.0, 0.9), len(prompt), 12)
+        gb = b.generate_greedy(b.sample(0.0, 0.9), len(prompt), 12)
+        assert ga == gb
+    finally:
+        a.close()
+        b.close()
