@@ -195,7 +195,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     pkg = load_package()
-    shape = pkg.model_file.LLAMA_3_2_1B
+    shape = pkg.model_file.ModelShape(layers=args.layers)
     torch.cuda.set_device(local_rank)
     if world > 1:
         dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
@@ -329,9 +329,10 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "decode-b1: LLaMA-3.2-1B shape, LLM4S128 block-128 4-bit, seeded random-init "
-                                   "N(0,0.02) weights, batch 1 per GPU, greedy, 128-token generation at positions "
-                                   "31..158 repeated",
+            "config": {"workload": ("decode-b1: LLaMA-3.2-1B shape" if args.layers == 16 else
+                                    f"decode-b1 profiling model: LLaMA-3.2-1B widths, {args.layers} layers")
+                                   + ", LLM4S128 block-128 4-bit, seeded random-init N(0,0.02) weights, batch 1 per "
+                                   "GPU, greedy, 128-token generation at positions 31..158 repeated",
                        "global_batch": world, "seq_len": start + GEN_LEN, "parallelism": f"dp{world} (replicas)",
                        "l2": "no flush: 657 MB of weights streamed per step > 126 MB L2"},
             "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu,
@@ -395,6 +396,8 @@ def main():
     ap.add_argument("--ref-max-steps", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's phase timeline")
+    ap.add_argument("--layers", type=int, default=16,
+                    help="layers of the synthetic model (16 = LLaMA-3.2-1B; fewer only for profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -181,9 +181,9 @@ struct Engine {
   PCtaSched* d_sched = nullptr;
   PSeg* d_segs = nullptr;
   PItem* d_items = nullptr;
-  unsigned long long* d_recs = nullptr;
-  const float** d_norms = nullptr;
-  uint32_t* d_ctr = nullptr;
+  uint32_t* d_recs = nullptr;
+  float* d_norms = nullptr;  // [2*layers + 1][dim] contiguous copy of the norm weights
+  unsigned long long* d_tagged = nullptr;  // x | qkv | attn | act as (value, phase tag) words
   PCtrl* d_ctrl = nullptr;
   uint32_t* h_err = nullptr;  // pinned mirror of PCtrl::error / err_where
   unsigned long long* d_trace = nullptr;  // optional phase trace of the persistent kernel
@@ -326,7 +326,7 @@ static bool persistent_supported(const Engine* E) {
 }
 
 static size_t persistent_smem() {
-  return (size_t)kRingSlots * kRecBytes + kImageBytes + kMiscFloats * 4 + 2 * kRingSlots * 8;
+  return (size_t)kRingSlots * kRecBytes + kImageBytes + kMiscFloats * 4 + kRingSlots * 8 + kSchedBytes;
 }
 
 static bool init_persistent(Engine* E) {
@@ -336,7 +336,14 @@ static bool init_persistent(Engine* E) {
   LE_CK(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
   LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, kPThreads, smem));
-  if (per_sm < 1) return true;  // keep the kernel-chain path
+  if (per_sm < 1) {  // keep the kernel-chain path, and say why
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, k_decode_persistent);
+    E->err = "persistent kernel declined: 0 resident CTAs per SM (regs " + std::to_string(fa.numRegs) +
+             ", static smem " + std::to_string(fa.sharedSizeBytes) + ", dynamic smem " + std::to_string(smem) +
+             ", max threads " + std::to_string(fa.maxThreadsPerBlock) + ")";
+    return true;
+  }
   // record arena: per layer [q|k|v tiles][o tiles][gate tiles][up tiles][down tiles x 4], lm_head
   const size_t rec_qkv = (E->dim + 2 * E->kv_dim) / 16, rec_o = E->dim / 16, rec_g = E->ffn / 16;
   const size_t rec_d = (E->dim / 16) * (E->ffn / 2048), rec_lm = E->vocab / 16;
@@ -368,7 +375,7 @@ static bool init_persistent(Engine* E) {
   if (!repack(E->lm_head, lm_base)) return false;
 
   // ---- static schedule ----
-  struct CtaLists { std::vector<PSeg> segs; std::vector<PItem> items; std::vector<unsigned long long> recs; };
+  struct CtaLists { std::vector<PSeg> segs; std::vector<PItem> items; std::vector<uint32_t> recs; };
   std::vector<CtaLists> C(G);
   std::vector<int> warp_rr(G, 0);
   int rot = 0;
@@ -378,20 +385,21 @@ static bool init_persistent(Engine* E) {
     for (int i = 0; i < n_items; ++i) per[cta_of(i)].push_back(i);
     for (int c = 0; c < G; ++c) {
       if (per[c].empty()) continue;
-      PSeg sg{kind, (uint16_t)layer, (uint32_t)C[c].items.size(), 0};
-      int w = 0;
+      PSeg sg{};
+      sg.kind = (uint8_t)kind;
+      sg.layer = (uint16_t)layer;
+      sg.item_begin = (uint16_t)C[c].items.size();
       for (int i : per[c]) {
         PItem it{};
-        it.kind = kind;
+        it.kind = (uint8_t)kind;
         it.layer = (uint16_t)layer;
-        it.tile = (uint32_t)i;
-        it.rec = (uint32_t)C[c].recs.size();
-        it.nrec = (uint16_t)nrec_per_item;
-        it.warp = (uint16_t)(w++ % kPConsumerWarps);
-        for (int r = 0; r < nrec_per_item; ++r) C[c].recs.push_back((unsigned long long)rec_of(i, r) * kRecBytes);
+        it.tile = (uint16_t)i;
+        it.rec = (uint16_t)C[c].recs.size();
+        it.nrec = (uint8_t)nrec_per_item;
+        for (int r = 0; r < nrec_per_item; ++r) C[c].recs.push_back((uint32_t)rec_of(i, r));
         C[c].items.push_back(it);
       }
-      sg.item_end = (uint32_t)C[c].items.size();
+      sg.item_end = (uint16_t)C[c].items.size();
       C[c].segs.push_back(sg);
     }
   };
@@ -428,10 +436,19 @@ static bool init_persistent(Engine* E) {
   for (int c = 0; c < G; ++c)
     for (const auto& sg : C[c].segs)
       if (sg.kind == PK_LMHEAD) ++n_lm_ctas;
+  for (int c = 0; c < G; ++c) {
+    if (C[c].recs.size() > (size_t)kMaxRecs || C[c].items.size() > (size_t)kMaxItems ||
+        C[c].segs.size() > (size_t)kMaxSegs) {
+      E->err = "persistent kernel declined: a CTA's schedule exceeds its shared-memory capacity";
+      cudaFree(E->rec_arena);
+      E->rec_arena = nullptr;
+      return true;  // keep the kernel-chain path
+    }
+  }
   std::vector<PCtaSched> sched(G);
   std::vector<PSeg> segs;
   std::vector<PItem> items;
-  std::vector<unsigned long long> recs;
+  std::vector<uint32_t> recs;
   for (int c = 0; c < G; ++c) {
     sched[c].seg_off = (uint32_t)segs.size();
     sched[c].nseg = (uint32_t)C[c].segs.size();
@@ -452,13 +469,17 @@ static bool init_persistent(Engine* E) {
   if (!upload((void**)&E->d_sched, sched.data(), sched.size() * sizeof(PCtaSched))) return false;
   if (!upload((void**)&E->d_segs, segs.data(), segs.size() * sizeof(PSeg))) return false;
   if (!upload((void**)&E->d_items, items.data(), items.size() * sizeof(PItem))) return false;
-  if (!upload((void**)&E->d_recs, recs.data(), recs.size() * sizeof(unsigned long long))) return false;
-  std::vector<const float*> norms;
-  for (int l = 0; l < L; ++l) { norms.push_back(E->L[l].in_norm); norms.push_back(E->L[l].post_norm); }
-  norms.push_back(E->final_norm);
-  if (!upload((void**)&E->d_norms, norms.data(), norms.size() * sizeof(float*))) return false;
-  LE_CK(cudaMalloc(&E->d_ctr, ctr_count(L) * sizeof(uint32_t)));
-  LE_CK(cudaMemset(E->d_ctr, 0, ctr_count(L) * sizeof(uint32_t)));
+  if (!upload((void**)&E->d_recs, recs.data(), recs.size() * sizeof(uint32_t))) return false;
+  LE_CK(cudaMalloc(&E->d_norms, (size_t)(2 * L + 1) * E->dim * 4));
+  for (int l = 0; l < L; ++l) {
+    LE_CK(cudaMemcpy(E->d_norms + (size_t)(2 * l) * E->dim, E->L[l].in_norm, E->dim * 4, cudaMemcpyDeviceToDevice));
+    LE_CK(cudaMemcpy(E->d_norms + (size_t)(2 * l + 1) * E->dim, E->L[l].post_norm, E->dim * 4,
+                     cudaMemcpyDeviceToDevice));
+  }
+  LE_CK(cudaMemcpy(E->d_norms + (size_t)(2 * L) * E->dim, E->final_norm, E->dim * 4, cudaMemcpyDeviceToDevice));
+  const size_t n_tagged = (size_t)E->dim + (E->dim + 2 * E->kv_dim) + E->dim + E->ffn;
+  LE_CK(cudaMalloc(&E->d_tagged, n_tagged * sizeof(unsigned long long)));
+  LE_CK(cudaMemset(E->d_tagged, 0, n_tagged * sizeof(unsigned long long)));  // tag 0 is never valid
   LE_CK(cudaMalloc(&E->d_ctrl, sizeof(PCtrl)));
   LE_CK(cudaMemset(E->d_ctrl, 0, sizeof(PCtrl)));
   LE_CK(cudaMallocHost(&E->h_err, 4 * sizeof(uint32_t)));
@@ -469,14 +490,17 @@ static bool init_persistent(Engine* E) {
   A.sched = E->d_sched; A.segs = E->d_segs; A.items = E->d_items; A.recs = E->d_recs;
   A.norms = E->d_norms;
   A.rope_cos = E->rope_cos; A.rope_sin = E->rope_sin;
-  A.x = E->x; A.qkv = E->qkv; A.attn = E->attn; A.act = E->act; A.logits = E->logits;
+  A.x = E->d_tagged;
+  A.qkv = A.x + E->dim;
+  A.attn = A.qkv + E->dim + 2 * E->kv_dim;
+  A.act = A.attn + E->dim;
+  A.logits = E->logits;
   A.kcache = E->kcache; A.vcache = E->vcache;
-  A.ctr = E->d_ctr; A.ctrl = E->d_ctrl; A.prm = E->d_params;
+  A.ctrl = E->d_ctrl; A.prm = E->d_params;
   A.token_log = E->token_log; A.am_result = E->am_result;
   A.lm_rec_base = (unsigned long long)lm_base * kRecBytes;
   A.layers = L; A.dim = (int)E->dim; A.ffn = (int)E->ffn; A.vocab = (int)E->vocab;
   A.heads = (int)E->heads; A.kv_heads = (int)E->kv_heads; A.max_seq = E->max_seq;
-  A.n_qkv_items = n_qkv; A.n_o_items = n_o; A.n_gu_items = n_gu; A.n_down_items = n_down;
   A.n_lm_ctas = n_lm_ctas;
   A.n_tokens = 1; A.do_logits = 1;
   E->p_grid = G;
@@ -623,7 +647,7 @@ static void destroy(Engine* E) {
   for (auto& g : E->g_fwd) if (g) cudaGraphExecDestroy(g);
   if (E->g_gen) cudaGraphExecDestroy(E->g_gen);
   for (auto& ev : E->ring_ev) if (ev) cudaEventDestroy(ev);
-  void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_ctr, E->d_ctrl};
+  void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged, E->d_ctrl};
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
   void* dev_ptrs[] = {E->arena, E->rope_cos, E->rope_sin, E->kcache, E->vcache, E->x, E->qkv, E->attn,

@@ -1,24 +1,34 @@
 // Persistent token-step kernel for batch-1 decode (sm_100a).
 //
 // One cooperative launch runs whole token steps (src/llama_engine.cpp:935-1042 and the greedy
-// sampler :784-792): one CTA per SM, each with
-//   * a producer warp that streams the CTA's weight records from HBM into a shared-memory ring
-//     with cp.async.bulk (TMA bulk copies) and mbarriers, running ahead across phases and layers
-//     (weights never depend on activations), and
-//   * eight consumer warps that, phase by phase, wait for the phase's inputs through
-//     release/acquire counters in global memory, stage the input vector as MMA digit fragments
-//     (rms-norm fused where the reference normalises), and reduce their records on the integer
-//     tensor-core path (mma_gemv.cuh).
+// sampler :784-792): one CTA of 16 warps per SM.  The CTA's weight records stream from HBM into
+// a 10-slot shared-memory ring with cp.async.bulk (TMA bulk copies) and mbarriers: the ring is
+// filled at start, and the warps that finish a record immediately issue the copy of the record
+// ten positions later into the freed slot, so the weight stream runs ahead across phases and
+// layers (weights never depend on activations).  Phase by phase the warps stage the phase's
+// input vector as MMA digit fragments (rms-norm fused where the reference normalises) and reduce
+// their records on the integer tensor-core path (mma_gemv.cuh).
 // Phases of layer l: QKV rows -> attention per head (RoPE, KV append, softmax, PV) -> o-proj
 // rows (+ residual) -> gate/up rows (SiLU * up) -> down rows (+ residual); then lm_head rows with
 // a fused greedy argmax.  Every phase's work is split statically over the CTAs by a host-built
-// schedule.  All waits are bounded in time; on timeout a global error word is set, every later
-// wait returns immediately and the launch drains, so the host sees an error, never a hang.
+// schedule.
+//
+// Hand-offs between phases are self-validating: every activation element (x, q|k|v, attention
+// output, SwiGLU output) is one 64-bit word, fp32 value in the low half and a phase tag in the
+// high half, written with one 64-bit store and read with 64-bit relaxed loads, so a staging load
+// is its own readiness check (no fences, counters or polls on the data path).  The tag of
+// (token step s, layer l, phase p) is unique over a launch and its neighbours.  Each element has
+// exactly one writer per phase, and the dependency chain guarantees that no element is
+// overwritten before every reader of its previous value has read it.
+//
+// All waits are bounded in time; on timeout a global error word is set, every later wait returns
+// at once and the launch drains, so the host sees an error, never a hang.
 //
 // Record format (built at load time from the LLM4S128 matrices): 16 rows x 16 blocks
 // (2048 columns) of one matrix, 17408 bytes:
-//   [0, 16384): for block j = 0..15, lane L = 0..31 (g = L/4, t = L%4): 16 bytes of row g at
-//               block bytes [16t, 16t+16), then 16 bytes of row g+8 (the MMA A fragments);
+//   [0, 16384): block j = 0..15 takes 1024 bytes: for lane L = 0..31 (g = L/4, t = L%4), the 16
+//               bytes of row g at block bytes [16t, 16t+16) at j*1024 + L*16, and the 16 bytes of
+//               row g+8 at j*1024 + 512 + L*16 (the MMA A fragments, conflict-free 16-byte loads);
 //   [16384, 17408): for block j, row r = 0..15: u32 = step_bf16 | min_bf16 << 16.
 #pragma once
 
@@ -28,26 +38,37 @@ namespace le {
 
 constexpr int kRecBytes = 17408;
 constexpr int kRecNibBytes = 16384;
-constexpr int kPConsumerWarps = 8;
-constexpr int kPThreads = 32 * (kPConsumerWarps + 1);
+constexpr int kPConsumerWarps = 16;
+constexpr int kPThreads = 32 * kPConsumerWarps;
 constexpr int kRingSlots = 10;
-constexpr int kMiscFloats = 1536;  // attention scratch (q, k, v, reductions, 16x64 partials)
+constexpr int kMiscFloats = 2304;          // attention scratch (q, k, v, reductions, 32x64 partials)
 constexpr int kImageBytes = 32768 + 1024;  // digit fragments for K <= 8192, or attention scores
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every wait
+constexpr int kTraceCap = 1024;
 
 enum PKind : uint16_t { PK_QKV = 0, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN, PK_LMHEAD };
+// phase tags of the activation hand-offs
+enum PTag : uint32_t { TG_XIN = 0, TG_QKV = 1, TG_ATTN = 2, TG_XO = 3, TG_ACT = 4 };
 
+// Schedule entries are packed small: each CTA copies its whole schedule into shared memory at
+// launch, so no descriptor load sits on the critical path.
 struct PItem {
-  uint16_t kind, layer;
-  uint32_t tile;      // row tile (16 rows) within the phase's row space; head index for PK_ATTN
-  uint32_t rec;       // first record of the item in the CTA's per-token record stream
-  uint16_t nrec, warp;
+  uint8_t kind, nrec;
+  uint16_t layer;
+  uint16_t tile;      // row tile (16 rows) within the phase's row space; head index for PK_ATTN
+  uint16_t rec;       // first record of the item in the CTA's per-token record stream
 };
 
 struct PSeg {
-  uint16_t kind, layer;
-  uint32_t item_begin, item_end;
+  uint8_t kind, pad;
+  uint16_t layer;
+  uint16_t item_begin, item_end;
 };
+
+constexpr int kMaxRecs = 512;   // per CTA and token
+constexpr int kMaxItems = 512;
+constexpr int kMaxSegs = 128;
+constexpr int kSchedBytes = kMaxRecs * 4 + kMaxItems * 8 + kMaxSegs * 8;
 
 struct PCtaSched {
   uint32_t seg_off, nseg;
@@ -64,7 +85,8 @@ struct PCtrl {
   uint32_t done_ctas;  // CTAs finished in the current launch
   uint32_t error;      // nonzero after a wait timed out
   uint32_t err_where;  // code of the first wait that timed out
-  uint32_t pad[3];
+  uint32_t lm_ctr;     // CTAs done with the lm_head (monotonic, generate-mode token feedback)
+  uint32_t pad[2];
   unsigned long long key[3];  // packed greedy candidates, by lm step modulo 3
 };
 
@@ -73,40 +95,31 @@ struct PArgs {
   const PCtaSched* sched;
   const PSeg* segs;
   const PItem* items;
-  const unsigned long long* recs; // byte offsets of records in `arena`
-  const float* const* norms;      // [2*layers + 1]: in_norm[l], post_norm[l] ..., final_norm
+  const uint32_t* recs;           // record indices into `arena` (byte offset = index * kRecBytes)
+  const float* norms;             // [2*layers + 1][dim]: in_norm[l], post_norm[l] ..., final_norm
   const float* rope_cos;
   const float* rope_sin;
-  float* x;         // [dim]
-  float* qkv;       // [dim + 2*kv_dim]
-  float* attn;      // [dim]
-  float* act;       // [ffn]
+  unsigned long long* x;    // [dim]            tagged
+  unsigned long long* qkv;  // [dim + 2 kv_dim] tagged
+  unsigned long long* attn; // [dim]            tagged
+  unsigned long long* act;  // [ffn]            tagged
   float* logits;    // [vocab]
   float* kcache;    // slot 0: [layers][max_seq][kv_dim]
   float* vcache;
-  uint32_t* ctr;    // counters
   PCtrl* ctrl;
   const StepParams* prm;
   int32_t* token_log;
   int32_t* am_result;
   unsigned long long lm_rec_base;  // record offset of lm_head tile 0 (embedding lookup)
   int layers, dim, ffn, vocab, heads, kv_heads, max_seq;
-  int n_qkv_items, n_o_items, n_gu_items, n_down_items, n_lm_ctas;
+  int n_lm_ctas;
   int n_tokens, do_logits;
   unsigned long long* trace;  // optional: per CTA kTraceCap (time, tag) pairs, first token only
 };
 
-constexpr int kTraceCap = 1024;
-
-// Counter layout: per layer 5 counters, then emb and lm.
-__host__ __device__ inline int ctr_x(int l) { return 5 * l + 0; }   // x ready for layer l (l >= 1)
-__host__ __device__ inline int ctr_qkv(int l) { return 5 * l + 1; }
-__host__ __device__ inline int ctr_attn(int l) { return 5 * l + 2; }
-__host__ __device__ inline int ctr_o(int l) { return 5 * l + 3; }
-__host__ __device__ inline int ctr_act(int l) { return 5 * l + 4; }
-__host__ __device__ inline int ctr_emb(int layers) { return 5 * layers + 5; }
-__host__ __device__ inline int ctr_lm(int layers) { return 5 * layers + 6; }
-__host__ __device__ inline int ctr_count(int layers) { return 5 * layers + 8; }
+__device__ __forceinline__ uint32_t phase_tag(uint32_t s, int layers, int l, uint32_t p) {
+  return ((s * (uint32_t)(layers + 1) + (uint32_t)l) << 3) + p + 1u;
+}
 
 // ---------------------------------------------------------------------------------------------
 // PTX helpers
@@ -124,9 +137,6 @@ __device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t a) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_n(uint32_t a, uint32_t n) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(n) : "memory");
@@ -148,11 +158,45 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                "l"(src), "r"(bytes), "r"(mbar)
                : "memory");
 }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a) { return __uint_as_float(lds32(a)); }
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void ld_tag2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tag(const unsigned long long* p) {
+  unsigned long long a;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+__device__ __forceinline__ void st_tag(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ uint32_t tag_of(unsigned long long w) { return (uint32_t)(w >> 32); }
+
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(32 * kPConsumerWarps) : "memory");
 }
@@ -166,8 +210,7 @@ __device__ __forceinline__ void fail(const PArgs& A, uint32_t where) {
 }
 
 // Bounded wait for a global counter.  Returns false (and flags the launch) on timeout.
-__device__ bool wait_counter(const PArgs& A, int c, uint32_t target, uint32_t where) {
-  const uint32_t* p = A.ctr + c;
+__device__ bool wait_counter(const PArgs& A, const uint32_t* p, uint32_t target, uint32_t where) {
   if (reached(ld_acquire(p), target)) return true;
   const unsigned long long t0 = gtimer();
   while (true) {
@@ -188,11 +231,57 @@ __device__ bool wait_mbar(const PArgs& A, uint32_t bar, uint32_t parity, uint32_
   }
 }
 
-// Release of one unit of work: every lane fences its own stores, then lane 0 adds.
-__device__ __forceinline__ void warp_signal(uint32_t* ctr) {
-  __threadfence();
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) atomicAdd(ctr, 1u);
+// Waits until ring slot `slot` has been issued record q (bounded).
+__device__ __forceinline__ void wait_slot(const PArgs& A, volatile int* slot_rec, uint32_t slot, uint32_t q,
+                                          uint32_t where) {
+  if (slot_rec[slot] == (int)q) return;
+  const unsigned long long t0 = gtimer();
+  while (slot_rec[slot] != (int)q) {
+    if (failed(A)) return;
+    if (gtimer() - t0 > kWaitNs) { fail(A, where); return; }
+    __nanosleep(20);
+  }
+}
+
+// Loads N2 pairs of tagged words starting at p until every tag equals `tag` (bounded).
+template <int N2>
+__device__ __forceinline__ void ld_tagged(const PArgs& A, const unsigned long long* p, uint32_t tag, float* out,
+                                          uint32_t where) {
+  unsigned long long w[2 * N2];
+#pragma unroll
+  for (int i = 0; i < N2; ++i) ld_tag2(p + 2 * i, w[2 * i], w[2 * i + 1]);
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 2 * N2; ++i) ok &= tag_of(w[i]) == tag;
+  if (!ok) {
+    const unsigned long long t0 = gtimer();
+    while (true) {
+#pragma unroll
+      for (int i = 0; i < N2; ++i) ld_tag2(p + 2 * i, w[2 * i], w[2 * i + 1]);
+      ok = true;
+#pragma unroll
+      for (int i = 0; i < 2 * N2; ++i) ok &= tag_of(w[i]) == tag;
+      if (ok || failed(A)) break;
+      if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+      __nanosleep(20);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2 * N2; ++i) out[i] = tag_val(w[i]);
+}
+
+__device__ __forceinline__ float ld_tagged1(const PArgs& A, const unsigned long long* p, uint32_t tag, uint32_t where) {
+  unsigned long long w = ld_tag(p);
+  if (tag_of(w) != tag) {
+    const unsigned long long t0 = gtimer();
+    while (true) {
+      w = ld_tag(p);
+      if (tag_of(w) == tag || failed(A)) break;
+      if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+      __nanosleep(20);
+    }
+  }
+  return tag_val(w);
 }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
@@ -202,77 +291,71 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Staging: the consumer group (256 threads) turns an input vector into MX = 1 digit fragments
+// Staging: the CTA turns an input vector of K elements into MX = 1 digit fragments
 //   bfrag[(b*4 + i)*16 + p*4 + t] = (b0, b1) for digit plane p, MMA i, quad lane t of block b,
-// plus block sums and scales.  Thread `tid` owns 8-element groups q = tid + 256*r; group q
-// covers elements 8q..8q+7 = block q/16, (t, i) = ((q%16)/4, (q%16)%4).
+// plus block sums and scales.  8-element group q covers elements 8q..8q+7 = block q/16,
+// (t, i) = ((q%16)/4, (q%16)%4); thread `tid` owns groups q = tid + 512*r (q < K/8).
 // ---------------------------------------------------------------------------------------------
 struct Stage {
   uint2* bfrag;
   float* bsum;
   float* escl;
-  float* red;  // 16 floats
+  float* red;  // 32 floats
 };
 
-template <int G>  // groups of 8 per thread: 1 for K = 2048, 4 for K = 8192
-__device__ __forceinline__ void stage_groups(float (&v)[G][8], int K, const Stage& S) {
-  const int tid = threadIdx.x - 32;
+// Digits of one group.  The MMA's A operand is the raw nibble byte r = q_even + 16 q_odd for the
+// low K-half of each fragment word and the high nibble q_odd for the high K-half, so the B
+// operand carries y = x_even for the first and z = x_odd - 16 x_even for the second:
+//   r * y + q_odd * z = q_even x_even + q_odd x_odd.
+__device__ __forceinline__ void stage_group(const float (&x)[8], int q, const Stage& S) {
+  const int b = q >> 4, ti = q & 15, t = ti >> 2, i = ti & 3;
+  float v[8];
+  float s = 0.0f, a = 0.0f;
 #pragma unroll
-  for (int r = 0; r < G; ++r) {
-    const int q = tid + 256 * r;
-    const int b = q >> 4, ti = q & 15, t = ti >> 2, i = ti & 3;
-    float s = 0.0f, a = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      s += v[r][e];
-      a = fmaxf(a, fabsf(v[r][e]));
-    }
-    // the 16 threads of a block are a half warp
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) {
-      s += __shfl_xor_sync(0xffffffffu, s, o);
-      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    }
-    // a < 2^ex with ex from the exponent field (denormals bounded by 2^-126)
-    const int ex = max((int)((__float_as_uint(a) >> 23) & 0xFFu), 1) - 126;
-    const int e = min(29 - ex, 126);
-    const float up = __uint_as_float((uint32_t)(e + 127) << 23);  // 2^e, exact scaling
-    if (ti == 0) {
-      S.bsum[b] = s;
-      S.escl[b] = a > 0.0f ? __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
-    }
-    uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      int X = __float2int_rn(v[r][k] * up);
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int d = ((X + 128) & 255) - 128;
-        X = (X - d) >> 8;
-        w[p][k & 1] |= (uint32_t)(d & 255) << (8 * (k >> 1));
-      }
-    }
-#pragma unroll
-    for (int p = 0; p < 4; ++p) S.bfrag[(b * 4 + i) * 16 + p * 4 + t] = make_uint2(w[p][0], w[p][1]);
+  for (int e = 0; e < 8; e += 2) {
+    s += x[e] + x[e + 1];
+    v[e] = x[e];
+    v[e + 1] = fmaf(-16.0f, x[e], x[e + 1]);
+    a = fmaxf(a, fmaxf(fabsf(v[e]), fabsf(v[e + 1])));
   }
-  (void)K;
+  // the 16 threads of a block are a half warp
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  }
+  // a < 2^ex with ex from the exponent field (denormals bounded by 2^-126)
+  const int ex = max((int)((__float_as_uint(a) >> 23) & 0xFFu), 1) - 126;
+  const int e = min(29 - ex, 126);
+  const float up = __uint_as_float((uint32_t)(e + 127) << 23);  // 2^e, exact scaling
+  if (ti == 0) {
+    S.bsum[b] = s;
+    S.escl[b] = a > 0.0f ? __uint_as_float((uint32_t)(127 - e) << 23) : 0.0f;
+  }
+  uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    int X = __float2int_rn(v[k] * up);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const int d = ((X + 128) & 255) - 128;
+      X = (X - d) >> 8;
+      w[p][k & 1] |= (uint32_t)(d & 255) << (8 * (k >> 1));
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < 4; ++p) S.bfrag[(b * 4 + i) * 16 + p * 4 + t] = make_uint2(w[p][0], w[p][1]);
 }
 
-// rms-norm staging of a 2048-wide activation (one group per thread): out = x * g * inv.
-// `x` was produced inside this launch, so it is read through L2 (ld.cg).  Writes the normalised
-// values to `keep` (if non-null; used by nothing else than callers that need them).
-__device__ __forceinline__ void stage_norm2048(const float* x, const float* gamma, const Stage& S) {
-  const int tid = threadIdx.x - 32;
-  float v[1][8];
-  const float4 a = __ldcg(reinterpret_cast<const float4*>(x) + 2 * tid);
-  const float4 b = __ldcg(reinterpret_cast<const float4*>(x) + 2 * tid + 1);
-  const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * tid);
-  const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * tid + 1);
-  float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-  float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+// rms-norm staging of a 2048-wide tagged activation: out = x * g * inv (rms_norm, :87-115).
+// Threads 0..255 own one group each.
+__device__ __forceinline__ void stage_norm2048_vals(const float (&xv)[8], const float4 (&gm)[2], const Stage& S) {
+  const int tid = threadIdx.x;
   float ss = 0.0f;
+  if (tid < 256) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) ss = fmaf(xv[k], xv[k], ss);
+    for (int k = 0; k < 8; ++k) ss = fmaf(xv[k], xv[k], ss);
+  }
   ss = warp_sum(ss);
   if ((tid & 31) == 0) S.red[tid >> 5] = ss;
   consumer_sync();
@@ -280,146 +363,201 @@ __device__ __forceinline__ void stage_norm2048(const float* x, const float* gamm
 #pragma unroll
   for (int w = 0; w < kPConsumerWarps; ++w) tot += S.red[w];
   const float inv = 1.0f / sqrtf(tot / 2048.0f + 1e-5f);
+  if (tid < 256) {
+    const float gv[8] = {gm[0].x, gm[0].y, gm[0].z, gm[0].w, gm[1].x, gm[1].y, gm[1].z, gm[1].w};
+    float v[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) v[0][k] = __fmul_rn(__fmul_rn(xv[k], gv[k]), inv);
-  stage_groups<1>(v, 2048, S);
+    for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fmul_rn(xv[k], gv[k]), inv);
+    stage_group(v, tid, S);
+  }
   consumer_sync();
 }
 
-// plain staging of a 2048-wide (G=1) or 8192-wide (G=4) activation
-template <int G>
-__device__ __forceinline__ void stage_plain(const float* x, const Stage& S) {
-  const int tid = threadIdx.x - 32;
-  float v[G][8];
-#pragma unroll
-  for (int r = 0; r < G; ++r) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(x) + 2 * (tid + 256 * r));
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(x) + 2 * (tid + 256 * r) + 1);
-    v[r][0] = a.x; v[r][1] = a.y; v[r][2] = a.z; v[r][3] = a.w;
-    v[r][4] = b.x; v[r][5] = b.y; v[r][6] = b.z; v[r][7] = b.w;
-  }
-  stage_groups<G>(v, 256 * G * 8, S);
+__device__ __forceinline__ void load_gamma(const float* gamma, float4 (&gm)[2]) {
+  const int i = threadIdx.x & 255;  // threads >= 256 load a duplicate they never use
+  gm[0] = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * i);
+  gm[1] = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * i + 1);
+}
+
+__device__ __forceinline__ void stage_norm2048(const PArgs& A, const unsigned long long* x, uint32_t tag,
+                                               const float* gamma, const Stage& S, uint32_t where) {
+  float4 gm[2];
+  load_gamma(gamma, gm);  // independent of the dependency: issued first
+  float xv[8];
+  if (threadIdx.x < 256) ld_tagged<4>(A, x + 8 * threadIdx.x, tag, xv, where);
+  stage_norm2048_vals(xv, gm, S);
+}
+
+// plain staging of a tagged activation of K = 2048, 4096 or 8192 elements
+__device__ __forceinline__ void stage_plain(const PArgs& A, const unsigned long long* x, int K, uint32_t tag,
+                                            const Stage& S, uint32_t where) {
+  const int tid = threadIdx.x;
+  const int ngroups = K / 8;
+  float v0[8], v1[8];
+  if (tid < ngroups) ld_tagged<4>(A, x + 8 * tid, tag, v0, where);
+  if (tid + 512 < ngroups) ld_tagged<4>(A, x + 8 * (tid + 512), tag, v1, where);
+  if (tid < ngroups) stage_group(v0, tid, S);
+  if (tid + 512 < ngroups) stage_group(v1, tid + 512, S);
   consumer_sync();
 }
 
 // ---------------------------------------------------------------------------------------------
-// One record (16 rows x 16 blocks) on the MMA path, split over the consumer warps: warp cw
-// reduces blocks 2*cw and 2*cw+1 (of kq*16 .. kq*16+15 of the staged input).  The four MMAs of a
-// block use independent accumulators (their int32 sums are exact), so they issue back to back.
+// Blocks [j0, j0 + NBLK) of one record on the MMA path (blocks kq*16 + j of the staged input).
+// MMAs i = 0,1 and 2,3 chain through two accumulators; their int32 sums are exact.  Every lane
+// folds its digit planes pairwise (planes 0+1 on lanes t = 0, 2; planes 2+3 on t = 1, 3), so
+// one shuffle per row brings the high planes to the owner lane t == 0.
 // Lanes with t == 0 return the partial sums of rows g (p0) and g+8 (p1).
 // ---------------------------------------------------------------------------------------------
-template <int NBLK>
-__device__ __forceinline__ void record_part(const uint8_t* rec, int kq, int j0, const Stage& S, float& p0, float& p1) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const uint4* nib = reinterpret_cast<const uint4*>(rec);
-  const uint32_t* sc = reinterpret_cast<const uint32_t*>(rec + kRecNibBytes);
-  p0 = 0.0f;
-  p1 = 0.0f;
-#pragma unroll 2
-  for (int jj = 0; jj < NBLK; ++jj) {
+template <int NB>  // NB <= 4 blocks: the three passes over one chunk
+__device__ __forceinline__ void record_chunk(uint32_t r_nib, uint32_t r_sc, uint32_t s_bf, uint32_t s_es,
+                                             uint32_t s_bs, int kq, int j0, float& a0, float& a1) {
+  const int lane = threadIdx.x & 31, t = lane & 3;
+  const bool bl = lane < 16;
+  // pass 1: the MMAs of the chunk's blocks (independent across blocks)
+  int xg[NB], xh[NB];
+#pragma unroll
+  for (int jj = 0; jj < NB; ++jj) {
     const int j = j0 + jj, b = kq * 16 + j;
-    const uint4 wa = nib[j * 64 + lane * 2];
-    const uint4 wb = nib[j * 64 + lane * 2 + 1];
-    int c[4][4];
+    const uint4 wa = lds128(r_nib + 1024u * j);
+    const uint4 wb = lds128(r_nib + 1024u * j + 512u);
+    const uint32_t bfa = s_bf + 512u * b;
+    uint2 b0 = lds64(bfa), b1 = lds64(bfa + 128u), b2 = lds64(bfa + 256u), b3 = lds64(bfa + 384u);
+    if (!bl) b0 = b1 = b2 = b3 = make_uint2(0u, 0u);
+    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+    // low K-half: raw bytes (q_even + 16 q_odd); high K-half: q_odd (see stage_group)
+    mma_u8s8(c0, wa.x, wb.x, (wa.x >> 4) & 0x0F0F0F0Fu, (wb.x >> 4) & 0x0F0F0F0Fu, b0.x, b0.y);
+    mma_u8s8(c1, wa.z, wb.z, (wa.z >> 4) & 0x0F0F0F0Fu, (wb.z >> 4) & 0x0F0F0F0Fu, b2.x, b2.y);
+    mma_u8s8(c0, wa.y, wb.y, (wa.y >> 4) & 0x0F0F0F0Fu, (wb.y >> 4) & 0x0F0F0F0Fu, b1.x, b1.y);
+    mma_u8s8(c1, wa.w, wb.w, (wa.w >> 4) & 0x0F0F0F0Fu, (wb.w >> 4) & 0x0F0F0F0Fu, b3.x, b3.y);
+    // planes (2t, 2t+1) of rows g (e = 0, 1) and g+8 (e = 2, 3); fold pairwise: X = P_even + 256 P_odd
+    // (|P| <= 4 MMAs * (16*255 + 16*15) * 128 < 2.3e6, so |X| < 6e8 fits int32)
+    xg[jj] = (c0[0] + c1[0]) + (c0[1] + c1[1]) * 256;
+    xh[jj] = (c0[2] + c1[2]) + (c0[3] + c1[3]) * 256;
+  }
+  // pass 2: bring the high planes (lanes t = 1, 3) to the owner lanes
+  int hg[NB], hh[NB];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      c[i][0] = c[i][1] = c[i][2] = c[i][3] = 0;
-      const uint32_t xa = i == 0 ? wa.x : i == 1 ? wa.y : i == 2 ? wa.z : wa.w;
-      const uint32_t xb = i == 0 ? wb.x : i == 1 ? wb.y : i == 2 ? wb.z : wb.w;
-      const uint2 bb = lane < 16 ? S.bfrag[(b * 4 + i) * 16 + lane] : make_uint2(0u, 0u);
-      mma_u8s8(c[i], xa & 0x0F0F0F0Fu, xb & 0x0F0F0F0Fu, (xa >> 4) & 0x0F0F0F0Fu, (xb >> 4) & 0x0F0F0F0Fu, bb.x, bb.y);
-    }
-    int cs[4];
+  for (int jj = 0; jj < NB; ++jj) {
+    hg[jj] = __shfl_xor_sync(0xffffffffu, xg[jj], 1);
+    hh[jj] = __shfl_xor_sync(0xffffffffu, xh[jj], 1);
+  }
+  // pass 3: per-block scaling on the owner lanes
+  if (t == 0) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) cs[e] = (c[0][e] + c[1][e]) + (c[2][e] + c[3][e]);
-    const int p2 = __shfl_xor_sync(0xffffffffu, cs[0], 1);
-    const int p3 = __shfl_xor_sync(0xffffffffu, cs[1], 1);
-    const int q2 = __shfl_xor_sync(0xffffffffu, cs[2], 1);
-    const int q3 = __shfl_xor_sync(0xffffffffu, cs[3], 1);
-    if (t == 0) {
-      const uint32_t s0 = sc[j * 16 + g], s1 = sc[j * 16 + g + 8];
-      const float es = S.escl[b], xsb = S.bsum[b];
-      float v0 = (float)p3;
-      v0 = fmaf(v0, 256.0f, (float)p2);
-      v0 = fmaf(v0, 256.0f, (float)cs[1]);
-      v0 = fmaf(v0, 256.0f, (float)cs[0]);
-      float v1 = (float)q3;
-      v1 = fmaf(v1, 256.0f, (float)q2);
-      v1 = fmaf(v1, 256.0f, (float)cs[3]);
-      v1 = fmaf(v1, 256.0f, (float)cs[2]);
-      p0 += fmaf(bf16_bits_to_f32(s0 & 0xFFFFu) * es, v0, bf16_bits_to_f32(s0 >> 16) * xsb);
-      p1 += fmaf(bf16_bits_to_f32(s1 & 0xFFFFu) * es, v1, bf16_bits_to_f32(s1 >> 16) * xsb);
+    for (int jj = 0; jj < NB; ++jj) {
+      const int j = j0 + jj, b = kq * 16 + j;
+      const uint32_t s0 = lds32(r_sc + 64u * j), s1 = lds32(r_sc + 64u * j + 32u);
+      const float es = ldsf(s_es + 4u * b), xsb = ldsf(s_bs + 4u * b);
+      const float v0 = fmaf((float)hg[jj], 65536.0f, (float)xg[jj]);
+      const float v1 = fmaf((float)hh[jj], 65536.0f, (float)xh[jj]);
+      a0 += fmaf(__uint_as_float(s0 << 16) * es, v0, __uint_as_float(s0 & 0xFFFF0000u) * xsb);
+      a1 += fmaf(__uint_as_float(s1 << 16) * es, v1, __uint_as_float(s1 & 0xFFFF0000u) * xsb);
     }
   }
+}
+
+// Blocks [j0, j0 + NBLK) of one record; lanes with t == 0 return rows g (p0) and g+8 (p1).
+template <int NBLK>
+__device__ __forceinline__ void record_part(const uint8_t* rec, int kq, int j0, const Stage& S, float& p0, float& p1) {
+  const int lane = threadIdx.x & 31, g = lane >> 2;
+  // explicit shared-space addressing: ring record, digit fragments, block scales
+  const uint32_t r_nib = smem_u32(rec) + 16u * lane;
+  const uint32_t r_sc = smem_u32(rec) + kRecNibBytes + 4u * g;
+  const uint32_t s_bf = smem_u32(S.bfrag) + 8u * (lane & 15);
+  const uint32_t s_es = smem_u32(S.escl), s_bs = smem_u32(S.bsum);
+  float a0 = 0.f, a1 = 0.f;
+  constexpr int NB = NBLK < 4 ? NBLK : 4;
+#pragma unroll
+  for (int c = 0; c < NBLK; c += NB) record_chunk<NB>(r_nib, r_sc, s_bf, s_es, s_bs, kq, j0 + c, a0, a1);
+  p0 = a0;
+  p1 = a1;
 }
 
 __device__ __forceinline__ void record_blocks(int F, const uint8_t* rec, int kq, int mi, const Stage& S, float& p0,
                                               float& p1) {
   switch (F) {
-    case 1: record_part<16>(rec, kq, 0, S, p0, p1); break;
     case 2: record_part<8>(rec, kq, 8 * mi, S, p0, p1); break;
     case 4: record_part<4>(rec, kq, 4 * mi, S, p0, p1); break;
-    default: record_part<2>(rec, kq, 2 * mi, S, p0, p1); break;
+    case 8: record_part<2>(rec, kq, 2 * mi, S, p0, p1); break;
+    default: record_part<1>(rec, kq, mi, S, p0, p1); break;
   }
 }
 
 // ---------------------------------------------------------------------------------------------
-// Attention of one head on the consumer group (src/llama_engine.cpp:953-1021).
+// Attention of one head on the CTA (src/llama_engine.cpp:953-1021): RoPE from the table, KV
+// append at pos (by the first q head of each kv group), softmax over 0..pos, PV.
 // ---------------------------------------------------------------------------------------------
-__device__ void attention_head(const PArgs& A, int l, int h, int pos, float* scores, float* sm) {
-  const int tid = threadIdx.x - 32;
+__device__ void attention_head(const PArgs& A, int l, int h, int pos, uint32_t s, float* scores, float* sm) {
+  const int tid = threadIdx.x;
+  constexpr int NT = kPThreads;
   const int group = A.heads / A.kv_heads, kvh = h / group;
   const int kv_dim = A.kv_heads * LE_HEAD_DIM, q_dim = A.heads * LE_HEAD_DIM;
   float* sq = sm;            // 64
   float* sk = sm + 64;       // 64
   float* sv = sm + 128;      // 64
-  float* red = sm + 192;     // 16
-  float* pv = sm + 256;      // 16 x 64 partial outputs (1024 floats)
+  float* red = sm + 192;     // 32
+  float* pv = sm + 256;      // 32 x 64 partial outputs
   float* kc = A.kcache + (size_t)l * A.max_seq * kv_dim + kvh * LE_HEAD_DIM;
   float* vc = A.vcache + (size_t)l * A.max_seq * kv_dim + kvh * LE_HEAD_DIM;
+  const uint32_t tq = phase_tag(s, A.layers, l, TG_QKV);
+
+  // The K and V rows of positions < pos do not depend on this step: pull this head's rows into
+  // L2 before its q/k/v are ready (bulk prefetches, 256 bytes per row).
+  for (int t = tid; t < pos; t += NT) {
+    prefetch_l2(kc + (size_t)t * kv_dim, 256);
+    prefetch_l2(vc + (size_t)t * kv_dim, 256);
+  }
+  // a thread pair owns one position: thread 2t+hf holds dims 32*hf .. 32*hf+31 of K row t
+  const int hf = tid & 1, tp = tid >> 1;
   if (tid < 32) {
-    const float c = A.rope_cos[pos * 32 + tid], s = A.rope_sin[pos * 32 + tid];
-    const float r0 = __ldcg(A.qkv + h * LE_HEAD_DIM + tid), r1 = __ldcg(A.qkv + h * LE_HEAD_DIM + tid + 32);
-    sq[tid] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, s));
-    sq[tid + 32] = __fadd_rn(__fmul_rn(r0, s), __fmul_rn(r1, c));
+    const float c = A.rope_cos[pos * 32 + tid], sn = A.rope_sin[pos * 32 + tid];
+    const float r0 = ld_tagged1(A, A.qkv + h * LE_HEAD_DIM + tid, tq, 100 + l);
+    const float r1 = ld_tagged1(A, A.qkv + h * LE_HEAD_DIM + tid + 32, tq, 100 + l);
+    sq[tid] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, sn));
+    sq[tid + 32] = __fadd_rn(__fmul_rn(r0, sn), __fmul_rn(r1, c));
   } else if (tid < 64) {
     const int i = tid - 32;
-    const float c = A.rope_cos[pos * 32 + i], s = A.rope_sin[pos * 32 + i];
-    const float* kh = A.qkv + q_dim + kvh * LE_HEAD_DIM;
-    const float r0 = __ldcg(kh + i), r1 = __ldcg(kh + i + 32);
-    sk[i] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, s));
-    sk[i + 32] = __fadd_rn(__fmul_rn(r0, s), __fmul_rn(r1, c));
+    const float c = A.rope_cos[pos * 32 + i], sn = A.rope_sin[pos * 32 + i];
+    const unsigned long long* kh = A.qkv + q_dim + kvh * LE_HEAD_DIM;
+    const float r0 = ld_tagged1(A, kh + i, tq, 100 + l), r1 = ld_tagged1(A, kh + i + 32, tq, 100 + l);
+    sk[i] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, sn));
+    sk[i + 32] = __fadd_rn(__fmul_rn(r0, sn), __fmul_rn(r1, c));
   } else if (tid < 128) {
-    sv[tid - 64] = __ldcg(A.qkv + q_dim + kv_dim + kvh * LE_HEAD_DIM + tid - 64);
+    sv[tid - 64] = ld_tagged1(A, A.qkv + q_dim + kv_dim + kvh * LE_HEAD_DIM + tid - 64, tq, 100 + l);
   }
   consumer_sync();
   if (h % group == 0 && tid < 64) {
     kc[(size_t)pos * kv_dim + tid] = sk[tid];
     vc[(size_t)pos * kv_dim + tid] = sv[tid];
   }
-  // scores: one position per thread, the 16 row loads issued together
+  // scores: one position per thread pair
   float mx = -INFINITY;
-  for (int t = tid; t <= pos; t += 256) {
+  for (int t0 = 0; t0 <= pos; t0 += NT / 2) {
+    const int t = t0 + tp;
     float dot = 0.0f;
-    if (t == pos) {
+    if (t < pos) {
+      float4 k0[8];
+      const float4* kt = reinterpret_cast<const float4*>(kc + (size_t)t * kv_dim) + 8 * hf;
 #pragma unroll
-      for (int d = 0; d < 64; ++d) dot = fmaf(sq[d], sk[d], dot);
-    } else {
-      const float4* kt = reinterpret_cast<const float4*>(kc + (size_t)t * kv_dim);
-      float4 k4[16];
+      for (int d4 = 0; d4 < 8; ++d4) k0[d4] = __ldcg(kt + d4);
+      const float* qh = sq + 32 * hf;
 #pragma unroll
-      for (int d4 = 0; d4 < 16; ++d4) k4[d4] = __ldcg(kt + d4);
-#pragma unroll
-      for (int d4 = 0; d4 < 16; ++d4) {
-        dot = fmaf(sq[4 * d4], k4[d4].x, dot);
-        dot = fmaf(sq[4 * d4 + 1], k4[d4].y, dot);
-        dot = fmaf(sq[4 * d4 + 2], k4[d4].z, dot);
-        dot = fmaf(sq[4 * d4 + 3], k4[d4].w, dot);
+      for (int d4 = 0; d4 < 8; ++d4) {
+        dot = fmaf(qh[4 * d4], k0[d4].x, dot);
+        dot = fmaf(qh[4 * d4 + 1], k0[d4].y, dot);
+        dot = fmaf(qh[4 * d4 + 2], k0[d4].z, dot);
+        dot = fmaf(qh[4 * d4 + 3], k0[d4].w, dot);
       }
+    } else if (t == pos) {
+#pragma unroll
+      for (int d = 0; d < 32; ++d) dot = fmaf(sq[32 * hf + d], sk[32 * hf + d], dot);
     }
-    const float s = dot * 0.125f;
-    scores[t] = s;
-    mx = fmaxf(mx, s);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    if (t <= pos) {
+      const float sc = dot * 0.125f;
+      if (hf == 0) scores[t] = sc;
+      mx = fmaxf(mx, sc);
+    }
   }
   mx = warp_max(mx);
   if ((tid & 31) == 0) red[tid >> 5] = mx;
@@ -428,38 +566,38 @@ __device__ void attention_head(const PArgs& A, int l, int h, int pos, float* sco
 #pragma unroll
   for (int w = 1; w < kPConsumerWarps; ++w) mx = fmaxf(mx, red[w]);
   float se = 0.0f;
-  for (int t = tid; t <= pos; t += 256) {
+  for (int t = tid; t <= pos; t += NT) {
     const float e = expf(scores[t] - mx);
     scores[t] = e;
     se += e;
   }
   se = warp_sum(se);
-  consumer_sync();  // everyone has read red[0..7] and written scores[]
-  if ((tid & 31) == 0) red[8 + (tid >> 5)] = se;
+  consumer_sync();  // everyone has read red[0..15] and written scores[]
+  if ((tid & 31) == 0) red[16 + (tid >> 5)] = se;
   consumer_sync();
   float tot = 0.0f;
 #pragma unroll
-  for (int w = 0; w < kPConsumerWarps; ++w) tot += red[8 + w];
+  for (int w = 0; w < kPConsumerWarps; ++w) tot += red[16 + w];
   const float inv = 1.0f / tot;
-  // PV: thread = (4 dims d4, position group tg of 16); loads unrolled by 4
+  // PV: thread = (4 dims d4, position group tg of 32); loads unrolled by 4
   const int d4 = tid & 15, tg = tid >> 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   const float4 svn = reinterpret_cast<const float4*>(sv)[d4];
   int t = tg;
-  for (; t + 48 < pos; t += 64) {  // rows < pos only: row pos may still be in flight
+  for (; t + 96 < pos; t += 128) {  // rows < pos only: row pos may still be in flight
     float4 v[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(vc + (size_t)(t + 16 * u) * kv_dim) + d4);
+    for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(vc + (size_t)(t + 32 * u) * kv_dim) + d4);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const float p = scores[t + 16 * u] * inv;
+      const float p = scores[t + 32 * u] * inv;
       acc.x = fmaf(p, v[u].x, acc.x);
       acc.y = fmaf(p, v[u].y, acc.y);
       acc.z = fmaf(p, v[u].z, acc.z);
       acc.w = fmaf(p, v[u].w, acc.w);
     }
   }
-  for (; t <= pos; t += 16) {
+  for (; t <= pos; t += 32) {
     const float4 v = t == pos ? svn : __ldcg(reinterpret_cast<const float4*>(vc + (size_t)t * kv_dim) + d4);
     const float p = scores[t] * inv;
     acc.x = fmaf(p, v.x, acc.x);
@@ -472,25 +610,24 @@ __device__ void attention_head(const PArgs& A, int l, int h, int pos, float* sco
   if (tid < 64) {
     float o = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) o += pv[k * 64 + tid];
-    A.attn[h * LE_HEAD_DIM + tid] = o;
-    __threadfence();
+    for (int k = 0; k < 32; ++k) o += pv[k * 64 + tid];
+    st_tag(A.attn + h * LE_HEAD_DIM + tid, o, phase_tag(s, A.layers, l, TG_ATTN));
+    __threadfence();  // orders this thread's KV-cache stores before its later releases
   }
   consumer_sync();
-  if (tid == 0) atomicAdd(A.ctr + ctr_attn(l), 1u);
 }
 
 // Embedding row `token` of the tied lm_head, read from its records, as 8 values per thread
 // (elements 8*tid .. 8*tid+7 of the 2048-wide row; dequantize_embedding_row, :182-220).
 __device__ __forceinline__ void embed_group(const PArgs& A, int token, float (&v)[8]) {
-  const int tid = threadIdx.x - 32;
+  const int tid = threadIdx.x & 255;
   const int T = token >> 4, gr = token & 15;
   const uint8_t* rec = A.arena + A.lm_rec_base + (unsigned long long)T * kRecBytes;
   const int b = tid >> 4, q = tid & 15, t = q >> 2, i = q & 3;
   const int L = (gr & 7) * 4 + t, half = gr >> 3;
-  const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(rec + b * 1024 + L * 32 + half * 16 + 4 * i));
-  const uint32_t s = __ldg(reinterpret_cast<const uint32_t*>(rec + kRecNibBytes + b * 64 + gr * 4));
-  const float st = bf16_bits_to_f32(s & 0xFFFFu), mv = bf16_bits_to_f32(s >> 16);
+  const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(rec + b * 1024 + half * 512 + L * 16 + 4 * i));
+  const uint32_t sw = __ldg(reinterpret_cast<const uint32_t*>(rec + kRecNibBytes + b * 64 + gr * 4));
+  const float st = bf16_bits_to_f32(sw & 0xFFFFu), mv = bf16_bits_to_f32(sw >> 16);
 #pragma unroll
   for (int k = 0; k < 8; ++k) v[k] = __fadd_rn(mv, __fmul_rn((float)((w >> (4 * k)) & 0xFu), st));
 }
@@ -498,10 +635,11 @@ __device__ __forceinline__ void embed_group(const PArgs& A, int token, float (&v
 // ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void trace_mark(const PArgs& A, int& n, int tok, uint32_t tag) {
+__device__ __forceinline__ void trace_mark(const PArgs& A, int& n, int tok, uint32_t tag,
+                                           unsigned long long value = 0ull) {
   if (A.trace != nullptr && tok == 0 && n < kTraceCap) {
     unsigned long long* tr = A.trace + ((size_t)blockIdx.x * kTraceCap + n) * 2;
-    tr[0] = gtimer();
+    tr[0] = value ? value : gtimer();
     tr[1] = tag;
     ++n;
   }
@@ -512,280 +650,235 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   uint8_t* ring = psmem;                                          // kRingSlots * kRecBytes
   uint8_t* image = ring + (size_t)kRingSlots * kRecBytes;          // kImageBytes
   float* misc = reinterpret_cast<float*>(image + kImageBytes);     // kMiscFloats
-  unsigned long long* bars = reinterpret_cast<unsigned long long*>(misc + kMiscFloats);  // 2*kRingSlots
+  unsigned long long* bars = reinterpret_cast<unsigned long long*>(misc + kMiscFloats);  // kRingSlots
+  uint32_t* s_recs = reinterpret_cast<uint32_t*>(bars + kRingSlots);                     // kMaxRecs
+  PItem* s_items = reinterpret_cast<PItem*>(s_recs + kMaxRecs);                          // kMaxItems
+  PSeg* s_segs = reinterpret_cast<PSeg*>(s_items + kMaxItems);                           // kMaxSegs
   __shared__ float s_part[2][kPConsumerWarps][16];
   __shared__ unsigned long long s_best[kPConsumerWarps];
   __shared__ int s_token;
+  // record index currently issued into each ring slot.  A consumer of record q first waits until
+  // its slot holds q: only then does the slot's mbarrier parity refer unambiguously to q (a
+  // consumer that ran two uses ahead would otherwise see an older phase of the same parity).
+  __shared__ volatile int s_slot_rec[kRingSlots];
 
   const PCtaSched cs = A.sched[blockIdx.x];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kRingSlots);
+  const int tid = threadIdx.x;
+  const uint32_t full0 = smem_u32(bars);
   const uint32_t step_seq = A.ctrl->step_seq, lm_seq = A.ctrl->lm_seq;
+  const uint32_t per_tok = A.do_logits ? cs.nrec : cs.nrec_nolm;
+  const uint32_t total = per_tok * (uint32_t)A.n_tokens;
 
-  if (threadIdx.x == 0) {
+  // record q of this launch -> (slot q % kRingSlots, its use count q / kRingSlots)
+  auto issue = [&](uint32_t q) {
+    const uint32_t slot = q % kRingSlots;
+    const unsigned long long off = (unsigned long long)s_recs[q % per_tok] * kRecBytes;
+    s_slot_rec[slot] = (int)q;
+    mbar_expect_tx(full0 + 8 * slot, kRecBytes);
+    bulk_g2s(smem_u32(ring + (size_t)slot * kRecBytes), A.arena + off, kRecBytes, full0 + 8 * slot);
+  };
+
+  for (uint32_t i = tid; i < cs.nrec; i += kPThreads) s_recs[i] = A.recs[cs.rec_off + i];
+  for (uint32_t i = tid; i < cs.nitem; i += kPThreads) s_items[i] = A.items[cs.item_off + i];
+  for (uint32_t i = tid; i < cs.nseg; i += kPThreads) s_segs[i] = A.segs[cs.seg_off + i];
+  if (tid == 0) {
     for (int s = 0; s < kRingSlots; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, kPConsumerWarps);  // arrivals are weighted: 8 per consumed record
+      s_slot_rec[s] = -1;
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  if (tid == 0)
+    for (uint32_t q = 0; q < total && q < (uint32_t)kRingSlots; ++q) issue(q);
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      const uint32_t per_tok = A.do_logits ? cs.nrec : cs.nrec_nolm;
-      const uint32_t total = per_tok * (uint32_t)A.n_tokens;
-      uint32_t issued = 0;
-      for (uint32_t q = 0; q < total; ++q) {
-        const uint32_t slot = q % kRingSlots, use = q / kRingSlots;
-        if (use > 0 && !wait_mbar(A, empty0 + 8 * slot, (use - 1) & 1, 1)) break;
-        const uint32_t r = q % per_tok;
-        const unsigned long long off = A.recs[cs.rec_off + r];
-        mbar_expect_tx(full0 + 8 * slot, kRecBytes);
-        bulk_g2s(smem_u32(ring + (size_t)slot * kRecBytes), A.arena + off, kRecBytes, full0 + 8 * slot);
-        issued = q + 1;
+  const int cw = warp;
+  Stage S;
+  S.bfrag = reinterpret_cast<uint2*>(image);
+  S.bsum = reinterpret_cast<float*>(image + 32768);
+  S.escl = S.bsum + 64;
+  S.red = S.escl + 64;
+  float* scores = reinterpret_cast<float*>(image);  // attention reuses the image buffer
+  int token = A.prm->token;
+  const int pos0 = A.prm->pos;
+  const int L = A.layers;
+  int ntr = 0;
+  int buf = 0;
+
+  for (int tok = 0; tok < A.n_tokens; ++tok) {
+    const uint32_t s = step_seq + (uint32_t)tok;
+    const int pos = pos0 + tok;
+    const uint32_t rec_base = per_tok * (uint32_t)tok;
+    if (tid == 0) trace_mark(A, ntr, tok, 0xFFFF0000u);
+    if (tok > 0) {
+      // next token = greedy id of the previous step (all CTAs' lm_head work done)
+      if (tid == 0) {
+        wait_counter(A, &A.ctrl->lm_ctr, (lm_seq + (uint32_t)tok) * (uint32_t)A.n_lm_ctas, 3);
+        const unsigned long long k = atomicAdd(&A.ctrl->key[(lm_seq + tok - 1) % 3], 0ull);
+        s_token = k == 0ull ? 0 : (int)(~(uint32_t)(k & 0xFFFFFFFFull));
       }
-      // drain: never leave bulk copies in flight into a CTA that is about to exit
-      for (uint32_t q = (issued > kRingSlots ? issued - kRingSlots : 0); q < issued; ++q)
-        wait_mbar(A, full0 + 8 * (q % kRingSlots), (q / kRingSlots) & 1, 2);
+      consumer_sync();
+      token = s_token;
     }
-  } else {
-    // ---------------- consumers ----------------
-    const int cw = warp - 1;  // consumer warp index
-    const int tid = threadIdx.x - 32;
-    Stage S;
-    S.bfrag = reinterpret_cast<uint2*>(image);
-    S.bsum = reinterpret_cast<float*>(image + 32768);
-    S.escl = S.bsum + 64;
-    S.red = S.escl + 64;
-    float* scores = reinterpret_cast<float*>(image);  // attention reuses the image buffer
-    const uint32_t per_tok = A.do_logits ? cs.nrec : cs.nrec_nolm;
-    int token = A.prm->token;
-    const int pos0 = A.prm->pos;
-    int ntr = 0;
-    int buf = 0;
-
-    for (int tok = 0; tok < A.n_tokens; ++tok) {
-      const uint32_t s = step_seq + (uint32_t)tok;
-      const int pos = pos0 + tok;
-      const uint32_t rec_base = per_tok * (uint32_t)tok;
-      if (tid == 0) trace_mark(A, ntr, tok, 0xFFFF0000u);
-      if (tok > 0) {
-        // next token = greedy id of the previous step (all CTAs' lm_head work done)
-        if (tid == 0) {
-          wait_counter(A, ctr_lm(A.layers), (lm_seq + (uint32_t)tok) * (uint32_t)A.n_lm_ctas, 3);
-          const unsigned long long k = atomicAdd(&A.ctrl->key[(lm_seq + tok - 1) % 3], 0ull);
-          s_token = k == 0ull ? 0 : (int)(~(uint32_t)(k & 0xFFFFFFFFull));
-        }
-        consumer_sync();
-        token = s_token;
+    // threads 0..255 dequantise the embedding row (layer-0 input); CTA 0 also publishes it as x
+    float emb[8];
+    embed_group(A, token, emb);
+    if (blockIdx.x == 0 && tid < 256) {
+      const uint32_t tx = phase_tag(s, L, 0, TG_XIN);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) st_tag(A.x + 8 * tid + k, emb[k], tx);
+      if (tid == 0) {
+        A.ctrl->key[(lm_seq + tok + 1) % 3] = 0ull;
+        if (tok > 0) A.token_log[tok - 1] = token;
       }
-      // CTA 0: embedding into x, token log, reset of the next greedy key
-      float emb[8];
-      embed_group(A, token, emb);
-      if (blockIdx.x == 0) {
-        float4* xo = reinterpret_cast<float4*>(A.x) + 2 * tid;
-        xo[0] = make_float4(emb[0], emb[1], emb[2], emb[3]);
-        xo[1] = make_float4(emb[4], emb[5], emb[6], emb[7]);
-        if (tid == 0) {
-          A.ctrl->key[(lm_seq + tok + 1) % 3] = 0ull;
-          if (tok > 0) A.token_log[tok - 1] = token;
-        }
-        __threadfence();
-        consumer_sync();
-        if (tid == 0) atomicAdd(A.ctr + ctr_emb(A.layers), 1u);
-      }
+    }
 
-      for (uint32_t si = 0; si < cs.nseg; ++si) {
-        const PSeg sg = A.segs[cs.seg_off + si];
-        const int l = sg.layer;
-        if (sg.kind == PK_LMHEAD && !A.do_logits) continue;
-        const uint32_t tag = ((uint32_t)sg.kind << 8) | (uint32_t)l;
-        if (tid == 0) trace_mark(A, ntr, tok, tag | 0x10000u);
-        // ---- dependency + staging ----
-        switch (sg.kind) {
-          case PK_QKV: {
-            if (l == 0) {
-              // the input is the embedding computed above (no wait)
-              const float* gm = A.norms[0];
-              float ss = 0.0f;
-#pragma unroll
-              for (int k = 0; k < 8; ++k) ss = fmaf(emb[k], emb[k], ss);
-              ss = warp_sum(ss);
-              if (lane == 0) S.red[cw] = ss;
-              consumer_sync();
-              if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-              float tot = 0.0f;
-#pragma unroll
-              for (int w = 0; w < kPConsumerWarps; ++w) tot += S.red[w];
-              const float inv = 1.0f / sqrtf(tot / 2048.0f + 1e-5f);
-              const float4 ga = __ldg(reinterpret_cast<const float4*>(gm) + 2 * tid);
-              const float4 gb = __ldg(reinterpret_cast<const float4*>(gm) + 2 * tid + 1);
-              const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-              float v[1][8];
-#pragma unroll
-              for (int k = 0; k < 8; ++k) v[0][k] = __fmul_rn(__fmul_rn(emb[k], gv[k]), inv);
-              stage_groups<1>(v, 2048, S);
-              consumer_sync();
-            } else {
-              if (tid == 0) wait_counter(A, ctr_x(l), (s + 1) * (uint32_t)A.n_down_items, 10 + l);
-              consumer_sync();
-              if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-              stage_norm2048(A.x, A.norms[2 * l], S);
-            }
-            break;
+    for (uint32_t si = 0; si < cs.nseg; ++si) {
+      const PSeg sg = s_segs[si];
+      const int l = sg.layer;
+      if (sg.kind == PK_LMHEAD && !A.do_logits) continue;
+      const uint32_t tag = ((uint32_t)sg.kind << 8) | (uint32_t)l;
+      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x10000u);
+      consumer_sync();  // previous segment's readers of the image are done
+      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
+      // ---- staging (the tagged loads are the dependency waits) ----
+      switch (sg.kind) {
+        case PK_QKV:
+          if (l == 0) {
+            float4 gm[2];
+            load_gamma(A.norms, gm);
+            stage_norm2048_vals(emb, gm, S);
           }
-          case PK_ATTN:
-            if (tid == 0) wait_counter(A, ctr_qkv(l), (s + 1) * (uint32_t)A.n_qkv_items, 100 + l);
-            consumer_sync();
-            if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-            break;
-          case PK_O:
-            if (tid == 0) {
-              wait_counter(A, ctr_attn(l), (s + 1) * (uint32_t)A.heads, 200 + l);
-              if (l == 0) wait_counter(A, ctr_emb(A.layers), s + 1, 290);
-            }
-            consumer_sync();
-            if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-            stage_plain<1>(A.attn, S);
-            break;
-          case PK_GATEUP:
-            if (tid == 0) wait_counter(A, ctr_o(l), (s + 1) * (uint32_t)A.n_o_items, 300 + l);
-            consumer_sync();
-            if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-            stage_norm2048(A.x, A.norms[2 * l + 1], S);
-            break;
-          case PK_DOWN:
-            if (tid == 0) wait_counter(A, ctr_act(l), (s + 1) * (uint32_t)A.n_gu_items, 400 + l);
-            consumer_sync();
-            if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-            if (A.ffn == 8192) stage_plain<4>(A.act, S);
-            else if (A.ffn == 4096) stage_plain<2>(A.act, S);
-            else stage_plain<1>(A.act, S);
-            break;
-          case PK_LMHEAD:
-            if (tid == 0) wait_counter(A, ctr_x(A.layers), (s + 1) * (uint32_t)A.n_down_items, 500);
-            consumer_sync();
-            if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
-            stage_norm2048(A.x, A.norms[2 * A.layers], S);
-            break;
-        }
-        if (tid == 0) trace_mark(A, ntr, tok, tag | 0x30000u);
-        // ---- work ----
-        if (sg.kind == PK_ATTN) {
-          for (uint32_t it = sg.item_begin; it < sg.item_end; ++it) {
-            attention_head(A, l, (int)A.items[cs.item_off + it].tile, pos, scores, misc);
-            consumer_sync();
-          }
-          if (tid == 0) trace_mark(A, ntr, tok, tag | 0x40000u);
-          continue;
-        }
-        // Split factor F: groups of F warps share one item, each warp reducing 16/F blocks of every
-        // record of it; F = 1 (one warp per item) when the CTA has at least 8 items in the phase.
-        const int n_items = (int)(sg.item_end - sg.item_begin);
-        const int F = n_items >= 8 ? 1 : n_items >= 4 ? 2 : n_items >= 2 ? 4 : 8;
-        const int n_groups = kPConsumerWarps / F, gi = cw / F, mi = cw % F;
-        unsigned long long best = 0ull;
-        unsigned long long wait_cycles = 0;
-        for (int ii = gi; ii < n_items; ii += n_groups) {
-          const PItem item = A.items[cs.item_off + sg.item_begin + ii];
-          float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [record kind: gate/up][row g, g+8]
-          for (int rr = 0; rr < item.nrec; ++rr) {
-            const uint32_t q = rec_base + item.rec + rr;
-            const uint32_t slot = q % kRingSlots;
-            const long long w0 = clock64();
-            wait_mbar(A, full0 + 8 * slot, (q / kRingSlots) & 1, 600 + item.kind);
-            wait_cycles += (unsigned long long)(clock64() - w0);
-            float p0, p1;
-            record_blocks(F, ring + (size_t)slot * kRecBytes, item.kind == PK_DOWN ? rr : 0, mi, S, p0, p1);
-            __syncwarp();
-            if (lane == 0) mbar_arrive_n(empty0 + 8 * slot, (uint32_t)(kPConsumerWarps / F));
-            const int k = item.kind == PK_GATEUP ? rr : 0;
-            if (F == 1) {
-              acc[k][0] += p0;
-              acc[k][1] += p1;
-            } else {
-              if ((lane & 3) == 0) {
-                s_part[buf][cw][lane >> 2] = p0;
-                s_part[buf][cw][(lane >> 2) + 8] = p1;
-              }
-              group_sync(gi, 32 * F);
-              if (mi == 0 && (lane & 3) == 0) {
-                float v0 = 0.f, v1 = 0.f;
-                for (int w = 0; w < F; ++w) {
-                  v0 += s_part[buf][gi * F + w][lane >> 2];
-                  v1 += s_part[buf][gi * F + w][(lane >> 2) + 8];
-                }
-                acc[k][0] += v0;
-                acc[k][1] += v1;
-              }
-              buf ^= 1;
-            }
-          }
-          // epilogue: lanes t == 0 of the group's first warp own rows g and g+8
-          if (mi == 0 && (lane & 3) == 0) {
-            const int r0 = (int)item.tile * 16 + (lane >> 2), r1 = r0 + 8;
-            switch (item.kind) {
-              case PK_QKV:
-                A.qkv[r0] = acc[0][0];
-                A.qkv[r1] = acc[0][1];
-                break;
-              case PK_O:
-              case PK_DOWN:
-                A.x[r0] = __ldcg(A.x + r0) + acc[0][0];
-                A.x[r1] = __ldcg(A.x + r1) + acc[0][1];
-                break;
-              case PK_GATEUP:
-                A.act[r0] = (acc[0][0] / (1.0f + expf(-acc[0][0]))) * acc[1][0];
-                A.act[r1] = (acc[0][1] / (1.0f + expf(-acc[0][1]))) * acc[1][1];
-                break;
-              case PK_LMHEAD:
-                A.logits[r0] = acc[0][0];
-                A.logits[r1] = acc[0][1];
-                if (acc[0][0] > -1e30f) best = max(best, argmax_key(acc[0][0], r0));
-                if (acc[0][1] > -1e30f) best = max(best, argmax_key(acc[0][1], r1));
-                break;
-            }
-            __threadfence();
-          }
-          if (mi == 0) {
-            __syncwarp();
-            if (lane == 0 && item.kind != PK_LMHEAD) {
-              uint32_t* c = A.ctr + (item.kind == PK_QKV ? ctr_qkv(l)
-                                     : item.kind == PK_O  ? ctr_o(l)
-                                     : item.kind == PK_GATEUP ? ctr_act(l)
-                                                              : ctr_x(l + 1));
-              atomicAdd(c, 1u);
-            }
-          }
-        }
-        if (sg.kind == PK_LMHEAD) {
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-          if (lane == 0) s_best[cw] = best;
-          consumer_sync();
-          if (tid == 0) {
-            for (int w = 0; w < kPConsumerWarps; ++w) best = max(best, s_best[w]);
-            atomicMax(&A.ctrl->key[(lm_seq + tok) % 3], best);
-            __threadfence();
-            atomicAdd(A.ctr + ctr_lm(A.layers), 1u);
-          }
-        }
-        if (cw == 0 && lane == 0 && A.trace != nullptr && tok == 0 && ntr < kTraceCap) {
-          unsigned long long* tr = A.trace + ((size_t)blockIdx.x * kTraceCap + ntr) * 2;
-          tr[0] = wait_cycles;
-          tr[1] = tag | 0x50000u;
-          ++ntr;
-        }
+          else stage_norm2048(A, A.x, phase_tag(s, L, l, TG_XIN), A.norms + (size_t)(2 * l) * 2048, S, 10 + l);
+          break;
+        case PK_ATTN:
+          break;
+        case PK_O:
+          stage_plain(A, A.attn, A.dim, phase_tag(s, L, l, TG_ATTN), S, 200 + l);
+          break;
+        case PK_GATEUP:
+          stage_norm2048(A, A.x, phase_tag(s, L, l, TG_XO), A.norms + (size_t)(2 * l + 1) * 2048, S, 300 + l);
+          break;
+        case PK_DOWN:
+          stage_plain(A, A.act, A.ffn, phase_tag(s, L, l, TG_ACT), S, 400 + l);
+          break;
+        case PK_LMHEAD:
+          stage_norm2048(A, A.x, phase_tag(s, L, L, TG_XIN), A.norms + (size_t)(2 * L) * 2048, S, 500);
+          break;
+      }
+      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x30000u);
+      // ---- work ----
+      if (sg.kind == PK_ATTN) {
+        for (uint32_t it = sg.item_begin; it < sg.item_end; ++it)
+          attention_head(A, l, (int)s_items[it].tile, pos, s, scores, misc);
         if (tid == 0) trace_mark(A, ntr, tok, tag | 0x40000u);
+        continue;
       }
+      // Split factor F: groups of F warps share one item, each warp reducing 16/F blocks of every
+      // record of it.  Streaming phases keep pairs of warps per record.
+      const int n_items = (int)(sg.item_end - sg.item_begin);
+      const int F = n_items >= 8 ? 2 : n_items >= 4 ? 4 : n_items >= 2 ? 8 : 16;
+      const int n_groups = kPConsumerWarps / F, gi = cw / F, mi = cw % F;
+      // output tags of this phase
+      const uint32_t t_out = sg.kind == PK_QKV      ? phase_tag(s, L, l, TG_QKV)
+                             : sg.kind == PK_O      ? phase_tag(s, L, l, TG_XO)
+                             : sg.kind == PK_GATEUP ? phase_tag(s, L, l, TG_ACT)
+                                                    : phase_tag(s, L, l + 1, TG_XIN);
+      const uint32_t t_res = sg.kind == PK_O ? phase_tag(s, L, l, TG_XIN) : phase_tag(s, L, l, TG_XO);
+      unsigned long long best = 0ull;
+      unsigned long long wait_cycles = 0;
+      for (int ii = gi; ii < n_items; ii += n_groups) {
+        const PItem item = s_items[sg.item_begin + ii];
+        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [record kind: gate/up][row g, g+8]
+        // residual rows of o-proj / down: ready before this phase started; fetch them now
+        float res0 = 0.f, res1 = 0.f;
+        const bool owner = mi == 0 && (lane & 3) == 0;
+        if (owner && (item.kind == PK_O || item.kind == PK_DOWN)) {
+          const int r0 = (int)item.tile * 16 + (lane >> 2);
+          res0 = ld_tagged1(A, A.x + r0, t_res, 700 + l);
+          res1 = ld_tagged1(A, A.x + r0 + 8, t_res, 700 + l);
+        }
+        for (int rr = 0; rr < item.nrec; ++rr) {
+          const uint32_t q = rec_base + item.rec + rr;
+          const uint32_t slot = q % kRingSlots;
+          const long long w0 = clock64();
+          wait_slot(A, s_slot_rec, slot, q, 650 + item.kind);
+          wait_mbar(A, full0 + 8 * slot, (q / kRingSlots) & 1, 600 + item.kind);
+          wait_cycles += (unsigned long long)(clock64() - w0);
+          float p0, p1;
+          record_blocks(F, ring + (size_t)slot * kRecBytes, item.kind == PK_DOWN ? rr : 0, mi, S, p0, p1);
+          const int k = item.kind == PK_GATEUP ? rr : 0;
+          if ((lane & 3) == 0) {
+            s_part[buf][cw][lane >> 2] = p0;
+            s_part[buf][cw][(lane >> 2) + 8] = p1;
+          }
+          if (F == 1) __syncwarp(); else group_sync(gi, 32 * F);
+          // every warp of the group is done with the slot: refill it with the record ten ahead
+          if (mi == 0 && lane == 0 && q + kRingSlots < total) issue(q + kRingSlots);
+          if (owner) {
+            float v0 = 0.f, v1 = 0.f;
+            for (int w = 0; w < F; ++w) {
+              v0 += s_part[buf][gi * F + w][lane >> 2];
+              v1 += s_part[buf][gi * F + w][(lane >> 2) + 8];
+            }
+            acc[k][0] += v0;
+            acc[k][1] += v1;
+          }
+          buf ^= 1;
+        }
+        // epilogue: lanes t == 0 of the group's first warp own rows g and g+8
+        if (owner) {
+          const int r0 = (int)item.tile * 16 + (lane >> 2), r1 = r0 + 8;
+          switch (item.kind) {
+            case PK_QKV:
+              st_tag(A.qkv + r0, acc[0][0], t_out);
+              st_tag(A.qkv + r1, acc[0][1], t_out);
+              break;
+            case PK_O:
+            case PK_DOWN:
+              st_tag(A.x + r0, res0 + acc[0][0], t_out);
+              st_tag(A.x + r1, res1 + acc[0][1], t_out);
+              break;
+            case PK_GATEUP:
+              st_tag(A.act + r0, (acc[0][0] / (1.0f + expf(-acc[0][0]))) * acc[1][0], t_out);
+              st_tag(A.act + r1, (acc[0][1] / (1.0f + expf(-acc[0][1]))) * acc[1][1], t_out);
+              break;
+            case PK_LMHEAD:
+              A.logits[r0] = acc[0][0];
+              A.logits[r1] = acc[0][1];
+              if (acc[0][0] > -1e30f) best = max(best, argmax_key(acc[0][0], r0));
+              if (acc[0][1] > -1e30f) best = max(best, argmax_key(acc[0][1], r1));
+              break;
+          }
+        }
+      }
+      if (sg.kind == PK_LMHEAD) {
+        __threadfence();
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+        if (lane == 0) s_best[cw] = best;
+        consumer_sync();
+        if (tid == 0) {
+          for (int w = 0; w < kPConsumerWarps; ++w) best = max(best, s_best[w]);
+          atomicMax(&A.ctrl->key[(lm_seq + tok) % 3], best);
+          __threadfence();
+          atomicAdd(&A.ctrl->lm_ctr, 1u);
+        }
+      }
+      if (cw == 0 && lane == 0) trace_mark(A, ntr, tok, tag | 0x50000u, wait_cycles | 1ull);
+      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x40000u);
     }
   }
 
   // ---------------- launch epilogue ----------------
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
+    // every issued copy has been consumed, unless a wait gave up: make sure none is in flight
+    for (uint32_t sl = 0; sl < (uint32_t)kRingSlots && sl < total; ++sl) {
+      const uint32_t qlast = ((total - 1 - sl) / kRingSlots) * kRingSlots + sl;
+      wait_mbar(A, full0 + 8 * sl, (qlast / kRingSlots) & 1, 2);
+    }
     __threadfence();
     const uint32_t prev = atomicAdd(&A.ctrl->done_ctas, 1u);
     if (prev == gridDim.x - 1) {
@@ -805,10 +898,6 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   }
 }
 
-}  // namespace le
-
-namespace le {
-
 // Repack one LLM4S128 matrix (rows N % 16 == 0, K % 2048 == 0) into records
 // (T, kq) -> dst + (T * K/2048 + kq) * kRecBytes.  One thread per 16-byte piece.
 __global__ void k_repack(QMat W, uint8_t* __restrict__ dst) {
@@ -826,7 +915,7 @@ __global__ void k_repack(QMat W, uint8_t* __restrict__ dst) {
       const int L = g * 4 + t;
       uint8_t* rec = dst + ((size_t)T * KQ + kq) * kRecBytes;
       const uint4 v = *reinterpret_cast<const uint4*>(W.nib + (size_t)n * (W.K / 2) + (size_t)c * 16);
-      *reinterpret_cast<uint4*>(rec + j * 1024 + L * 32 + half * 16) = v;
+      *reinterpret_cast<uint4*>(rec + j * 1024 + half * 512 + L * 16) = v;
     } else {
       const long long q = p - pieces_nib;  // 4 consecutive (n, b) scale entries of one row
       const long long e0 = q * 4;

@@ -107,7 +107,7 @@ def _oracle_logits(oracle_lib, o, vocab):
 def test_small_model_golden(small_engine):
     g = np.load(GOLDEN / "small_greedy.npz")
     eng = small_engine
-    assert eng.decode_path == "persistent"
+    assert eng.decode_path == "persistent", eng.bindings.last_error(eng.handle)
     prompt = [int(t) for t in g["prompt"]]
     eng.reset()
     eng.prefill(prompt[:-1], 0, False)
