@@ -161,6 +161,19 @@ void* llama_engine_get_stream(llama_engine_t engine);
  * Activations are whatever the last step left; the numbers are timings only. */
 int llama_engine_profile_phase(llama_engine_t engine, const char* phase, int iters, float* avg_ms);
 
+/* Greedy argmax of n device-resident fp32 logits that allocates no memory: writes the first
+ * index among the maxima (values <= -1e30 and NaN never win; 0 when none qualifies, the
+ * reference's rule at src/llama_engine.cpp:785-792) to *out_index (device memory).  No
+ * counterpart in the reference ABI.  It is for callers that cannot allocate device memory while
+ * running (a fixed memory budget reserved at start-up, or a decode loop that cannot afford the
+ * device synchronisation a cudaMalloc may cause): its scratch is a fixed 8 KB device array inside
+ * this library, held by every GPU that loads the library until the process exits.  The first
+ * call on a device looks up that array's device address; make that first call before any stream
+ * capture.  All calls share the array, so calls that overlap on the GPU (different streams
+ * without ordering) race; calls on one stream are safe.  n <= 16,777,216.  Returns 0, -1 on bad
+ * arguments or a launch error, -2 when n exceeds the maximum. */
+int llama_b128_argmax_noalloc(const float* logits, int n, int32_t* out_index, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1103,3 +1103,50 @@ LE_API int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, co
   }
   return 0;
 }
+
+// ---------------------------------------------------------------------------------------------
+// Greedy argmax that allocates nothing
+//
+// For callers that must not allocate device memory once they are running: serving processes
+// that reserve their whole memory budget at start-up, and latency-critical decode loops, where a
+// cudaMalloc can synchronise the device and stall every stream.  The per-CTA candidates live in
+// a fixed file-scope device array instead of caller- or engine-allocated scratch.  Every GPU
+// that loads this library holds the array (8 KB) until the process exits.
+// ---------------------------------------------------------------------------------------------
+namespace {
+constexpr int kNoAllocParts = 1024;               // candidate slots in the static scratch array
+constexpr int kNoAllocPerThread = 64;             // at most this many logits per thread
+constexpr long long kNoAllocMaxN = (long long)kNoAllocParts * le::kThreads * kNoAllocPerThread;  // 16,777,216
+
+static __device__ __align__(256) le::ArgmaxPart g_argmax_scratch[kNoAllocParts];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_argmax_scratch, per device ordinal
+}  // namespace
+
+LE_API int llama_b128_argmax_noalloc(const float* logits, int n, int32_t* out_index, void* stream) {
+  if (!logits || !out_index || n < 1) return -1;
+  if ((long long)n > kNoAllocMaxN) return -2;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  void* scratch = nullptr;
+  {
+    // once per device, with that device current: the host-side symbol is only a stand-in, the
+    // kernels need the device address
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_argmax_scratch) != cudaSuccess || !p) return -1;
+      g_noalloc_addr[dev] = p;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  le::ArgmaxPart* part = static_cast<le::ArgmaxPart*>(scratch);
+  // every candidate slot the finish kernel reads is written by this call: nothing to clear
+  const long long per_part = (long long)le::kThreads * 4;
+  const int parts = (int)std::min<long long>(kNoAllocParts, ((long long)n + per_part - 1) / per_part);
+  le::k_argmax_rows<<<parts, le::kThreads, 0, s>>>(logits, n, part);
+  le::k_argmax_finish<<<1, 1024, 0, s>>>(part, parts, out_index, nullptr, nullptr, 0);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}

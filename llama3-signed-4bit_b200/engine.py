@@ -89,6 +89,8 @@ class LlamaEngineBindings:
         lib.llama_engine_get_logits_batch.restype = _FP
         lib.llama_b128_gemv.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P]
         lib.llama_b128_gemv.restype = ctypes.c_int
+        lib.llama_b128_argmax_noalloc.argtypes = [_P, ctypes.c_int, _P, _P]
+        lib.llama_b128_argmax_noalloc.restype = ctypes.c_int
 
     def last_error(self, handle=None) -> str:
         return self.lib.llama_engine_last_error(handle).decode(errors="replace")
