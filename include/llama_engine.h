@@ -136,11 +136,26 @@ const float* llama_engine_get_logits_batch(llama_engine_t engine, int row);
 int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
                     int N, int K, const float* x, int M, float* y, void* stream);
 
+/* Same product for 1 <= M <= 4096 rows on the tensor-core (tcgen05) kernel that the batched
+ * decode and prefill use: the weights become exact bf16 codes, x is split into bf16 hi + lo
+ * parts, fp32 accumulation per 128-block, scales applied in fp32.  K in {2048, 4096, 6144,
+ * 8192}.  Builds its working layout in temporary device buffers and returns after the result
+ * is complete (synchronises `stream`), so it is meant for tests and measurements.  Needs an
+ * sm_100 device.  Returns 0, or -1 on bad arguments / device error. */
+int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
+                    int N, int K, const float* x, int M, float* y, void* stream);
+
 /* Which implementation runs the slot-0 token steps: 1 = the persistent token-step kernel (one
  * cooperative launch per forward_token, or per whole generate_greedy call; used for dim 2048
  * and ffn_dim in {2048, 4096, 8192}), 0 = the per-phase kernel chain in a CUDA graph (any other
  * supported geometry, or LLAMA_B200_PERSISTENT=0 at create time).  -1 for a NULL handle. */
 int llama_engine_decode_path(llama_engine_t engine);
+
+/* Which implementation runs prefill (2 or more tokens) and llama_engine_forward_batch: 1 = the
+ * token-batched path with tensor-core (tcgen05) GEMMs (sm_100 devices, dim and ffn_dim
+ * multiples of 2048, 4 q heads per kv head; LLAMA_B200_BATCHED=0 at create time turns it off),
+ * 0 = token by token through the decode path.  -1 for a NULL handle. */
+int llama_engine_batch_path(llama_engine_t engine);
 
 /* Diagnostics for the persistent kernel: enable = 1 starts recording a phase trace of the first
  * token of each following launch (globaltimer timestamps per CTA at every phase's start, after

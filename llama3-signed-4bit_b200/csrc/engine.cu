@@ -20,9 +20,11 @@
 #include <string>
 #include <vector>
 
+#include "batch_kernels.cuh"
 #include "decode_kernels.cuh"
 #include "mma_gemv.cuh"
 #include "persistent.cuh"
+#include "tc_gemm.cuh"
 #include "llama_engine.h"
 
 #define LE_API extern "C" __attribute__((visibility("default")))
@@ -129,6 +131,16 @@ struct DevLayer {
 
 constexpr int kRing = 64;
 
+// Weight records of one tensor-core GEMM (row tiles x K blocks, tc_gemm.cuh layout).
+struct TcMat {
+  const uint8_t* recs = nullptr;
+  int tiles = 0, kb = 0;
+};
+struct TcLayer {
+  TcMat qkv, o, gu, d;
+};
+constexpr int kTcMaxSplits = 8;
+
 struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -189,6 +201,27 @@ struct Engine {
   unsigned long long* d_trace = nullptr;  // optional phase trace of the persistent kernel
   PArgs pargs{};
   int p_grid = 0;
+
+  // token-batched path: tensor-core GEMMs over tc_T tokens at most per step
+  bool tc = false;
+  int tc_T = 0;
+  uint8_t* tc_arena = nullptr;
+  std::vector<TcLayer> tcl;
+  TcMat tc_lm;
+  uint8_t* img_d = nullptr;  // activation images, K = dim   [tc_T/64][dim/128][kImgBytes]
+  uint8_t* img_f = nullptr;  //                      K = ffn
+  float* t_x = nullptr;      // [tc_T][dim] residual stream
+  float* t_q = nullptr;      // [tc_T][dim] rotated queries
+  float* t_attn = nullptr;   // [tc_T][dim]
+  float* t_act = nullptr;    // [tc_T][ffn]
+  float* t_part = nullptr;   // [kTcMaxSplits][tc_T][dim] split-K partial sums
+  int32_t* t_idx = nullptr;  // [3][tc_T] token | position | slot of the step's rows
+  int32_t* h_idx = nullptr;  // pinned staging of t_idx
+  cudaEvent_t idx_ev = nullptr;
+  bool idx_pending = false;
+  ArgmaxPart* t_am = nullptr;  // [tc_T][tc_am_parts]
+  int tc_am_parts = 0;
+  uint32_t* tc_err = nullptr;  // device error word of the tensor-core GEMM
 
   cudaGraphExec_t g_fwd[2] = {nullptr, nullptr};  // [compute_logits]
   cudaGraphExec_t g_gen = nullptr;                // forward + greedy + advance
@@ -482,9 +515,6 @@ static bool init_persistent(Engine* E) {
   LE_CK(cudaMemset(E->d_tagged, 0, n_tagged * sizeof(unsigned long long)));  // tag 0 is never valid
   LE_CK(cudaMalloc(&E->d_ctrl, sizeof(PCtrl)));
   LE_CK(cudaMemset(E->d_ctrl, 0, sizeof(PCtrl)));
-  LE_CK(cudaMallocHost(&E->h_err, 4 * sizeof(uint32_t)));
-  E->h_err[0] = E->h_err[1] = 0;
-
   PArgs& A = E->pargs;
   A.arena = E->rec_arena;
   A.sched = E->d_sched; A.segs = E->d_segs; A.items = E->d_items; A.recs = E->d_recs;
@@ -520,13 +550,239 @@ static bool launch_persistent(Engine* E, int n_tokens, bool logits) {
   return true;
 }
 
-// Reads the persistent kernel's error word (after the stream has been synchronised).
-static bool persistent_ok(Engine* E) {
-  if (!E->persist) return true;
-  LE_CK(cudaMemcpyAsync(E->h_err, &E->d_ctrl->error, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
+
+// ---------------------------------------------------------------------------------------------
+// Token-batched path: batched decode over sequence slots and chunked prefill, with every weight
+// GEMM on the tensor cores (tc_gemm.cuh).
+// ---------------------------------------------------------------------------------------------
+static bool tc_supported(const Engine* E) {
+  const char* v = getenv("LLAMA_B200_BATCHED");
+  if (v && std::strcmp(v, "0") == 0) return false;
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, E->device) != cudaSuccess || prop.major != 10) return false;
+  return E->dim % 2048 == 0 && E->ffn % 2048 == 0 && E->heads == 4 * E->kv_heads;
+}
+
+static bool init_tc(Engine* E) {
+  if (!tc_supported(E)) return true;
+  using namespace tc;
+  const int dim = (int)E->dim, ffn = (int)E->ffn, kvd = (int)E->kv_dim, L = (int)E->layers;
+  // rows per batched step: the sequence slots, and at least one prefill chunk
+  // ($LLAMA_B200_PREFILL_CHUNK tokens, default 1024)
+  int chunk = 1024;
+  if (const char* c = getenv("LLAMA_B200_PREFILL_CHUNK")) chunk = std::max(kTok, std::min(8192, atoi(c)));
+  chunk = (chunk + kTok - 1) / kTok * kTok;
+  E->tc_T = std::max(chunk, (E->max_batch + kTok - 1) / kTok * kTok);
+  const int T = E->tc_T;
+  // ---- weight records ----
+  const int kb_d = dim / 128, kb_f = ffn / 128;
+  const int t_qkv = (dim + 2 * kvd + kM - 1) / kM, t_o = dim / kM, t_gu = ffn / 64, t_d = dim / kM;
+  const int t_lm = ((int)E->vocab + kM - 1) / kM;
+  const size_t per_layer = (size_t)(t_qkv + t_o + t_gu) * kb_d + (size_t)t_d * kb_f;
+  const size_t total = (per_layer * L + (size_t)t_lm * kb_d) * tc::kRecBytes;
+  LE_CK(cudaMalloc(&E->tc_arena, total));
+  LE_CK(cudaMemsetAsync(E->tc_arena, 0, total, E->stream));
+  size_t off = 0;
+  auto take = [&](int tiles, int kb) {
+    TcMat m;
+    m.recs = E->tc_arena + off;
+    m.tiles = tiles;
+    m.kb = kb;
+    off += (size_t)tiles * kb * tc::kRecBytes;
+    return m;
+  };
+  auto repack = [&](const QMat& W, const TcMat& M, int row0, int G, int o) -> bool {
+    k_tc_repack<<<E->num_sms * 8, 256, 0, E->stream>>>(W, const_cast<uint8_t*>(M.recs), row0, G, o);
+    LE_CK(cudaGetLastError());
+    return true;
+  };
+  E->tcl.resize(L);
+  for (int l = 0; l < L; ++l) {
+    TcLayer& Y = E->tcl[l];
+    const DevLayer& D = E->L[l];
+    Y.qkv = take(t_qkv, kb_d);
+    Y.o = take(t_o, kb_d);
+    Y.gu = take(t_gu, kb_d);
+    Y.d = take(t_d, kb_f);
+    if (!repack(D.q, Y.qkv, 0, kM, 0) || !repack(D.k, Y.qkv, dim, kM, 0) || !repack(D.v, Y.qkv, dim + kvd, kM, 0))
+      return false;
+    if (!repack(D.o, Y.o, 0, kM, 0)) return false;
+    if (!repack(D.g, Y.gu, 0, 64, 0) || !repack(D.u, Y.gu, 0, 64, 64)) return false;
+    if (!repack(D.d, Y.d, 0, kM, 0)) return false;
+  }
+  E->tc_lm = take(t_lm, kb_d);
+  if (!repack(E->lm_head, E->tc_lm, 0, kM, 0)) return false;
+  // ---- activations ----
+  const size_t tiles_T = (size_t)T / kTok;
+  LE_CK(cudaMalloc(&E->img_d, tiles_T * kb_d * kImgBytes));
+  LE_CK(cudaMalloc(&E->img_f, tiles_T * kb_f * kImgBytes));
+  LE_CK(cudaMemsetAsync(E->img_d, 0, tiles_T * kb_d * kImgBytes, E->stream));
+  LE_CK(cudaMemsetAsync(E->img_f, 0, tiles_T * kb_f * kImgBytes, E->stream));
+  LE_CK(cudaMalloc(&E->t_x, (size_t)T * dim * 4));
+  LE_CK(cudaMalloc(&E->t_q, (size_t)T * dim * 4));
+  LE_CK(cudaMalloc(&E->t_attn, (size_t)T * dim * 4));
+  LE_CK(cudaMalloc(&E->t_act, (size_t)T * ffn * 4));
+  LE_CK(cudaMalloc(&E->t_part, (size_t)kTcMaxSplits * T * dim * 4));
+  LE_CK(cudaMalloc(&E->t_idx, (size_t)3 * T * 4));
+  LE_CK(cudaMallocHost(&E->h_idx, (size_t)3 * T * 4));
+  LE_CK(cudaEventCreateWithFlags(&E->idx_ev, cudaEventDisableTiming));
+  E->tc_am_parts = std::min<int>(64, ((int)E->vocab + 4 * 256 - 1) / (4 * 256));
+  LE_CK(cudaMalloc(&E->t_am, (size_t)T * E->tc_am_parts * sizeof(ArgmaxPart)));
+  LE_CK(cudaMalloc(&E->tc_err, 16));
+  LE_CK(cudaMemsetAsync(E->tc_err, 0, 16, E->stream));
+  LE_CK(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  int per_sm = 0;
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm, tc::kThreads, kSmemBytes));
+  if (per_sm < 1) {
+    E->err = "tensor-core GEMM declined: 0 resident CTAs per SM";
+    return true;
+  }
   LE_CK(cudaStreamSynchronize(E->stream));
-  if (E->h_err[0] != 0) {
+  E->tc = true;
+  return true;
+}
+
+// Number of K splits for a GEMM whose tiles x token tiles alone would leave SMs idle.
+static int tc_splits(const Engine* E, const TcMat& W, int tok_tiles) {
+  const int base = W.tiles * tok_tiles;
+  if (base >= E->num_sms) return 1;
+  int s = std::min(kTcMaxSplits, E->num_sms / base);
+  s = std::min(s, std::max(1, W.kb / 2));
+  return std::max(1, s);
+}
+
+// Launches one tensor-core GEMM over T token rows of `img`; returns the number of K splits used.
+static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int splits, tc::Args A) {
+  A.recs = W.recs;
+  A.img = img;
+  A.tiles = W.tiles;
+  A.kb_total = W.kb;
+  A.tok_tiles = (T + tc::kTok - 1) / tc::kTok;
+  A.T = T;
+  A.nt = T >= tc::kTok ? tc::kTok : (T + 15) / 16 * 16;
+  A.kb_split = (W.kb + splits - 1) / splits;
+  A.splits = (W.kb + A.kb_split - 1) / A.kb_split;
+  A.error = E->tc_err;
+  const int units = A.tiles * A.tok_tiles * A.splits;
+  tc::k_tc_gemm<<<std::min(units, E->num_sms), tc::kThreads, tc::kSmemBytes, E->stream>>>(A);
+  return A.splits;
+}
+
+// Copies (token, position, slot) of n rows to the device (one H2D copy from pinned memory).
+static bool tc_upload_rows(Engine* E, const int32_t* tok, const int32_t* pos, const int32_t* slot, int n) {
+  if (E->idx_pending) LE_CK(cudaEventSynchronize(E->idx_ev));
+  for (int i = 0; i < n; ++i) {
+    int32_t t = tok[i];
+    if (t < 0 || t >= (int32_t)E->vocab) t = 0;  // src/llama_engine.cpp:937
+    E->h_idx[i] = t;
+    E->h_idx[n + i] = pos[i];
+    E->h_idx[2 * n + i] = slot[i];
+  }
+  LE_CK(cudaMemcpyAsync(E->t_idx, E->h_idx, (size_t)3 * n * 4, cudaMemcpyHostToDevice, E->stream));
+  LE_CK(cudaEventRecord(E->idx_ev, E->stream));
+  E->idx_pending = true;
+  return true;
+}
+
+// One forward step of n rows (rows already uploaded).  Logits and greedy ids are produced for
+// rows [lrow0, lrow0 + nlog) into logits rows 0..nlog-1 and am_result[0..nlog-1].
+static bool tc_step(Engine* E, int n, int lrow0, int nlog) {
+  using namespace tc;
+  const int dim = (int)E->dim, ffn = (int)E->ffn, kvd = (int)E->kv_dim;
+  const size_t layer_stride = (size_t)E->max_seq * kvd;
+  const size_t slot_stride = (size_t)E->layers * layer_stride;
+  const size_t part_stride = (size_t)E->tc_T * dim;
+  const int32_t* tok = E->t_idx;
+  const int32_t* pos = E->t_idx + n;
+  const int32_t* slot = E->t_idx + 2 * n;
+  const int tok_tiles = (n + kTok - 1) / kTok;
+  cudaStream_t s = E->stream;
+  k_embed_batch<<<n, 256, 0, s>>>(E->lm_head, tok, E->t_x, dim);
+  int d_splits = 0;
+  for (uint32_t l = 0; l < E->layers; ++l) {
+    const TcLayer& Y = E->tcl[l];
+    const DevLayer& D = E->L[l];
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, dim, E->img_d);
+    Args A{};
+    A.mode = MODE_QKV;
+    A.out = E->t_q;
+    A.ldo = dim;
+    A.N = dim + 2 * kvd;
+    A.pos = pos;
+    A.slot = slot;
+    A.rope_cos = E->rope_cos;
+    A.rope_sin = E->rope_sin;
+    A.kc = E->kcache + l * layer_stride;
+    A.vc = E->vcache + l * layer_stride;
+    A.slot_stride = slot_stride;
+    A.q_rows = dim;
+    A.kv_dim = kvd;
+    tc_launch(E, Y.qkv, E->img_d, n, 1, A);
+    k_attn_batch<<<dim3(n, E->kv_heads), 128, 0, s>>>(E->t_q, dim, E->kcache + l * layer_stride,
+                                                       E->vcache + l * layer_stride, slot_stride, kvd, pos, slot,
+                                                       E->t_attn);
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, dim, E->img_d);
+    Args R{};
+    R.mode = MODE_ROWS;
+    R.out = E->t_part;
+    R.ldo = dim;
+    R.N = dim;
+    R.split_stride = part_stride;
+    const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), R);
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, so, part_stride, D.post_norm, dim, E->img_d);
+    Args G{};
+    G.mode = MODE_SWIGLU;
+    G.out = E->t_act;
+    G.ldo = ffn;
+    G.N = ffn;
+    tc_launch(E, Y.gu, E->img_d, n, 1, G);
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_act, ffn, nullptr, 0, 0, nullptr, ffn, E->img_f);
+    d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), R);
+  }
+  if (nlog > 0) {
+    k_tc_stage<<<nlog, 256, 0, s>>>(E->t_x + (size_t)lrow0 * dim, dim, E->t_part + (size_t)lrow0 * dim, d_splits,
+                                     part_stride, E->final_norm, dim, E->img_d);
+    Args R{};
+    R.mode = MODE_ROWS;
+    R.out = E->logits;
+    R.ldo = (int)E->vocab;
+    R.N = (int)E->vocab;
+    R.split_stride = 0;
+    tc_launch(E, E->tc_lm, E->img_d, nlog, 1, R);
+    k_argmax_rows_batch<<<dim3(E->tc_am_parts, nlog), 256, 0, s>>>(E->logits, (int)E->vocab, E->vocab, E->t_am);
+    k_argmax_finish_batch<<<nlog, 256, 0, s>>>(E->t_am, E->tc_am_parts, E->am_result);
+  }
+  LE_CK(cudaGetLastError());
+  return true;
+}
+
+// Chunked prefill of `count` tokens of slot 0 at positions start .. start+count-1.
+static bool tc_prefill(Engine* E, const int32_t* ids, size_t count, size_t start, bool last_logits) {
+  std::vector<int32_t> pos(E->tc_T), slot(E->tc_T, 0);
+  for (size_t c0 = 0; c0 < count; c0 += (size_t)E->tc_T) {
+    const int n = (int)std::min<size_t>((size_t)E->tc_T, count - c0);
+    for (int i = 0; i < n; ++i) pos[i] = (int32_t)(start + c0 + i);
+    if (!tc_upload_rows(E, ids + c0, pos.data(), slot.data(), n)) return false;
+    const bool lg = last_logits && c0 + n == count;
+    if (!tc_step(E, n, n - 1, lg ? 1 : 0)) return false;
+  }
+  return true;
+}
+
+// Reads the persistent kernel's error word (after the stream has been synchronised).
+// Also reads the tensor-core GEMM's error word.
+static bool persistent_ok(Engine* E) {
+  if (!E->persist && !E->tc) return true;
+  if (E->persist)
+    LE_CK(cudaMemcpyAsync(E->h_err, &E->d_ctrl->error, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
+  if (E->tc) LE_CK(cudaMemcpyAsync(E->h_err + 2, E->tc_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
+  LE_CK(cudaStreamSynchronize(E->stream));
+  if (E->persist && E->h_err[0] != 0) {
     E->err = "persistent decode kernel: a dependency wait timed out (code " + std::to_string(E->h_err[1]) + ")";
+    return false;
+  }
+  if (E->tc && E->h_err[2] != 0) {
+    E->err = "tensor-core GEMM: a pipeline wait timed out (code " + std::to_string(E->h_err[2]) + ")";
     return false;
   }
   return true;
@@ -629,6 +885,8 @@ static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   for (int i = 0; i < kRing; ++i) LE_CK(cudaEventCreateWithFlags(&E->ring_ev[i], cudaEventDisableTiming));
   LE_CK(cudaMallocHost(&E->h_logits, B * E->vocab * 4));
   LE_CK(cudaMallocHost(&E->h_small, (size_t)LE_MAX_SEQ_LEN * 4));
+  LE_CK(cudaMallocHost(&E->h_err, 4 * sizeof(uint32_t)));
+  for (int i = 0; i < 4; ++i) E->h_err[i] = 0;
   if (!set_smem_attrs(E)) return false;
 
   // ---- graphs ----
@@ -637,6 +895,7 @@ static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   if (!capture(E, row_buffers(E, 0, 0, true, 1), &E->g_gen)) return false;
   LE_CK(cudaStreamSynchronize(E->stream));
   if (!init_persistent(E)) return false;
+  if (!init_tc(E)) return false;
   return true;
 }
 
@@ -650,6 +909,11 @@ static void destroy(Engine* E) {
   void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged, E->d_ctrl};
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
+  void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_act, E->t_part, E->t_idx,
+                  E->t_am, E->tc_err};
+  for (void* p : tdev) if (p) cudaFree(p);
+  if (E->h_idx) cudaFreeHost(E->h_idx);
+  if (E->idx_ev) cudaEventDestroy(E->idx_ev);
   void* dev_ptrs[] = {E->arena, E->rope_cos, E->rope_sin, E->kcache, E->vcache, E->x, E->qkv, E->attn,
                       E->act, E->logits, E->emb, E->red, E->d_misc, E->part, E->am_result, E->token_log, E->d_params};
   for (void* p : dev_ptrs) if (p) cudaFree(p);
@@ -819,9 +1083,21 @@ LE_API int llama_engine_prefill(llama_engine_t engine, const int32_t* token_ids,
   if (!engine || !token_ids) return -1;
   Engine* E = H(engine);
   DeviceGuard dg(E->device);
-  for (size_t i = 0; i < count; ++i) {
-    const bool last = (i + 1 == count) && compute_last_logits != 0;
-    if (!forward_token(E, token_ids[i], start_pos + i, last)) return -1;
+  // positions at or past max_seq_len are silent no-ops (src/llama_engine.cpp:936)
+  if (start_pos >= (size_t)E->max_seq) return 0;
+  const size_t n = std::min(count, (size_t)E->max_seq - start_pos);
+  const bool last = compute_last_logits != 0 && n == count;
+  if (E->tc && n >= 2) {
+    if (!tc_prefill(E, token_ids, n, start_pos, last)) return -1;
+    if (last) {
+      E->logits_on_host_fresh = false;
+      E->argmax_valid = true;
+      E->have_logits = true;
+    }
+    return 0;
+  }
+  for (size_t i = 0; i < n; ++i) {
+    if (!forward_token(E, token_ids[i], start_pos + i, last && i + 1 == n)) return -1;
   }
   return 0;
 }
@@ -915,6 +1191,14 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
     if (positions[i] < 0 || positions[i] >= E->max_seq) { E->err = "forward_batch: position out of range"; return -1; }
   }
   DeviceGuard dg(E->device);
+  if (E->tc) {
+    if (!tc_upload_rows(E, tokens, positions, slots, n)) return -1;
+    if (!tc_step(E, n, 0, compute_logits ? n : 0)) return -1;
+    if (!persistent_ok(E)) return -1;
+    E->logits_on_host_fresh = false;
+    if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
+    return 0;
+  }
   std::vector<StepParams> hp(n);
   for (int i = 0; i < n; ++i) {
     int32_t t = tokens[i];
@@ -958,6 +1242,11 @@ LE_API int llama_engine_trace(llama_engine_t engine, int enable, unsigned long l
 LE_API int llama_engine_decode_path(llama_engine_t engine) {
   if (!engine) return -1;
   return H(engine)->persist ? 1 : 0;
+}
+
+LE_API int llama_engine_batch_path(llama_engine_t engine) {
+  if (!engine) return -1;
+  return H(engine)->tc ? 1 : 0;
 }
 
 LE_API void* llama_engine_get_stream(llama_engine_t engine) { return engine ? (void*)H(engine)->stream : nullptr; }
@@ -1102,6 +1391,68 @@ LE_API int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, co
     if (rc != 0) return -1;
   }
   return 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Isolated tensor-core GEMM (the batched path's kernel on a caller's matrix): builds the weight
+// records and the activation image in temporary device buffers, runs k_tc_gemm, waits for it and
+// frees the buffers.  For tests and measurements, not for a serving loop.
+// ---------------------------------------------------------------------------------------------
+LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16, int N, int K,
+                           const float* x, int M, float* y, void* stream) {
+  using namespace le::tc;
+  if (!nibbles || !step_bf16 || !min_bf16 || !x || !y) return -1;
+  if (N < 1 || K < 2048 || K % 2048 != 0 || K > 8192 || M < 1 || M > 4096) return -1;
+  if ((reinterpret_cast<uintptr_t>(nibbles) | reinterpret_cast<uintptr_t>(x)) & 15u) return -1;
+  int dev = 0, sms = 148;
+  cudaDeviceProp prop{};
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return -1;
+  if (prop.major != 10) return -1;
+  sms = prop.multiProcessorCount;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int kb = K / 128, tiles = (N + kM - 1) / kM, tok_tiles = (M + kTok - 1) / kTok;
+  uint8_t *recs = nullptr, *img = nullptr;
+  uint32_t* err = nullptr;
+  int rc = -1;
+  const size_t rec_bytes = (size_t)tiles * kb * tc::kRecBytes, img_bytes = (size_t)tok_tiles * kb * kImgBytes;
+  if (cudaMalloc(&recs, rec_bytes) == cudaSuccess && cudaMalloc(&img, img_bytes) == cudaSuccess &&
+      cudaMalloc(&err, 16) == cudaSuccess) {
+    static bool attr = false;
+    if (!attr) attr = cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) ==
+                      cudaSuccess;
+    cudaMemsetAsync(recs, 0, rec_bytes, s);
+    cudaMemsetAsync(img, 0, img_bytes, s);
+    cudaMemsetAsync(err, 0, 16, s);
+    QMat W{nibbles, step_bf16, min_bf16, N, K};
+    k_tc_repack<<<sms * 8, 256, 0, s>>>(W, recs, 0, kM, 0);
+    k_tc_stage<<<M, 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, K, img);
+    Args A{};
+    A.recs = recs;
+    A.img = img;
+    A.tiles = tiles;
+    A.kb_total = kb;
+    A.tok_tiles = tok_tiles;
+    A.splits = 1;
+    A.kb_split = kb;
+    A.T = M;
+    A.nt = M >= kTok ? kTok : (M + 15) / 16 * 16;
+    A.N = N;
+    A.mode = MODE_ROWS;
+    A.out = y;
+    A.ldo = N;
+    A.error = err;
+    k_tc_gemm<<<std::min(tiles * tok_tiles, sms), tc::kThreads, kSmemBytes, s>>>(A);
+    uint32_t herr = 1;
+    if (attr && cudaGetLastError() == cudaSuccess &&
+        cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+        cudaStreamSynchronize(s) == cudaSuccess && herr == 0)
+      rc = 0;
+  }
+  cudaStreamSynchronize(s);
+  if (recs) cudaFree(recs);
+  if (img) cudaFree(img);
+  if (err) cudaFree(err);
+  return rc;
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -71,6 +71,8 @@ class LlamaEngineBindings:
         lib.llama_engine_create_ex.restype = _P
         lib.llama_engine_decode_path.argtypes = [_P]
         lib.llama_engine_decode_path.restype = ctypes.c_int
+        lib.llama_engine_batch_path.argtypes = [_P]
+        lib.llama_engine_batch_path.restype = ctypes.c_int
         lib.llama_engine_trace.argtypes = [_P, ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
         lib.llama_engine_trace.restype = ctypes.c_int
         lib.llama_engine_get_stream.argtypes = [_P]
@@ -89,6 +91,8 @@ class LlamaEngineBindings:
         lib.llama_engine_get_logits_batch.restype = _FP
         lib.llama_b128_gemv.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P]
         lib.llama_b128_gemv.restype = ctypes.c_int
+        lib.llama_b128_gemm.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P]
+        lib.llama_b128_gemm.restype = ctypes.c_int
         lib.llama_b128_argmax_noalloc.argtypes = [_P, ctypes.c_int, _P, _P]
         lib.llama_b128_argmax_noalloc.restype = ctypes.c_int
 
@@ -225,6 +229,11 @@ class LlamaEngine:
     @property
     def decode_path(self) -> str:
         return {1: "persistent", 0: "kernel-chain"}.get(self.bindings.lib.llama_engine_decode_path(self.handle), "?")
+
+    @property
+    def batch_path(self) -> str:
+        """Implementation of prefill and forward_batch: "tensor-core" or "token-loop"."""
+        return {1: "tensor-core", 0: "token-loop"}.get(self.bindings.lib.llama_engine_batch_path(self.handle), "?")
 
     def close(self):
         if getattr(self, "handle", None):

@@ -1,0 +1,176 @@
+"""GPU parity of the token-batched path (tensor-core GEMMs): the isolated GEMM against the oracle
+GEMV, batched prefill and batched decode against the oracle engine.
+
+Tolerances:
+* GEMM: |y_gpu - y_ref| <= 3e-5 * sum_k |w_nk| |x_k| per output.  The activations enter the
+  tensor cores as bf16 hi + lo parts, so each x carries a relative error of at most 2^-17
+  (7.6e-6) before fp32 accumulation; the bound leaves room for the accumulation order.
+* Logits: max|l_gpu - l_ref| <= 1e-3 * max|l_ref| per step; greedy ids identical.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import fptr
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_RTOL = 1e-3
+GEMM_TOL = 3e-5
+
+
+def rel_max_err(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def torch_cuda(gpu_available):
+    import torch
+    return torch
+
+
+@pytest.fixture(scope="module")
+def bindings(pkg, gpu_available):
+    return pkg.LlamaEngineBindings()
+
+
+def _gemv_ref(oracle_lib, nib, step, mn, N, K, X):
+    out = []
+    for x in X:
+        xs = np.zeros(K // 128, np.float32)
+        oracle_lib.orc_block_sums(fptr(x), K, fptr(xs))
+        y = np.zeros(N, np.float32)
+        oracle_lib.orc_gemv(fptr(nib), fptr(step), fptr(mn), N, K, fptr(x), fptr(xs), fptr(y))
+        out.append(y)
+    return np.stack(out)
+
+
+def _abs_scale(pkg, step, mn, N, K, X):
+    st = pkg.model_file.bf16_to_f32(step).reshape(N, K // 128).astype(np.float64)
+    mv = pkg.model_file.bf16_to_f32(mn).reshape(N, K // 128).astype(np.float64)
+    bound = np.abs(mv) + 15.0 * st
+    ax = np.abs(X.astype(np.float64)).reshape(len(X), K // 128, 128).sum(axis=2)
+    return ax @ bound.T  # [M, N]
+
+
+@pytest.mark.parametrize("K,N,M", [(2048, 2048, 1), (2048, 2048, 64), (2048, 320, 17), (8192, 2048, 64),
+                                   (2048, 512, 100), (8192, 384, 130), (2048, 128256, 64)])
+def test_tc_gemm_vs_oracle(pkg, bindings, oracle_lib, torch_cuda, K, N, M):
+    torch = torch_cuda
+    nib, step, mn = pkg.model_file.gen_matrix(N, K, seed=300 + K + N, tensor=3, uniform_codes=True)
+    X = np.random.default_rng(K + 3 * N + M).standard_normal((M, K)).astype(np.float32)
+    d_nib = torch.from_numpy(nib).cuda()
+    d_step = torch.from_numpy(step.view(np.int16)).cuda()
+    d_min = torch.from_numpy(mn.view(np.int16)).cuda()
+    d_x = torch.from_numpy(X).cuda()
+    d_y = torch.full((M, N), float("nan"), device="cuda")
+    rc = bindings.lib.llama_b128_gemm(d_nib.data_ptr(), d_step.data_ptr(), d_min.data_ptr(), N, K,
+                                      d_x.data_ptr(), M, d_y.data_ptr(), None)
+    assert rc == 0
+    y = d_y.cpu().numpy()
+    rows = np.arange(M) if M <= 8 else np.unique(np.r_[0, 1, M // 2, M - 2, M - 1])
+    ref = _gemv_ref(oracle_lib, nib, step, mn, N, K, X[rows])
+    scale = _abs_scale(pkg, step, mn, N, K, X[rows])
+    err = np.abs(y[rows].astype(np.float64) - ref)
+    assert np.isfinite(y).all()
+    assert (err <= GEMM_TOL * scale).all(), f"max err/scale {float((err / scale).max()):.3e}"
+
+
+def test_tc_gemm_rejects_bad_args(bindings, torch_cuda):
+    lib = bindings.lib
+    assert lib.llama_b128_gemm(None, None, None, 8, 2048, None, 1, None, None) == -1
+    buf = torch_cuda.zeros(1 << 20, dtype=torch_cuda.uint8, device="cuda")
+    p = buf.data_ptr()
+    assert lib.llama_b128_gemm(p, p, p, 8, 1024, p, 1, p, None) == -1    # K not a multiple of 2048
+    assert lib.llama_b128_gemm(p, p, p, 8, 2048, p, 0, p, None) == -1    # M < 1
+    assert lib.llama_b128_gemm(p, p, p, 8, 2048, p, 4097, p, None) == -1  # M > 4096
+    assert lib.llama_b128_gemm(p + 4, p, p, 8, 2048, p, 1, p, None) == -1  # misaligned nibbles
+
+
+def _oracle_logits(oracle_lib, o, vocab):
+    return np.ctypeslib.as_array(oracle_lib.orc_get_logits(o), shape=(vocab,)).copy()
+
+
+def test_batched_prefill_vs_oracle(pkg, bindings, small_model, oracle_lib, monkeypatch):
+    """150 prompt tokens in chunks of 64 (two full chunks and a ragged one), then greedy decode
+    on the KV cache the batched path wrote."""
+    monkeypatch.setenv("LLAMA_B200_PREFILL_CHUNK", "64")
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    o = oracle_lib.orc_create(str(small_model).encode())
+    try:
+        assert eng.batch_path == "tensor-core"
+        vocab = eng.vocab_size
+        ids = np.random.default_rng(31).integers(0, vocab, 150).astype(np.int32)
+        eng.prefill([int(t) for t in ids], 0, True)
+        oracle_lib.orc_prefill(o, fptr(ids), len(ids), 0, 1)
+        assert rel_max_err(eng.get_logits(), _oracle_logits(oracle_lib, o, vocab)) <= LOGIT_RTOL
+        tok = eng.sample(0.0, 0.9)
+        assert tok == oracle_lib.orc_sample_engine(o, ctypes.c_float(0.0), ctypes.c_float(0.9))
+        for pos in range(150, 156):
+            eng.forward_token(tok, pos, True)
+            oracle_lib.orc_forward_token(o, tok, pos, 1)
+            assert rel_max_err(eng.get_logits(), _oracle_logits(oracle_lib, o, vocab)) <= LOGIT_RTOL
+            tok = eng.sample(0.0, 0.9)
+            assert tok == oracle_lib.orc_sample_engine(o, ctypes.c_float(0.0), ctypes.c_float(0.9))
+    finally:
+        oracle_lib.orc_free(o)
+        eng.close()
+
+
+def test_prefill_without_logits_then_decode(pkg, bindings, small_model, oracle_lib):
+    """compute_last_logits = 0, then a single forward_token reads the batched KV."""
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    o = oracle_lib.orc_create(str(small_model).encode())
+    try:
+        vocab = eng.vocab_size
+        ids = np.random.default_rng(5).integers(0, vocab, 40).astype(np.int32)
+        eng.prefill([int(t) for t in ids[:-1]], 0, False)
+        oracle_lib.orc_prefill(o, fptr(ids), len(ids) - 1, 0, 0)
+        eng.forward_token(int(ids[-1]), len(ids) - 1, True)
+        oracle_lib.orc_forward_token(o, int(ids[-1]), len(ids) - 1, 1)
+        assert rel_max_err(eng.get_logits(), _oracle_logits(oracle_lib, o, vocab)) <= LOGIT_RTOL
+    finally:
+        oracle_lib.orc_free(o)
+        eng.close()
+
+
+def test_batched_decode_40_rows(pkg, bindings, small_model, oracle_lib):
+    """40 sequences with different prompt lengths decoded together (MMA N = 48 token columns);
+    four of them replayed on the oracle."""
+    n = 40
+    eng = pkg.LlamaEngine(str(small_model), bindings, device=0, max_batch=n, max_seq_len=256)
+    check = [0, 13, 27, 39]
+    orcs = {i: oracle_lib.orc_create(str(small_model).encode()) for i in check}
+    try:
+        assert eng.batch_path == "tensor-core"
+        vocab = eng.vocab_size
+        rng = np.random.default_rng(77)
+        lens = [int(x) for x in rng.integers(3, 30, n)]
+        prompts = [rng.integers(0, vocab, L).astype(np.int32) for L in lens]
+        slots = list(range(n))
+        # all but the last prompt token: batched steps over the slots still in their prompt
+        maxlen = max(lens)
+        for t in range(maxlen - 1):
+            rows = [i for i in range(n) if t < lens[i] - 1]
+            eng.forward_batch([int(prompts[i][t]) for i in rows], [t] * len(rows), rows, False)
+        for i in check:
+            oracle_lib.orc_prefill(orcs[i], fptr(prompts[i]), lens[i] - 1, 0, 0)
+        toks = [int(prompts[i][-1]) for i in range(n)]
+        pos = [lens[i] - 1 for i in range(n)]
+        for step in range(4):
+            eng.forward_batch(toks, pos, slots, True)
+            am = eng.argmax_batch(n)
+            for i in check:
+                oracle_lib.orc_forward_token(orcs[i], toks[i], pos[i], 1)
+                ref = _oracle_logits(oracle_lib, orcs[i], vocab)
+                assert rel_max_err(eng.get_logits_batch(i), ref) <= LOGIT_RTOL, (step, i)
+                assert am[i] == int(np.argmax(ref)), (step, i)
+            toks = am
+            pos = [p + 1 for p in pos]
+    finally:
+        for o in orcs.values():
+            oracle_lib.orc_free(o)
+        eng.close()
