@@ -114,8 +114,12 @@ int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_token, siz
                                  int32_t n_steps, int32_t* out_tokens);
 
 /* Batched decode: one step for n independent sequences.  Row i feeds tokens[i] at positions[i]
- * into sequence slot slots[i] (slots distinct, < max_batch; positions < max_seq_len).  Host
- * arrays.  compute_logits != 0 also runs the lm_head for every row.  Returns 0 or -1. */
+ * into sequence slot slots[i] (slots < max_batch; positions < max_seq_len).  Host arrays.
+ * Rows of one slot must come in increasing position order; each row attends to its slot's
+ * cache up to its own position, including rows of the same call.  n <= max_batch, or, on the
+ * tensor-core batched path (llama_engine_batch_path() == 1) and without logits, up to
+ * max(max_batch, prefill chunk) rows, e.g. several prompt positions of many slots at once.
+ * compute_logits != 0 also runs the lm_head for every row.  Returns 0 or -1. */
 int llama_engine_forward_batch(llama_engine_t engine, const int32_t* tokens, const int32_t* positions,
                                const int32_t* slots, int n, int compute_logits);
 

@@ -31,13 +31,14 @@ __global__ void k_embed_batch(QMat E, const int32_t* __restrict__ tok, float* __
 // (src/llama_engine.cpp:958-1021: kv_h = h / 4, s = (q . k) * 0.125, softmax over 0..pos,
 // o = sum p v).  The token's own k / v are already in the cache (written by the QKV epilogue).
 // One CTA of 4 warps per (t, g); warp w takes 32-position tiles w, w+4, ...: lane = position
-// for the scores (its k row read whole), then lane = dimension pair for p . v (v rows read
-// coalesced).  Softmax runs online per warp (running max and sum, rescaled per tile); the four
-// warps' partial results are merged at the end.
-__global__ void __launch_bounds__(128) k_attn_batch(const float* __restrict__ q, int q_dim, const float* __restrict__ kc,
-                                                    const float* __restrict__ vc, size_t slot_stride, int kv_dim,
-                                                    const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
-                                                    float* __restrict__ out) {
+// for the scores (its k row read whole), lane = dimension pair for p . v (v rows read
+// coalesced); both loads of a tile are issued before either is used.  Softmax runs online per
+// warp (running max and sum, rescaled per tile); the four warps' partial results are merged at
+// the end.
+__global__ void __launch_bounds__(128, 3)
+    k_attn_batch(const float* __restrict__ q, int q_dim, const float* __restrict__ kc, const float* __restrict__ vc,
+                 size_t slot_stride, int kv_dim, const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
+                 float* __restrict__ out) {
   __shared__ float4 sq4[64];      // (q_h0[d], q_h1[d], q_h2[d], q_h3[d])
   __shared__ float4 sp[4][32];    // per warp: softmax numerators of the tile, 4 heads per position
   __shared__ float s_m[4][4], s_l[4][4];
@@ -58,14 +59,24 @@ __global__ void __launch_bounds__(128) k_attn_batch(const float* __restrict__ q,
   for (int h = 0; h < 4; ++h) { m[h] = -INFINITY; l[h] = 0.0f; o[h][0] = 0.0f; o[h][1] = 0.0f; }
   for (int j = warp; j * 32 < P; j += 4) {
     const int p = j * 32 + lane;
+    const int nv = min(32, P - j * 32);
+    // the tile's k row (this lane's position) and v rows (this lane's two dimensions of all 32
+    // positions) are requested together: one memory round trip per tile
+    float4 kv[16];
+    float2 vv[32];
+    const float* kr = Kb + (size_t)min(p, P - 1) * kv_dim;
+#pragma unroll
+    for (int d4 = 0; d4 < 16; ++d4) kv[d4] = *reinterpret_cast<const float4*>(kr + 4 * d4);
+    const float* vr = Vb + (size_t)(j * 32) * kv_dim + 2 * lane;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      vv[i] = i < nv ? *reinterpret_cast<const float2*>(vr + (size_t)i * kv_dim) : make_float2(0.0f, 0.0f);
     float s[4];
-    if (p < P) {
-      const float* kr = Kb + (size_t)p * kv_dim;
+    {
       float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int d4 = 0; d4 < 16; ++d4) {
-        const float4 kv = *reinterpret_cast<const float4*>(kr + 4 * d4);
-        const float ke[4] = {kv.x, kv.y, kv.z, kv.w};
+        const float ke[4] = {kv[d4].x, kv[d4].y, kv[d4].z, kv[d4].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float4 qq = sq4[4 * d4 + e];
@@ -76,10 +87,7 @@ __global__ void __launch_bounds__(128) k_attn_batch(const float* __restrict__ q,
         }
       }
 #pragma unroll
-      for (int h = 0; h < 4; ++h) s[h] = dot[h] * 0.125f;
-    } else {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) s[h] = -INFINITY;
+      for (int h = 0; h < 4; ++h) s[h] = p < P ? dot[h] * 0.125f : -INFINITY;
     }
     float pe[4];
 #pragma unroll
@@ -94,15 +102,13 @@ __global__ void __launch_bounds__(128) k_attn_batch(const float* __restrict__ q,
     }
     sp[warp][lane] = make_float4(pe[0], pe[1], pe[2], pe[3]);
     __syncwarp();
-    const int nv = min(32, P - j * 32);
-    const float* vr = Vb + (size_t)(j * 32) * kv_dim + 2 * lane;
-    for (int i = 0; i < nv; ++i) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {  // positions past the tile's end have p = 0 and v = 0
       const float4 pp = sp[warp][i];
-      const float2 vv = *reinterpret_cast<const float2*>(vr + (size_t)i * kv_dim);
-      o[0][0] = fmaf(pp.x, vv.x, o[0][0]); o[0][1] = fmaf(pp.x, vv.y, o[0][1]);
-      o[1][0] = fmaf(pp.y, vv.x, o[1][0]); o[1][1] = fmaf(pp.y, vv.y, o[1][1]);
-      o[2][0] = fmaf(pp.z, vv.x, o[2][0]); o[2][1] = fmaf(pp.z, vv.y, o[2][1]);
-      o[3][0] = fmaf(pp.w, vv.x, o[3][0]); o[3][1] = fmaf(pp.w, vv.y, o[3][1]);
+      o[0][0] = fmaf(pp.x, vv[i].x, o[0][0]); o[0][1] = fmaf(pp.x, vv[i].y, o[0][1]);
+      o[1][0] = fmaf(pp.y, vv[i].x, o[1][0]); o[1][1] = fmaf(pp.y, vv[i].y, o[1][1]);
+      o[2][0] = fmaf(pp.z, vv[i].x, o[2][0]); o[2][1] = fmaf(pp.z, vv[i].y, o[2][1]);
+      o[3][0] = fmaf(pp.w, vv[i].x, o[3][0]); o[3][1] = fmaf(pp.w, vv[i].y, o[3][1]);
     }
     __syncwarp();
   }

@@ -213,7 +213,8 @@ struct Engine {
   float* t_x = nullptr;      // [tc_T][dim] residual stream
   float* t_q = nullptr;      // [tc_T][dim] rotated queries
   float* t_attn = nullptr;   // [tc_T][dim]
-  float* t_act = nullptr;    // [tc_T][ffn]
+  float* t_qkv = nullptr;    // [kTcMaxSplits][tc_T][dim + 2 kv_dim] q | k | v before RoPE (split-K planes)
+  float* t_gu = nullptr;     // [tc_T][2 ffn] gate / up rows, 64-row groups interleaved
   float* t_part = nullptr;   // [kTcMaxSplits][tc_T][dim] split-K partial sums
   int32_t* t_idx = nullptr;  // [3][tc_T] token | position | slot of the step's rows
   int32_t* h_idx = nullptr;  // pinned staging of t_idx
@@ -621,7 +622,8 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMalloc(&E->t_x, (size_t)T * dim * 4));
   LE_CK(cudaMalloc(&E->t_q, (size_t)T * dim * 4));
   LE_CK(cudaMalloc(&E->t_attn, (size_t)T * dim * 4));
-  LE_CK(cudaMalloc(&E->t_act, (size_t)T * ffn * 4));
+  LE_CK(cudaMalloc(&E->t_qkv, (size_t)kTcMaxSplits * T * (dim + 2 * kvd) * 4));
+  LE_CK(cudaMalloc(&E->t_gu, (size_t)T * 2 * ffn * 4));
   LE_CK(cudaMalloc(&E->t_part, (size_t)kTcMaxSplits * T * dim * 4));
   LE_CK(cudaMalloc(&E->t_idx, (size_t)3 * T * 4));
   LE_CK(cudaMallocHost(&E->h_idx, (size_t)3 * T * 4));
@@ -659,7 +661,6 @@ static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int s
   A.kb_total = W.kb;
   A.tok_tiles = (T + tc::kTok - 1) / tc::kTok;
   A.T = T;
-  A.nt = T >= tc::kTok ? tc::kTok : (T + 15) / 16 * 16;
   A.kb_split = (W.kb + splits - 1) / splits;
   A.splits = (W.kb + A.kb_split - 1) / A.kb_split;
   A.error = E->tc_err;
@@ -697,58 +698,39 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog) {
   const int32_t* slot = E->t_idx + 2 * n;
   const int tok_tiles = (n + kTok - 1) / kTok;
   cudaStream_t s = E->stream;
+  auto rows = [&](float* out, int ldo, int N, size_t split_stride) {
+    Args A{};
+    A.out = out;
+    A.ldo = ldo;
+    A.N = N;
+    A.split_stride = split_stride;
+    return A;
+  };
   k_embed_batch<<<n, 256, 0, s>>>(E->lm_head, tok, E->t_x, dim);
   int d_splits = 0;
   for (uint32_t l = 0; l < E->layers; ++l) {
     const TcLayer& Y = E->tcl[l];
     const DevLayer& D = E->L[l];
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, dim, E->img_d);
-    Args A{};
-    A.mode = MODE_QKV;
-    A.out = E->t_q;
-    A.ldo = dim;
-    A.N = dim + 2 * kvd;
-    A.pos = pos;
-    A.slot = slot;
-    A.rope_cos = E->rope_cos;
-    A.rope_sin = E->rope_sin;
-    A.kc = E->kcache + l * layer_stride;
-    A.vc = E->vcache + l * layer_stride;
-    A.slot_stride = slot_stride;
-    A.q_rows = dim;
-    A.kv_dim = kvd;
-    tc_launch(E, Y.qkv, E->img_d, n, 1, A);
-    k_attn_batch<<<dim3(n, E->kv_heads), 128, 0, s>>>(E->t_q, dim, E->kcache + l * layer_stride,
-                                                       E->vcache + l * layer_stride, slot_stride, kvd, pos, slot,
-                                                       E->t_attn);
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, dim, E->img_d);
-    Args R{};
-    R.mode = MODE_ROWS;
-    R.out = E->t_part;
-    R.ldo = dim;
-    R.N = dim;
-    R.split_stride = part_stride;
-    const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), R);
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, so, part_stride, D.post_norm, dim, E->img_d);
-    Args G{};
-    G.mode = MODE_SWIGLU;
-    G.out = E->t_act;
-    G.ldo = ffn;
-    G.N = ffn;
-    tc_launch(E, Y.gu, E->img_d, n, 1, G);
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_act, ffn, nullptr, 0, 0, nullptr, ffn, E->img_f);
-    d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), R);
+    float* kc = E->kcache + l * layer_stride;
+    float* vc = E->vcache + l * layer_stride;
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, 0, dim, E->img_d);
+    const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
+    const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
+                             rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
+    k_rope_append<<<n, 256, 0, s>>>(E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q,
+                                    kc, vc, slot_stride);
+    k_attn_batch<<<dim3(n, E->kv_heads), 128, 0, s>>>(E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn);
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
+    const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, so, part_stride, D.post_norm, 0, dim, E->img_d);
+    tc_launch(E, Y.gu, E->img_d, n, 1, rows(E->t_gu, 2 * ffn, 2 * ffn, 0));
+    k_tc_stage<<<n, 256, 0, s>>>(E->t_gu, 2 * ffn, nullptr, 0, 0, nullptr, 1, ffn, E->img_f);
+    d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), rows(E->t_part, dim, dim, part_stride));
   }
   if (nlog > 0) {
     k_tc_stage<<<nlog, 256, 0, s>>>(E->t_x + (size_t)lrow0 * dim, dim, E->t_part + (size_t)lrow0 * dim, d_splits,
-                                     part_stride, E->final_norm, dim, E->img_d);
-    Args R{};
-    R.mode = MODE_ROWS;
-    R.out = E->logits;
-    R.ldo = (int)E->vocab;
-    R.N = (int)E->vocab;
-    R.split_stride = 0;
-    tc_launch(E, E->tc_lm, E->img_d, nlog, 1, R);
+                                     part_stride, E->final_norm, 0, dim, E->img_d);
+    tc_launch(E, E->tc_lm, E->img_d, nlog, 1, rows(E->logits, (int)E->vocab, (int)E->vocab, 0));
     k_argmax_rows_batch<<<dim3(E->tc_am_parts, nlog), 256, 0, s>>>(E->logits, (int)E->vocab, E->vocab, E->t_am);
     k_argmax_finish_batch<<<nlog, 256, 0, s>>>(E->t_am, E->tc_am_parts, E->am_result);
   }
@@ -909,8 +891,8 @@ static void destroy(Engine* E) {
   void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged, E->d_ctrl};
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
-  void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_act, E->t_part, E->t_idx,
-                  E->t_am, E->tc_err};
+  void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_qkv, E->t_gu, E->t_part,
+                  E->t_idx, E->t_am, E->tc_err};
   for (void* p : tdev) if (p) cudaFree(p);
   if (E->h_idx) cudaFreeHost(E->h_idx);
   if (E->idx_ev) cudaEventDestroy(E->idx_ev);
@@ -1185,7 +1167,13 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
                                       const int32_t* slots, int n, int compute_logits) {
   if (!engine || !tokens || !positions || !slots || n < 1) return -1;
   Engine* E = H(engine);
-  if (n > E->max_batch) { E->err = "forward_batch: n exceeds max_batch"; return -1; }
+  // the batched path takes up to tc_T rows (several positions of a slot may share a call); rows
+  // with logits land in the max_batch logits rows
+  const int max_rows = E->tc ? std::max(E->max_batch, E->tc_T) : E->max_batch;
+  if (n > max_rows || (compute_logits && n > E->max_batch)) {
+    E->err = "forward_batch: n exceeds the row capacity";
+    return -1;
+  }
   for (int i = 0; i < n; ++i) {
     if (slots[i] < 0 || slots[i] >= E->max_batch) { E->err = "forward_batch: slot out of range"; return -1; }
     if (positions[i] < 0 || positions[i] >= E->max_seq) { E->err = "forward_batch: position out of range"; return -1; }
@@ -1425,7 +1413,7 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     cudaMemsetAsync(err, 0, 16, s);
     QMat W{nibbles, step_bf16, min_bf16, N, K};
     k_tc_repack<<<sms * 8, 256, 0, s>>>(W, recs, 0, kM, 0);
-    k_tc_stage<<<M, 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, K, img);
+    k_tc_stage<<<M, 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, 0, K, img);
     Args A{};
     A.recs = recs;
     A.img = img;
@@ -1435,13 +1423,30 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     A.splits = 1;
     A.kb_split = kb;
     A.T = M;
-    A.nt = M >= kTok ? kTok : (M + 15) / 16 * 16;
     A.N = N;
-    A.mode = MODE_ROWS;
     A.out = y;
     A.ldo = N;
     A.error = err;
+    // diagnostics: $LLAMA_B128_GEMM_TRACE names a file that receives CTA 0's pipeline events
+    const char* trace_path = getenv("LLAMA_B128_GEMM_TRACE");
+    unsigned long long* trace = nullptr;
+    const size_t trace_bytes = (size_t)kTraceEvents * kTraceBlocks * 8;
+    if (trace_path && cudaMalloc(&trace, trace_bytes) == cudaSuccess) {
+      cudaMemsetAsync(trace, 0, trace_bytes, s);
+      A.trace = trace;
+    }
     k_tc_gemm<<<std::min(tiles * tok_tiles, sms), tc::kThreads, kSmemBytes, s>>>(A);
+    if (trace) {
+      std::vector<unsigned long long> h(trace_bytes / 8);
+      if (cudaMemcpyAsync(h.data(), trace, trace_bytes, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+          cudaStreamSynchronize(s) == cudaSuccess) {
+        if (FILE* f = fopen(trace_path, "wb")) {
+          fwrite(h.data(), 8, h.size(), f);
+          fclose(f);
+        }
+      }
+      cudaFree(trace);
+    }
     uint32_t herr = 1;
     if (attr && cudaGetLastError() == cudaSuccess &&
         cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&

@@ -4,25 +4,32 @@
 //
 //   y[t][n] = sum_b ( min[n][b] * xs[t][b]  +  step[n][b] * sum_{k in b} q[n][k] * x[t][k] )
 //
-// One CTA (10 warps, one per SM, persistent over work units) computes a tile of 128 weight rows
-// for up to 64 tokens over a range of 128-wide K blocks:
+// One CTA (19 warps, one per SM, persistent over work units) computes a tile of 128 weight rows
+// for up to 64 tokens over a range of 128-wide K blocks, as a pipeline over K blocks:
 //
 //   * warp 0 (one lane) streams, per K block, the activation image of the token tile (the 64
 //     token rows as bf16 hi and lo parts, x = hi + lo, hi = bf16(x), lo = bf16(x - hi), already
 //     in the UMMA K-major 128-byte-swizzled layout, plus the tokens' block sums) and the tile's
-//     weight record (nibbles + scales) with two 1-D bulk copies into a 4-stage shared-memory ring;
-//   * warps 2..9 (the row warps, thread = weight row) turn each record's nibbles into bf16 codes
-//     q (exact: 0..15) and write them into tensor memory (tcgen05.st) as the MMA's A operand;
-//   * warp 1 (one lane) issues, per 16-wide K step, two tcgen05.mma kind::f16 with A = q from
-//     tensor memory: D_hi += q . x_hi and D_lo += q . x_lo (fp32 accumulators in tensor memory,
-//     one pair per K block, double buffered);
-//   * the row warps then read D_hi and D_lo back (tcgen05.ld) and apply the block's scales in
-//     fp32: acc[t] += min * xs[t] + step * (D_hi[t] + D_lo[t]) (the reference's factored form).
+//     weight record (nibbles + scales) with two 1-D bulk copies into a 5-stage shared-memory
+//     ring, and prefetches the records of later blocks into L2;
+//   * warps 3..10 (dequantisers, two sets taking alternate blocks, thread = weight row) turn
+//     each record's nibbles into bf16 codes q (exact: 0..15), write them into tensor memory
+//     (tcgen05.st) as the MMA's A operand, and pass the block's scales and block sums to the
+//     epilogue through a small side ring;
+//   * warps 1 and 2 (one lane each, alternate blocks) issue, per 16-wide K step, one
+//     tcgen05.mma kind::f16 (M = 128, N = 128)
+//     with A = q from tensor memory and B = the 64 tokens' hi rows stacked on their lo rows, into
+//     an fp32 accumulator D in tensor memory (one per K block): D[t] = sum_k q . x_hi[t],
+//     D[64 + t] = sum_k q . x_lo[t]; the MMAs' completion frees the stage, the A buffer and
+//     signals the accumulator;
+//   * warps 11..18 (epilogue, thread = weight row, 32 tokens each) read D back (tcgen05.ld) and
+//     apply the block's scales in fp32: acc[t] += min * xs[t] + step * (D[t] + D[64 + t]) (the
+//     reference's factored form); at the end of a unit they store the rows (split-K partials,
+//     projections or logits).
+// A codes have four tensor-memory buffers, accumulators two.
 //
 // Products q * x_hi and q * x_lo are exact in fp32; the only rounding beyond fp32 accumulation
-// is lo's own bf16 rounding (relative 2^-17 of x).  Work units end with a mode-specific epilogue:
-// plain rows (split-K partials or logits), RoPE + KV-cache append for the q|k|v rows, or
-// SiLU(gate) * up for interleaved gate/up tiles.
+// is lo's own bf16 rounding (relative 2^-17 of x).
 //
 // Weight records are built at load time from the LLM4S128 matrices: per (row tile, K block)
 // 8704 bytes: [0, 8192) row r's 64 nibble bytes at r*64, its 16-byte chunk c stored at chunk
@@ -30,10 +37,10 @@
 // (step | min << 16) at 8192 + 4r.  Rows past the matrix are zero.
 //
 // Activation images are written by k_tc_stage: per (token tile, K block) 33024 bytes: four
-// 8192-byte atoms (hi k 0..63, hi k 64..127, lo k 0..63, lo k 64..127), each 64 token rows of
+// 8192-byte atoms (hi k 0..63, lo k 0..63, hi k 64..127, lo k 64..127), each 64 token rows of
 // 128 bytes with 16-byte chunk c of row t at chunk position c ^ (t & 7) (the 128-byte swizzle
-// of the UMMA canonical K-major layout, 8-row groups 1024 bytes apart), then the 64 tokens'
-// block sums (fp32).
+// of the UMMA canonical K-major layout, 8-row groups 1024 bytes apart; a hi atom and the lo
+// atom after it form one 128-row B operand), then the 64 tokens' block sums (fp32).
 //
 // All mbarrier waits are bounded in time: on timeout the kernel records an error word and every
 // role drains, so the host sees an error instead of a hang.
@@ -51,42 +58,47 @@ constexpr int kTok = 64;                 // tokens per tile
 constexpr int kNibBytes = kM * 64;       // nibbles of one (tile, K block)
 constexpr int kRecBytes = kNibBytes + kM * 4;
 constexpr int kAtom = kTok * 128;        // one 64-wide K slice of 64 token rows (bf16, swizzled)
-constexpr int kStages = 4;
 constexpr int kImgBytes = 4 * kAtom + kTok * 4;  // activation image of one (token tile, K block)
-constexpr int kOffXs = 4 * kAtom;        // stage: hi0 | hi1 | lo0 | lo1 | xs | record
+constexpr int kOffXs = 4 * kAtom;        // stage: hi0 | lo0 | hi1 | lo1 | xs | record
 constexpr int kOffRec = kImgBytes;
 constexpr int kStageTx = kImgBytes + kRecBytes;
 constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
-constexpr int kXchStride = kM + 1;       // exchange rows of 128 floats, padded
-constexpr int kXchBytes = 2 * 32 * kXchStride * 4;
-constexpr int kWarps = 10;
+constexpr int kStages = 5;
+constexpr int kSide = 8;                 // side ring: per block the rows' scales and the block sums
+constexpr int kSideBytes = kM * 4 + kTok * 4;
+constexpr int kWarps = 19;               // 0 producer, 1-2 MMA issuers, 3-10 dequantisers, 11-18 epilogue
 constexpr int kThreads = 32 * kWarps;
-constexpr int kTmemCols = 512;           // A[2] (64 cols each) | D[2] (hi 64 | lo 64 each)
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kXchBytes + 256;
-
-enum Mode : int { MODE_ROWS = 0, MODE_QKV = 1, MODE_SWIGLU = 2 };
+constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64 columns each)
+constexpr int kBufsD = 2;                // accumulator buffers (128 columns: hi | lo tokens)
+constexpr int kTmemCols = 512;
+constexpr int kDCol = kBufsA * 64;
+constexpr int kPrefetch = 8;             // records prefetched into L2 this many blocks ahead
+constexpr int kNumBars = 2 * kStages + kBufsA + kBufsD + 2 * kSide + 1;
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kSide * kSideBytes + (kNumBars * 8 + 63) / 64 * 64;
 
 struct Args {
   const uint8_t* recs;   // [tiles][kb_total][kRecBytes]
   const uint8_t* img;    // [tok_tiles][kb_total][kImgBytes]
   int tiles, kb_total, tok_tiles, splits, kb_split;
-  int T, nt;             // valid tokens, MMA N (16..64)
-  int N;                 // valid output rows (MODE_ROWS / MODE_QKV), ffn (MODE_SWIGLU)
-  int mode;
-  float* out;            // ROWS: out[(split * T + t) * ldo + n]; QKV: q rows; SWIGLU: act
+  int T;                 // valid tokens
+  int N;                 // valid output rows
+  float* out;            // out[split * split_stride + t * ldo + n]
   int ldo;
-  size_t split_stride;   // ROWS: floats between split planes
-  // MODE_QKV
-  const int32_t* pos;
-  const int32_t* slot;
-  const float* rope_cos;
-  const float* rope_sin;
-  float* kc;             // cache of slot 0 at this layer; slot s at + s * slot_stride
-  float* vc;
-  size_t slot_stride;
-  int q_rows, kv_dim;
+  size_t split_stride;
   uint32_t* error;       // set to a nonzero code on a wait timeout
+  unsigned long long* trace;  // optional: CTA 0's pipeline events, [kTraceEvents][kTraceBlocks]
 };
+
+// Pipeline trace (diagnostics): globaltimer stamps of CTA 0 for its first kTraceBlocks blocks.
+// 0: copies issued, 1: MMA inputs ready (waits passed), 2: dequantiser sees the stage,
+// 3: A codes written, 4: epilogue sees the accumulator, 5: epilogue done with the block,
+// 6: MMAs issued, 7: commit issued, 8: MMA loop top, 9: MMA issuer past the A-codes wait.
+constexpr int kTraceEvents = 10;
+constexpr int kTraceBlocks = 256;
+__device__ __forceinline__ void trace_ev(const Args& A, int ev, int g) {
+  if (A.trace && blockIdx.x == 0 && g < kTraceBlocks && (threadIdx.x & 31) == 0)
+    A.trace[ev * kTraceBlocks + g] = gtimer();
+}
 
 // ---------------------------------------------------------------------------------------------
 // PTX wrappers (tcgen05, TMA)
@@ -132,6 +144,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -172,16 +191,27 @@ __device__ __forceinline__ uint32_t nib_pair_bf16(uint32_t w, uint32_t w4) {
 
 struct Shared {
   uint32_t base;   // 1024-aligned shared address of stage 0
-  uint32_t xch;    // exchange buffer
-  uint32_t bar;    // barriers: full[4] empty[4] afull[2] dfull[2] dempty[2] final xch[2]
+  uint32_t side;   // side ring
+  uint32_t bar;    // barriers
 };
+// barrier index layout: full[S] done[S] afull[BA] dempty[BD] sfull[8] sempty[8] final.
+// done[g % S] completes when the MMAs of block g have: the stage, the A buffer of block g and
+// its accumulator are then free or ready (one tcgen05.commit serves all three).
 __device__ __forceinline__ uint32_t bar_full(const Shared& S, int s) { return S.bar + 8 * s; }
-__device__ __forceinline__ uint32_t bar_empty(const Shared& S, int s) { return S.bar + 8 * (kStages + s); }
-__device__ __forceinline__ uint32_t bar_afull(const Shared& S, int a) { return S.bar + 8 * (2 * kStages + a); }
-__device__ __forceinline__ uint32_t bar_dfull(const Shared& S, int a) { return S.bar + 8 * (2 * kStages + 2 + a); }
-__device__ __forceinline__ uint32_t bar_dempty(const Shared& S, int a) { return S.bar + 8 * (2 * kStages + 4 + a); }
-__device__ __forceinline__ uint32_t bar_final(const Shared& S) { return S.bar + 8 * (2 * kStages + 6); }
-__device__ __forceinline__ uint32_t bar_xch(const Shared& S, int h) { return S.bar + 8 * (2 * kStages + 7 + h); }
+__device__ __forceinline__ uint32_t bar_done(const Shared& S, int s) { return S.bar + 8 * (kStages + s); }
+__device__ __forceinline__ uint32_t bar_afull(const Shared& S, int b) { return S.bar + 8 * (2 * kStages + b); }
+__device__ __forceinline__ uint32_t bar_dempty(const Shared& S, int b) {
+  return S.bar + 8 * (2 * kStages + kBufsA + b);
+}
+__device__ __forceinline__ uint32_t bar_sfull(const Shared& S, int j) {
+  return S.bar + 8 * (2 * kStages + kBufsA + kBufsD + j);
+}
+__device__ __forceinline__ uint32_t bar_sempty(const Shared& S, int j) {
+  return S.bar + 8 * (2 * kStages + kBufsA + kBufsD + kSide + j);
+}
+// Parity of the completion of done[] that belongs to block g.
+__device__ __forceinline__ uint32_t done_parity(int g) { return (uint32_t)(g / kStages) & 1u; }
+__device__ __forceinline__ uint32_t bar_final(const Shared& S) { return S.bar + 8 * (kNumBars - 1); }
 
 // Bounded wait on an mbarrier phase.  Returns false when the launch has failed (here or in
 // another role); the first timeout records `where`.
@@ -199,6 +229,12 @@ __device__ __forceinline__ bool wait_bar(const Args& A, volatile uint32_t* abort
     }
   }
 }
+// Warp-uniform bounded wait: lanes leave the poll at different times, the vote reconverges the
+// warp (tcgen05.ld / st are warp-aligned) and makes a timeout the whole warp's.
+__device__ __forceinline__ bool warp_wait(const Args& A, volatile uint32_t* abort_flag, uint32_t bar, uint32_t parity,
+                                          uint32_t where) {
+  return __all_sync(0xffffffffu, wait_bar(A, abort_flag, bar, parity, where));
+}
 
 struct Unit {
   int tile, tt, split, kb0, kb1;
@@ -215,91 +251,46 @@ __device__ __forceinline__ Unit unit_of(const Args& A, int u) {
   return U;
 }
 
-// Unit epilogue of the row warps.  Thread (q, h, lane) owns weight row r = 32q + lane of the
-// tile and tokens 32h .. 32h+31 of the token tile.
-// The exchange between the four row warps of a token half uses an mbarrier (bounded wait), so a
-// warp that has given up after a timeout cannot leave the others blocked.
-__device__ __forceinline__ bool xch_sync(const Args& A, volatile uint32_t* abort_flag, const Shared& S, int h,
-                                         int& xph) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive_n(bar_xch(S, h), 1);
-  const bool ok = __all_sync(0xffffffffu, wait_bar(A, abort_flag, bar_xch(S, h), (uint32_t)(xph & 1), 9));
-  ++xph;
-  return ok;
-}
-
-__device__ __forceinline__ bool emit_unit(const Args& A, volatile uint32_t* abort_flag, const Shared& S,
-                                          const Unit& U, int r, int h, int& xph, const float (&acc)[32]) {
-  const int tok0 = U.tt * kTok + 32 * h;
-  if (A.mode == MODE_ROWS) {
-    const int n = U.tile * kM + r;
-    if (n >= A.N) return true;
-    float* o = A.out + (size_t)U.split * A.split_stride + n;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int t = tok0 + i;
-      if (t < A.T) o[(size_t)t * A.ldo] = acc[i];
-    }
-    return true;
+// Walks the (unit, K block) sequence of this CTA.
+struct Cursor {
+  int u, kb;
+  Unit U;
+  __device__ __forceinline__ void start(const Args& A, int n_units) {
+    u = blockIdx.x;
+    if (u < n_units) { U = unit_of(A, u); kb = U.kb0; }
   }
-  // exchange through shared memory: xch[h][i][r]
-  const uint32_t xb = S.xch + (uint32_t)(h * 32 * kXchStride) * 4u;
-#pragma unroll
-  for (int i = 0; i < 32; ++i)
-    asm volatile("st.shared.f32 [%0], %1;" ::"r"(xb + (uint32_t)(i * kXchStride + r) * 4u), "f"(acc[i]) : "memory");
-  if (!xch_sync(A, abort_flag, S, h, xph)) return false;
-  if (A.mode == MODE_QKV) {
-    const int n = U.tile * kM + r;
-    const int i2 = r & 31;
-    const bool second = (r & 32) != 0;
-    const int partner = r ^ 32;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int t = tok0 + i;
-      if (t >= A.T || n >= A.N) continue;
-      const float own = acc[i];
-      const float oth = ldsf(xb + (uint32_t)(i * kXchStride + partner) * 4u);
-      if (n < A.q_rows + A.kv_dim) {
-        const int p = A.pos[t];
-        const float c = A.rope_cos[p * 32 + i2], s = A.rope_sin[p * 32 + i2];
-        // apply_rope (src/llama_engine.cpp:120-151): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c)
-        const float x0 = second ? oth : own, x1 = second ? own : oth;
-        const float v = second ? __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c))
-                               : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        if (n < A.q_rows) {
-          A.out[(size_t)t * A.ldo + n] = v;
-        } else {
-          A.kc[(size_t)A.slot[t] * A.slot_stride + (size_t)p * A.kv_dim + (n - A.q_rows)] = v;
-        }
-      } else {
-        const int p = A.pos[t];
-        A.vc[(size_t)A.slot[t] * A.slot_stride + (size_t)p * A.kv_dim + (n - A.q_rows - A.kv_dim)] = own;
-      }
-    }
-  } else {  // MODE_SWIGLU: rows 0..63 gate, 64..127 up of the same 64 ffn rows
-    if (r < 64) {
-      const int j = U.tile * 64 + r;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int t = tok0 + i;
-        if (t >= A.T || j >= A.N) continue;
-        const float g = acc[i];
-        const float u = ldsf(xb + (uint32_t)(i * kXchStride + r + 64) * 4u);
-        A.out[(size_t)t * A.ldo + j] = (g / (1.0f + expf(-g))) * u;
-      }
+  __device__ __forceinline__ bool valid(int n_units) const { return u < n_units; }
+  __device__ __forceinline__ void next(const Args& A, int n_units) {
+    if (++kb >= U.kb1) {
+      u += gridDim.x;
+      if (u < n_units) { U = unit_of(A, u); kb = U.kb0; }
     }
   }
-  return xch_sync(A, abort_flag, S, h, xph);  // the exchange rows are reused by the next unit
+};
+
+// Number of K blocks this CTA processes over all its units.
+__device__ __forceinline__ int cta_blocks(const Args& A, int n_units) {
+  int n = 0;
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const Unit U = unit_of(A, u);
+    n += U.kb1 - U.kb0;
+  }
+  return n;
 }
 
+// Warp roles: 0 = bulk-copy producer (one lane), 1 = tensor-memory owner and MMA issuer of the
+// even blocks (one lane), 2 = MMA issuer of the odd blocks, 3..10 = dequantisers, 11..18 =
+// epilogue.  A warp may only touch tensor-memory lanes 32 * (warp % 4) .. +31, so each group of
+// four covers the 128 rows once; the two dequantiser groups take alternate blocks, the two
+// epilogue groups the two halves of the token tile.
 __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
   extern __shared__ __align__(1024) uint8_t tc_smem[];
   __shared__ uint32_t s_tmem;
   __shared__ volatile uint32_t s_abort;
   Shared S;
   S.base = (smem_u32(tc_smem) + 1023u) & ~1023u;
-  S.xch = S.base + kStages * kStageBytes;
-  S.bar = S.xch + kXchBytes;
+  S.side = S.base + kStages * kStageBytes;
+  S.bar = S.side + kSide * kSideBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = A.tiles * A.tok_tiles * A.splits;
 
@@ -307,16 +298,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     s_abort = 0u;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar_full(S, s), 1);
-      mbar_init(bar_empty(S, s), 1 + 8);
+      mbar_init(bar_done(S, s), 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(bar_afull(S, a), 8);
-      mbar_init(bar_dfull(S, a), 1);
-      mbar_init(bar_dempty(S, a), 8);
+    for (int b = 0; b < kBufsA; ++b) mbar_init(bar_afull(S, b), 4);
+    for (int b = 0; b < kBufsD; ++b) mbar_init(bar_dempty(S, b), 8);
+    for (int j = 0; j < kSide; ++j) {
+      mbar_init(bar_sfull(S, j), 4);
+      mbar_init(bar_sempty(S, j), 8);
     }
-    mbar_init(bar_final(S), 1);
-    mbar_init(bar_xch(S, 0), 4);
-    mbar_init(bar_xch(S, 1), 4);
+    mbar_init(bar_final(S), 2);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -331,18 +321,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer ----------------
+      // ---------------- producer: activation image + weight record per K block ----------------
+      Cursor c, ahead;
+      c.start(A, n_units);
+      ahead.start(A, n_units);
+      for (int i = 0; i < kPrefetch && ahead.valid(n_units); ++i) {
+        prefetch_l2(A.recs + ((size_t)ahead.U.tile * A.kb_total + ahead.kb) * kRecBytes, kRecBytes);
+        ahead.next(A, n_units);
+      }
       int g = 0;
-      for (int u = blockIdx.x; u < n_units && !s_abort; u += gridDim.x) {
-        const Unit U = unit_of(A, u);
-        for (int kb = U.kb0; kb < U.kb1; ++kb, ++g) {
-          const int s = g % kStages, n = g / kStages;
-          if (g >= kStages && !wait_bar(A, &s_abort, bar_empty(S, s), (n - 1) & 1, 1)) break;
-          const uint32_t st = S.base + s * kStageBytes;
-          const uint32_t fb = bar_full(S, s);
-          mbar_expect_tx(fb, kStageTx);
-          bulk_g2s(st, A.img + ((size_t)U.tt * A.kb_total + kb) * kImgBytes, kImgBytes, fb);
-          bulk_g2s(st + kOffRec, A.recs + ((size_t)U.tile * A.kb_total + kb) * kRecBytes, kRecBytes, fb);
+      for (; c.valid(n_units) && !s_abort; c.next(A, n_units), ++g) {
+        const int s = g % kStages;
+        if (g >= kStages && !wait_bar(A, &s_abort, bar_done(S, s), done_parity(g - kStages), 1)) break;
+        const uint32_t st = S.base + s * kStageBytes;
+        const uint32_t fb = bar_full(S, s);
+        mbar_expect_tx(fb, kStageTx);
+        bulk_g2s(st, A.img + ((size_t)c.U.tt * A.kb_total + c.kb) * kImgBytes, kImgBytes, fb);
+        bulk_g2s(st + kOffRec, A.recs + ((size_t)c.U.tile * A.kb_total + c.kb) * kRecBytes, kRecBytes, fb);
+        trace_ev(A, 0, g);
+        if (ahead.valid(n_units)) {
+          prefetch_l2(A.recs + ((size_t)ahead.U.tile * A.kb_total + ahead.kb) * kRecBytes, kRecBytes);
+          ahead.next(A, n_units);
         }
       }
       // drain: every issued stage must have landed before the CTA may exit
@@ -352,121 +351,165 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         wait_bar(A, &s_abort, bar_full(S, s), (last / kStages) & 1, 2);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
     if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      const uint32_t idesc = idesc_bf16(A.nt);
-      int g = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const Unit U = unit_of(A, u);
-        for (int kb = U.kb0; kb < U.kb1; ++kb, ++g) {
-          const int s = g % kStages, n = g / kStages, a = g & 1, na = g >> 1;
-          ok = wait_bar(A, &s_abort, bar_full(S, s), n & 1, 3) && wait_bar(A, &s_abort, bar_afull(S, a), na & 1, 4) &&
-               (g < 2 || wait_bar(A, &s_abort, bar_dempty(S, a), (na - 1) & 1, 5));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t st = S.base + s * kStageBytes;
-          const uint32_t d_hi = tmem + 128 + a * 128, d_lo = d_hi + 64;
-          const uint32_t a_t = tmem + a * 64;
+      // ---------------- MMA issuers: warp 1 takes the even blocks, warp 2 the odd ones ----------------
+      // (two threads on different SM sub-partitions, so one's waits and bookkeeping overlap the
+      // other's MMAs; each commit tracks its own thread's MMAs).  One MMA per 16-wide K step: B
+      // rows 0..63 are the tokens' hi parts, rows 64..127 their lo parts, so D columns 0..63 and
+      // 64..127 accumulate q . x_hi and q . x_lo.  The loop is kept short: it runs on a sub-
+      // partition shared with busy dequant and epilogue warps.
+      const uint32_t idesc = idesc_bf16(2 * kTok);
+      const int nblk = cta_blocks(A, n_units);
+      const uint32_t desc_hi = (uint32_t)(sw128_desc(0) >> 32);
+      const uint32_t desc_lo0 = (uint32_t)sw128_desc(S.base);
+      for (int g = warp - 1; g < nblk; g += 2) {
+        const int s = g % kStages;
+        const int ba = g % kBufsA, na = g / kBufsA, bd = g % kBufsD, nd = g / kBufsD;
+        // afull(g) implies full(g): the dequantisers waited for the stage before arriving
+        trace_ev(A, 8, g);
+        bool ok = wait_bar(A, &s_abort, bar_afull(S, ba), na & 1, 4);
+        trace_ev(A, 9, g);
+        ok = ok && (g < kBufsD || wait_bar(A, &s_abort, bar_dempty(S, bd), (nd - 1) & 1, 5));
+        if (!ok) break;
+        trace_ev(A, 1, g);
+        tc_fence_after();
+        const uint32_t dl = desc_lo0 + (uint32_t)(s * (kStageBytes >> 4));
+        const uint32_t d = tmem + kDCol + bd * 2 * kTok;
+        const uint32_t a_t = tmem + ba * 64;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t b_hi = st + (k >> 2) * kAtom + (k & 3) * 32;
-            tc_mma_ts(d_hi, a_t + 8 * k, sw128_desc(b_hi), idesc, k > 0);
-            tc_mma_ts(d_lo, a_t + 8 * k, sw128_desc(b_hi + 2 * kAtom), idesc, k > 0);
-          }
-          tc_commit(bar_empty(S, s));
-          tc_commit(bar_dfull(S, a));
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t bdesc = ((uint64_t)desc_hi << 32) | (dl + (uint32_t)((((k >> 2) * 2 * kAtom) + (k & 3) * 32) >> 4));
+          tc_mma_ts(d, a_t + 8 * k, bdesc, idesc, k > 0);
         }
+        trace_ev(A, 6, g);
+        tc_commit(bar_done(S, s));
+        trace_ev(A, 7, g);
       }
       // all issued MMAs complete before the tensor memory is released
       tc_commit(bar_final(S));
       wait_bar(A, &s_abort, bar_final(S), 0, 6);
     }
-  } else {
-    // ---------------- row warps: dequantise into tensor memory, per-block epilogue ----------------
-    const int q = warp & 3;
-    const int h = warp < 6 ? 0 : 1;
+  } else if (warp < 11) {
+    // ---------------- dequantisers: nibbles -> bf16 codes in tensor memory ----------------
+    // two sets of four warps take alternate blocks (set h: blocks g with g % 2 == h), so one
+    // set's waits and tensor-memory store latency overlap the other's work; warp (q, h) converts
+    // rows 32q .. 32q+31 of its blocks
+    const int q = warp & 3, h = (warp - 3) >> 2;
     const int r = 32 * q + lane;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int sw = (r >> 1) & 3;
-    float acc[32];
+    const int nblk = cta_blocks(A, n_units);
+    for (int g = h; g < nblk; g += 2) {
+      const int s = g % kStages, n = g / kStages, b = g % kBufsA;
+      const int j = g % kSide, nj = g / kSide;
+      // A[b] is free once the MMAs of block g - kBufsA have completed; side slot j once the
+      // epilogue has read block g - kSide
+      if (!warp_wait(A, &s_abort, bar_full(S, s), n & 1, 8) ||
+          (g >= kBufsA && !warp_wait(A, &s_abort, bar_done(S, (g - kBufsA) % kStages), done_parity(g - kBufsA), 10)) ||
+          (g >= kSide && !warp_wait(A, &s_abort, bar_sempty(S, j), (nj - 1) & 1, 11)))
+        break;
+      if (warp == 3 || warp == 7) trace_ev(A, 2, g);
+      const uint32_t st = S.base + s * kStageBytes;
+      const uint32_t rec = st + kOffRec + 64 * r;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
-    int g = 0, xph = 0;
-    bool ok = true;
-    Unit prev{};
-    bool prev_last = false;
-    // per-block epilogue of block gp (stage sp, buffer ap)
-    auto epilogue = [&](int gp) -> bool {
-      const int sp = gp % kStages, ap = gp & 1, nap = gp >> 1;
-      // lanes leave the poll at different times; the vote reconverges the warp (tcgen05.ld is
-      // warp-aligned) and makes a timeout warp-uniform
-      if (!__all_sync(0xffffffffu, wait_bar(A, &s_abort, bar_dfull(S, ap), nap & 1, 7))) return false;
-      tc_fence_after();
-      uint32_t vh[32], vl[32];
-      const uint32_t dcol = tmem + lane_base + 128 + ap * 128 + 32 * h;
-      tmem_ld32(dcol, vh);
-      tmem_ld32(dcol + 64, vl);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(bar_dempty(S, ap), 1);
-      const uint32_t st = S.base + sp * kStageBytes;
-      const uint32_t sc = lds32(st + kOffRec + kNibBytes + 4 * r);
-      const float step = bf16_bits_to_f32(sc & 0xFFFFu), mn = bf16_bits_to_f32(sc >> 16);
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const uint4 x4 = lds128(st + kOffXs + 4 * (32 * h + i));
-        const float xs[4] = {__uint_as_float(x4.x), __uint_as_float(x4.y), __uint_as_float(x4.z),
-                             __uint_as_float(x4.w)};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float d = __uint_as_float(vh[i + j]) + __uint_as_float(vl[i + j]);
-          acc[i + j] = fmaf(step, d, fmaf(mn, xs[j], acc[i + j]));
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(bar_empty(S, sp), 1);
-      return true;
-    };
-    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-      const Unit U = unit_of(A, u);
-      for (int kb = U.kb0; kb < U.kb1; ++kb, ++g) {
-        const int s = g % kStages, n = g / kStages, a = g & 1;
-        if (!__all_sync(0xffffffffu, wait_bar(A, &s_abort, bar_full(S, s), n & 1, 8))) { ok = false; break; }
-        // dequantise this thread's half of the block row into A[a]
-        const uint32_t rec = S.base + s * kStageBytes + kOffRec + 64 * r;
-        const uint4 c0 = lds128(rec + (uint32_t)(((2 * h) ^ sw) << 4));
-        const uint4 c1 = lds128(rec + (uint32_t)(((2 * h + 1) ^ sw) << 4));
+      for (int half = 0; half < 2; ++half) {
+        const uint4 c0 = lds128(rec + (uint32_t)(((2 * half) ^ sw) << 4));
+        const uint4 c1 = lds128(rec + (uint32_t)(((2 * half + 1) ^ sw) << 4));
         const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
         uint32_t v[32];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t w4 = w[j] >> 4;
-          v[4 * j + 0] = nib_pair_bf16<0>(w[j], w4);
-          v[4 * j + 1] = nib_pair_bf16<1>(w[j], w4);
-          v[4 * j + 2] = nib_pair_bf16<2>(w[j], w4);
-          v[4 * j + 3] = nib_pair_bf16<3>(w[j], w4);
+        for (int jj = 0; jj < 8; ++jj) {
+          const uint32_t w4 = w[jj] >> 4;
+          v[4 * jj + 0] = nib_pair_bf16<0>(w[jj], w4);
+          v[4 * jj + 1] = nib_pair_bf16<1>(w[jj], w4);
+          v[4 * jj + 2] = nib_pair_bf16<2>(w[jj], w4);
+          v[4 * jj + 3] = nib_pair_bf16<3>(w[jj], w4);
         }
-        tmem_st32(tmem + lane_base + a * 64 + 32 * h, v);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(bar_afull(S, a), 1);
-        if (g > 0) {
-          if (!epilogue(g - 1)) { ok = false; break; }
-          if (prev_last) {
-            if (!emit_unit(A, &s_abort, S, prev, r, h, xph, acc)) { ok = false; break; }
+        tmem_st32(tmem + lane_base + b * 64 + 32 * half, v);
+      }
+      // scales of this row and (one warp) the 64 block sums into side slot j
+      const uint32_t sd = S.side + j * kSideBytes;
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sd + 4 * r), "r"(lds32(st + kOffRec + kNibBytes + 4 * r))
+                   : "memory");
+      if (q == 0) {
+        const uint2 x2 = lds64(st + kOffXs + 8 * lane);
+        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(sd + kM * 4 + 8 * lane), "r"(x2.x), "r"(x2.y)
+                     : "memory");
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_n(bar_afull(S, b), 1);
+        mbar_arrive_n(bar_sfull(S, j), 1);
+      }
+      if (warp == 3 || warp == 7) trace_ev(A, 3, g);
+    }
+  } else {
+    // ---------------- epilogue: per-block scales in fp32, unit results ----------------
+    // warp (q, h): rows 32q .. 32q+31, tokens 32h .. 32h+31 of the token tile
+    const int q = warp & 3, h = (warp - 11) >> 2;
+    const int r = 32 * q + lane;
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    constexpr int kHalf = kTok / 2;
+    float acc[kHalf];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
+    Cursor c;
+    c.start(A, n_units);
+    for (int g = 0; c.valid(n_units); c.next(A, n_units), ++g) {
+      const int b = g % kBufsD, j = g % kSide, nj = g / kSide;
+      if (!warp_wait(A, &s_abort, bar_done(S, g % kStages), done_parity(g), 7) ||
+          !warp_wait(A, &s_abort, bar_sfull(S, j), nj & 1, 12))
+        break;
+      if (warp == 11) trace_ev(A, 4, g);
+      tc_fence_after();
+      const uint32_t sd = S.side + j * kSideBytes;
+      const uint32_t sc = lds32(sd + 4 * r);
+      const float step = bf16_bits_to_f32(sc & 0xFFFFu), mn = bf16_bits_to_f32(sc >> 16);
+#pragma unroll
+      for (int cc = 0; cc < kHalf / 16; ++cc) {
+        uint32_t dv[16], dl[16];
+        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kHalf * h + 16 * cc, dv);
+        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kTok + kHalf * h + 16 * cc, dl);
+        tmem_wait_ld();
+        if (cc == kHalf / 16 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_n(bar_dempty(S, b), 1);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const uint4 x4 = lds128(sd + kM * 4 + 4 * (kHalf * h + 16 * cc + i));
+          const float xs[4] = {__uint_as_float(x4.x), __uint_as_float(x4.y), __uint_as_float(x4.z),
+                               __uint_as_float(x4.w)};
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            float& a = acc[16 * cc + i + jj];
+            a = fmaf(step, __uint_as_float(dv[i + jj]) + __uint_as_float(dl[i + jj]), fmaf(mn, xs[jj], a));
           }
         }
-        prev = U;
-        prev_last = (kb + 1 == U.kb1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_n(bar_sempty(S, j), 1);
+      if (warp == 11) trace_ev(A, 5, g);
+      if (c.kb + 1 == c.U.kb1) {  // unit complete: store its rows
+        const int n = c.U.tile * kM + r;
+        const int tok0 = c.U.tt * kTok + kHalf * h;
+        const int nt = min(kHalf, A.T - tok0);
+        float* o = A.out + (size_t)c.U.split * A.split_stride + (size_t)tok0 * A.ldo + n;
+        if (n < A.N) {
+#pragma unroll
+          for (int i = 0; i < kHalf; ++i) {
+            if (i < nt) *o = acc[i];
+            o += A.ldo;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
       }
     }
-    if (ok && g > 0 && epilogue(g - 1) && prev_last) emit_unit(A, &s_abort, S, prev, r, h, xph, acc);
   }
 
   tc_fence_before();
@@ -503,15 +546,19 @@ __global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G,
 }
 
 // ---------------------------------------------------------------------------------------------
-// Activation staging: for token row t (one CTA of 256 threads), optionally fold split-K partial
-// sums into the residual x (x += sum_s part[s]) and write x back, optionally rms-normalise with
-// gamma (rms_norm, src/llama_engine.cpp:87-115), then write row t of the activation image (bf16
-// hi / lo parts in the swizzled atom layout, and the 128-wide block sums of compute_x_block_sums,
-// :496-521).  K is a multiple of 2048; a thread handles runs of 8 consecutive elements.
+// Activation staging: for token row t (one CTA of 256 threads), form the GEMM input row and write
+// row t of the activation image (bf16 hi / lo parts in the swizzled atom layout, and the 128-wide
+// block sums of compute_x_block_sums, src/llama_engine.cpp:496-521).  The input row is
+//   * x[t] (+ sum_s part[s][t], the split-K partials of the previous projection, folded into the
+//     residual x, which is written back: x += proj, :1024-1025 and :1033-1034), rms-normalised
+//     with gamma when given (rms_norm, :87-115); or
+//   * with gateup != 0: silu(g) * u (:362-491, silu(v) = v / (1 + exp(-v))) from a gate/up GEMM
+//     output row whose 128-column tiles hold 64 gate rows then the 64 matching up rows.
+// K is a multiple of 2048; a thread handles runs of 8 consecutive elements.
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx, const float* __restrict__ part,
                                                   int nsplit, size_t split_stride, const float* __restrict__ gamma,
-                                                  int K, uint8_t* __restrict__ img) {
+                                                  int gateup, int K, uint8_t* __restrict__ img) {
   __shared__ float red[32];
   const int t = blockIdx.x;
   const int runs = K / 2048;  // runs of 8 per thread: 1..4
@@ -522,26 +569,37 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
   for (int j = 0; j < 4; ++j) {
     if (j >= runs) break;
     const int i0 = j * 2048 + threadIdx.x * 8;
-    float* xp = x + (size_t)t * ldx + i0;
-    const float4 a = *reinterpret_cast<const float4*>(xp), b = *reinterpret_cast<const float4*>(xp + 4);
-    float e[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    if (nsplit > 0) {
-      const float* pp = part + (size_t)t * K + i0;
-      float s8[8];
-      {
-        const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
-        s8[0] = p0.x; s8[1] = p0.y; s8[2] = p0.z; s8[3] = p0.w; s8[4] = p1.x; s8[5] = p1.y; s8[6] = p1.z; s8[7] = p1.w;
-      }
-      for (int sp = 1; sp < nsplit; ++sp) {
-        const float4 p0 = *reinterpret_cast<const float4*>(pp + sp * split_stride);
-        const float4 p1 = *reinterpret_cast<const float4*>(pp + sp * split_stride + 4);
-        s8[0] += p0.x; s8[1] += p0.y; s8[2] += p0.z; s8[3] += p0.w;
-        s8[4] += p1.x; s8[5] += p1.y; s8[6] += p1.z; s8[7] += p1.w;
-      }
+    float e[8];
+    if (gateup) {
+      const float* gp = x + (size_t)t * ldx + (i0 >> 6) * 128 + (i0 & 63);
+      const float4 g0 = *reinterpret_cast<const float4*>(gp), g1 = *reinterpret_cast<const float4*>(gp + 4);
+      const float4 u0 = *reinterpret_cast<const float4*>(gp + 64), u1 = *reinterpret_cast<const float4*>(gp + 68);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] += s8[k];
-      *reinterpret_cast<float4*>(xp) = make_float4(e[0], e[1], e[2], e[3]);
-      *reinterpret_cast<float4*>(xp + 4) = make_float4(e[4], e[5], e[6], e[7]);
+      for (int k = 0; k < 8; ++k) e[k] = (g[k] / (1.0f + expf(-g[k]))) * u[k];
+    } else {
+      float* xp = x + (size_t)t * ldx + i0;
+      const float4 a = *reinterpret_cast<const float4*>(xp), b = *reinterpret_cast<const float4*>(xp + 4);
+      e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w; e[4] = b.x; e[5] = b.y; e[6] = b.z; e[7] = b.w;
+      if (nsplit > 0) {
+        const float* pp = part + (size_t)t * K + i0;
+        float s8[8];
+        {
+          const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
+          s8[0] = p0.x; s8[1] = p0.y; s8[2] = p0.z; s8[3] = p0.w; s8[4] = p1.x; s8[5] = p1.y; s8[6] = p1.z; s8[7] = p1.w;
+        }
+        for (int sp = 1; sp < nsplit; ++sp) {
+          const float4 p0 = *reinterpret_cast<const float4*>(pp + sp * split_stride);
+          const float4 p1 = *reinterpret_cast<const float4*>(pp + sp * split_stride + 4);
+          s8[0] += p0.x; s8[1] += p0.y; s8[2] += p0.z; s8[3] += p0.w;
+          s8[4] += p1.x; s8[5] += p1.y; s8[6] += p1.z; s8[7] += p1.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] += s8[k];
+        *reinterpret_cast<float4*>(xp) = make_float4(e[0], e[1], e[2], e[3]);
+        *reinterpret_cast<float4*>(xp + 4) = make_float4(e[4], e[5], e[6], e[7]);
+      }
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -579,14 +637,55 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
     const int kb = i0 >> 7, kk = i0 & 127;
     uint8_t* im = img + ((size_t)tt * kbt + kb) * kImgBytes;
     const int atom = kk >> 6, c = (kk & 63) >> 3;
-    const size_t o = (size_t)atom * kAtom + tr * 128 + ((c ^ (tr & 7)) << 4);
+    const size_t o = (size_t)atom * 2 * kAtom + tr * 128 + ((c ^ (tr & 7)) << 4);
     *reinterpret_cast<uint4*>(im + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(im + 2 * kAtom + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *reinterpret_cast<uint4*>(im + kAtom + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     // 16 threads cover one 128-block
 #pragma unroll
     for (int o2 = 8; o2 > 0; o2 >>= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o2);
     if ((threadIdx.x & 15) == 0) reinterpret_cast<float*>(im + kOffXs)[tr] = bs;
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// RoPE and KV append for token row t of a q | k | v GEMM output (src/llama_engine.cpp:953-956,
+// apply_rope :120-151 with the host-built table), summing its nsplit split-K planes first:
+// rotated q to q_out[t], rotated k and v into the cache row (slot[t], pos[t]).  One CTA of 256
+// threads per token.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float sum_planes(const float* p, int nsplit, size_t stride) {
+  float v = p[0];
+  for (int s = 1; s < nsplit; ++s) v += p[s * stride];
+  return v;
+}
+__global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ qkv, int nsplit, size_t split_stride,
+                                                     int q_dim, int kv_dim, const int32_t* __restrict__ pos,
+                                                     const int32_t* __restrict__ slot, const float* __restrict__ rope_cos,
+                                                     const float* __restrict__ rope_sin, float* __restrict__ q_out,
+                                                     float* __restrict__ kc, float* __restrict__ vc, size_t slot_stride) {
+  const int t = blockIdx.x;
+  const int p = pos[t];
+  const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
+  const size_t cache = (size_t)slot[t] * slot_stride + (size_t)p * kv_dim;
+  const int npairs = (q_dim + kv_dim) / 2;  // rotated pairs (i, i + 32) of the q and k heads
+  for (int j = threadIdx.x; j < npairs; j += blockDim.x) {
+    const int head = j >> 5, i = j & 31;
+    const int base = head * LE_HEAD_DIM + i;  // q heads first, then k heads (row offset q_dim)
+    const float c = rope_cos[p * 32 + i], s = rope_sin[p * 32 + i];
+    const float r0 = sum_planes(row + base, nsplit, split_stride);
+    const float r1 = sum_planes(row + base + 32, nsplit, split_stride);
+    const float o0 = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, s));
+    const float o1 = __fadd_rn(__fmul_rn(r0, s), __fmul_rn(r1, c));
+    if (base < q_dim) {
+      q_out[(size_t)t * q_dim + base] = o0;
+      q_out[(size_t)t * q_dim + base + 32] = o1;
+    } else {
+      kc[cache + base - q_dim] = o0;
+      kc[cache + base - q_dim + 32] = o1;
+    }
+  }
+  for (int j = threadIdx.x; j < kv_dim; j += blockDim.x)
+    vc[cache + j] = sum_planes(row + q_dim + kv_dim + j, nsplit, split_stride);
 }
 
 }  // namespace tc
