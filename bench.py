@@ -311,6 +311,11 @@ def run_ours(args, rank, world, local_rank):
                      "frac": round(step_gbs / peak, 4), "bytes_per_token": int(bytes_tok),
                      "ideal_tok_s_per_gpu": round(peak * 1e9 / bytes_tok, 1)}
 
+    batched = None
+    if rank == 0 and world == 1 and args.b64_steps > 0:
+        eng_b1 = eng
+        batched = run_batched(args, model, shape, local_rank)
+        eng = eng_b1
     trace = None
     if persistent and rank == 0 and args.trace:
         tr = load_package().trace
@@ -340,6 +345,7 @@ def run_ours(args, rank, world, local_rank):
                     "api": "llama_engine_forward_token + llama_engine_sample per step (C ABI via ctypes)",
                     "wall_s": round(wall, 4)},
             "gpu_launches": launches_timed, "decode_path": eng.decode_path, "clocks": clocks,
+            **({"batch64": batched} if batched else {}),
             **({"phase_trace": trace} if trace else {}),
         }
     eng.close()
@@ -347,6 +353,91 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+# ---------------------------------------------------------------------------------------------
+# batched decode (64 sequences) and prefill (8 x 2048 tokens) on the tensor-core batched path
+# ---------------------------------------------------------------------------------------------
+def run_batched(args, model, shape, local_rank):
+    """Batch-64 greedy decode: 64 prompts of 512 ids (fed through forward_batch, 1024 rows per
+    call), then the greedy steps from position 512 on (b64_steps of them; 1536 reaches 2048).
+    Prefill: 8 prompts of 2048 ids through llama_engine_prefill (last-position logits)."""
+    import numpy as np
+    import torch
+
+    pkg = load_package()
+    B, P = 64, 512
+    bindings = pkg.LlamaEngineBindings()
+    eng = pkg.LlamaEngine(str(model), bindings, device=local_rank, max_batch=B, max_seq_len=2048)
+    lib = bindings.lib
+    out = {"batch_path": eng.batch_path}
+    if eng.batch_path != "tensor-core":
+        eng.close()
+        return out
+    stream = torch.cuda.ExternalStream(lib.llama_engine_get_stream(eng.handle))
+    rng = np.random.default_rng(2000 + local_rank)
+    prompts = rng.integers(0, shape.vocab, (B, P)).astype(np.int32)
+    per = 1024 // B
+    for p0 in range(0, P - 1, per):
+        ps = list(range(p0, min(P - 1, p0 + per)))
+        eng.forward_batch([int(prompts[s, p]) for p in ps for s in range(B)], [p for p in ps for s in range(B)],
+                          [s for p in ps for s in range(B)], False)
+    slots = list(range(B))
+    toks = [int(prompts[s, P - 1]) for s in range(B)]
+    pos0 = P - 1
+    steps = max(1, min(args.b64_steps, 2048 - P))
+    # the timed steps start at position 511; warm-up steps run first at the same positions
+    for w in range(3):
+        eng.forward_batch(toks, [pos0 + w] * B, slots, True)
+        eng.argmax_batch(B)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    w0 = time.perf_counter()
+    t = toks
+    for i in range(steps):
+        eng.forward_batch(t, [pos0 + i] * B, slots, True)
+        t = eng.argmax_batch(B)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    ms = ev0.elapsed_time(ev1)
+    peak, peak_kind = hbm_peak()
+    kv_row = shape.layers * shape.kv_dim * 4 * 2
+    step_bytes = [shape.weight_bytes() + B * kv_row * (pos0 + i + 2) for i in range(steps)]
+    gbs = sum(step_bytes) / (ms / 1e3) / 1e9
+    out.update({
+        "value": round(B * steps / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms / steps, 4),
+        "workload": f"decode-b64: {B} sequences, prompts of {P} ids, greedy steps at positions {pos0}..{pos0 + steps - 1}",
+        "e2e": {"value": round(B * steps / wall, 1), "unit": "tok/s", "h2d_bytes_per_step": B * 12,
+                "d2h_bytes_per_step": B * 4, "api": "llama_engine_forward_batch + llama_engine_argmax_batch per step"},
+        "step_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(gbs / peak, 4), "peak_source": peak_kind,
+                          "bytes_per_step": int(sum(step_bytes) / steps)},
+    })
+    # prefill: 8 prompts of 2048 ids, last-position logits
+    n_seq, L = 8, 2048
+    pre = rng.integers(0, shape.vocab, (n_seq, L)).astype(np.int32)
+    eng.prefill([int(x) for x in pre[0]], 0, True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    w0 = time.perf_counter()
+    for sq in range(n_seq):
+        eng.prefill([int(x) for x in pre[sq]], 0, True)
+        eng.sample(0.0, 0.9)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    pwall = time.perf_counter() - w0
+    pms = e0.elapsed_time(e1)
+    flops = n_seq * (2 * shape.layer_matrix_params() * L + shape.layers * 4 * shape.heads * 64 * L * (L + 1) // 2
+                     + 2 * shape.vocab * shape.dim)
+    out["prefill"] = {"value": round(n_seq * L / (pms / 1e3), 1), "unit": "tok/s", "ms_per_seq": round(pms / n_seq, 3),
+                      "workload": f"prefill: {n_seq} sequences of {L} ids, last-position logits + greedy id",
+                      "tflops": round(flops / (pms / 1e3) / 1e12, 2),
+                      "e2e": {"value": round(n_seq * L / pwall, 1), "unit": "tok/s"}}
+    eng.close()
+    return out
 
 
 def read_traffic(kernel_phase: str):
@@ -395,6 +486,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=12)
     ap.add_argument("--ref-max-steps", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--b64-steps", type=int, default=1536,
+                    help="timed batch-64 decode steps from position 511 (0 = skip the batched measurements)")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's phase timeline")
     ap.add_argument("--layers", type=int, default=16,
                     help="layers of the synthetic model (16 = LLaMA-3.2-1B; fewer only for profiling runs)")

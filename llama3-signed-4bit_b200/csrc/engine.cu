@@ -140,6 +140,7 @@ struct TcLayer {
   TcMat qkv, o, gu, d;
 };
 constexpr int kTcMaxSplits = 8;
+constexpr int kAttnMaxSplits = 8;
 
 struct Engine {
   int device = 0;
@@ -216,6 +217,7 @@ struct Engine {
   float* t_qkv = nullptr;    // [kTcMaxSplits][tc_T][dim + 2 kv_dim] q | k | v before RoPE (split-K planes)
   float* t_gu = nullptr;     // [tc_T][2 ffn] gate / up rows, 64-row groups interleaved
   float* t_part = nullptr;   // [kTcMaxSplits][tc_T][dim] split-K partial sums
+  float* t_attn_part = nullptr;  // [tc_T][kv_heads][kAttnMaxSplits][kAttnPart] attention partials
   int32_t* t_idx = nullptr;  // [3][tc_T] token | position | slot of the step's rows
   int32_t* h_idx = nullptr;  // pinned staging of t_idx
   cudaEvent_t idx_ev = nullptr;
@@ -625,6 +627,7 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMalloc(&E->t_qkv, (size_t)kTcMaxSplits * T * (dim + 2 * kvd) * 4));
   LE_CK(cudaMalloc(&E->t_gu, (size_t)T * 2 * ffn * 4));
   LE_CK(cudaMalloc(&E->t_part, (size_t)kTcMaxSplits * T * dim * 4));
+  LE_CK(cudaMalloc(&E->t_attn_part, (size_t)T * E->kv_heads * kAttnMaxSplits * kAttnPart * 4));
   LE_CK(cudaMalloc(&E->t_idx, (size_t)3 * T * 4));
   LE_CK(cudaMallocHost(&E->h_idx, (size_t)3 * T * 4));
   LE_CK(cudaEventCreateWithFlags(&E->idx_ev, cudaEventDisableTiming));
@@ -687,7 +690,9 @@ static bool tc_upload_rows(Engine* E, const int32_t* tok, const int32_t* pos, co
 
 // One forward step of n rows (rows already uploaded).  Logits and greedy ids are produced for
 // rows [lrow0, lrow0 + nlog) into logits rows 0..nlog-1 and am_result[0..nlog-1].
-static bool tc_step(Engine* E, int n, int lrow0, int nlog) {
+// With prefill_p0 >= 0 the rows are consecutive positions prefill_p0 .. of slot 0 (a prefill
+// chunk) and attention runs query-tiled.
+static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int prefill_p0 = -1) {
   using namespace tc;
   const int dim = (int)E->dim, ffn = (int)E->ffn, kvd = (int)E->kv_dim;
   const size_t layer_stride = (size_t)E->max_seq * kvd;
@@ -697,6 +702,8 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog) {
   const int32_t* pos = E->t_idx + n;
   const int32_t* slot = E->t_idx + 2 * n;
   const int tok_tiles = (n + kTok - 1) / kTok;
+  // attention: split each (token, kv head) over position ranges of >= 1024 positions
+  const int attn_splits = std::max(1, std::min(kAttnMaxSplits, (max_pos + 1) / 1024));
   cudaStream_t s = E->stream;
   auto rows = [&](float* out, int ldo, int N, size_t split_stride) {
     Args A{};
@@ -717,14 +724,21 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog) {
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
                              rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
-    k_rope_append<<<n, 256, 0, s>>>(E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q,
-                                    kc, vc, slot_stride);
-    k_attn_batch<<<dim3(n, E->kv_heads), 128, 0, s>>>(E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn);
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
+    k_rope_append<<<dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), 256, 0, s>>>(
+        E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
+    if (prefill_p0 >= 0) {
+      k_attn_prefill<<<dim3(E->kv_heads, (n + 31) / 32), 128, 0, s>>>(E->t_q, dim, kc, vc, kvd, prefill_p0, n,
+                                                                      E->t_attn);
+    } else {
+      k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, 0, s>>>(E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot,
+                                                                      E->t_attn, E->t_attn_part);
+      if (attn_splits > 1) k_attn_combine<<<n, 256, 0, s>>>(E->t_attn_part, E->kv_heads, attn_splits, dim, E->t_attn);
+    }
+    k_tc_stage<<<dim3(n, dim / 2048), 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
     const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
     k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, so, part_stride, D.post_norm, 0, dim, E->img_d);
     tc_launch(E, Y.gu, E->img_d, n, 1, rows(E->t_gu, 2 * ffn, 2 * ffn, 0));
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_gu, 2 * ffn, nullptr, 0, 0, nullptr, 1, ffn, E->img_f);
+    k_tc_stage<<<dim3(n, ffn / 2048), 256, 0, s>>>(E->t_gu, 2 * ffn, nullptr, 0, 0, nullptr, 1, ffn, E->img_f);
     d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), rows(E->t_part, dim, dim, part_stride));
   }
   if (nlog > 0) {
@@ -746,7 +760,7 @@ static bool tc_prefill(Engine* E, const int32_t* ids, size_t count, size_t start
     for (int i = 0; i < n; ++i) pos[i] = (int32_t)(start + c0 + i);
     if (!tc_upload_rows(E, ids + c0, pos.data(), slot.data(), n)) return false;
     const bool lg = last_logits && c0 + n == count;
-    if (!tc_step(E, n, n - 1, lg ? 1 : 0)) return false;
+    if (!tc_step(E, n, n - 1, lg ? 1 : 0, (int)(start + c0) + n - 1, (int)(start + c0))) return false;
   }
   return true;
 }
@@ -892,7 +906,7 @@ static void destroy(Engine* E) {
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
   void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_qkv, E->t_gu, E->t_part,
-                  E->t_idx, E->t_am, E->tc_err};
+                  E->t_idx, E->t_am, E->tc_err, E->t_attn_part};
   for (void* p : tdev) if (p) cudaFree(p);
   if (E->h_idx) cudaFreeHost(E->h_idx);
   if (E->idx_ev) cudaEventDestroy(E->idx_ev);
@@ -1181,7 +1195,7 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
   DeviceGuard dg(E->device);
   if (E->tc) {
     if (!tc_upload_rows(E, tokens, positions, slots, n)) return -1;
-    if (!tc_step(E, n, 0, compute_logits ? n : 0)) return -1;
+    if (!tc_step(E, n, 0, compute_logits ? n : 0, *std::max_element(positions, positions + n))) return -1;
     if (!persistent_ok(E)) return -1;
     E->logits_on_host_fresh = false;
     if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
@@ -1413,7 +1427,7 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     cudaMemsetAsync(err, 0, 16, s);
     QMat W{nibbles, step_bf16, min_bf16, N, K};
     k_tc_repack<<<sms * 8, 256, 0, s>>>(W, recs, 0, kM, 0);
-    k_tc_stage<<<M, 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, 0, K, img);
+    k_tc_stage<<<dim3(M, K / 2048), 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, 0, K, img);
     Args A{};
     A.recs = recs;
     A.img = img;

@@ -26,7 +26,7 @@
 //     apply the block's scales in fp32: acc[t] += min * xs[t] + step * (D[t] + D[64 + t]) (the
 //     reference's factored form); at the end of a unit they store the rows (split-K partials,
 //     projections or logits).
-// A codes have four tensor-memory buffers, accumulators two.
+// A codes have three tensor-memory buffers, accumulators two.
 //
 // Products q * x_hi and q * x_lo are exact in fp32; the only rounding beyond fp32 accumulation
 // is lo's own bf16 rounding (relative 2^-17 of x).
@@ -68,7 +68,7 @@ constexpr int kSide = 8;                 // side ring: per block the rows' scale
 constexpr int kSideBytes = kM * 4 + kTok * 4;
 constexpr int kWarps = 19;               // 0 producer, 1-2 MMA issuers, 3-10 dequantisers, 11-18 epilogue
 constexpr int kThreads = 32 * kWarps;
-constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64 columns each)
+constexpr int kBufsA = 3;                // tensor-memory buffers of A codes (64 columns each)
 constexpr int kBufsD = 2;                // accumulator buffers (128 columns: hi | lo tokens)
 constexpr int kTmemCols = 512;
 constexpr int kDCol = kBufsA * 64;
@@ -554,20 +554,24 @@ __global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G,
 //     with gamma when given (rms_norm, :87-115); or
 //   * with gateup != 0: silu(g) * u (:362-491, silu(v) = v / (1 + exp(-v))) from a gate/up GEMM
 //     output row whose 128-column tiles hold 64 gate rows then the 64 matching up rows.
-// K is a multiple of 2048; a thread handles runs of 8 consecutive elements.
+// K is a multiple of 2048; a thread handles runs of 8 consecutive elements.  Without gamma the
+// grid is (tokens, K / 2048), one 2048-wide run per CTA; with gamma (tokens, 1).
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx, const float* __restrict__ part,
                                                   int nsplit, size_t split_stride, const float* __restrict__ gamma,
                                                   int gateup, int K, uint8_t* __restrict__ img) {
   __shared__ float red[32];
   const int t = blockIdx.x;
-  const int runs = K / 2048;  // runs of 8 per thread: 1..4
+  // runs of 8 elements per thread: j0 .. j1-1 (all K / 2048 runs when normalising, which needs
+  // the whole row; otherwise gridDim.y CTAs share the row, one run each)
+  const int j0 = gamma ? 0 : blockIdx.y;
+  const int j1 = gamma ? K / 2048 : blockIdx.y + 1;
   const int kbt = K >> 7;
   float v[32];
   float ss = 0.0f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    if (j >= runs) break;
+    if (j < j0 || j >= j1) continue;
     const int i0 = j * 2048 + threadIdx.x * 8;
     float e[8];
     if (gateup) {
@@ -612,7 +616,7 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
     const float inv = 1.0f / sqrtf(ss / (float)K + 1e-5f);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (j >= runs) break;
+      if (j < j0 || j >= j1) continue;
       const int i0 = j * 2048 + threadIdx.x * 8;
 #pragma unroll
       for (int k = 0; k < 8; ++k) v[j * 8 + k] = __fmul_rn(__fmul_rn(v[j * 8 + k], gamma[i0 + k]), inv);
@@ -621,7 +625,7 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
   const int tt = t / kTok, tr = t % kTok;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    if (j >= runs) break;
+    if (j < j0 || j >= j1) continue;
     const int i0 = j * 2048 + threadIdx.x * 8;
     uint32_t hw[4], lw[4];
     float bs = 0.0f;
@@ -650,8 +654,8 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
 // ---------------------------------------------------------------------------------------------
 // RoPE and KV append for token row t of a q | k | v GEMM output (src/llama_engine.cpp:953-956,
 // apply_rope :120-151 with the host-built table), summing its nsplit split-K planes first:
-// rotated q to q_out[t], rotated k and v into the cache row (slot[t], pos[t]).  One CTA of 256
-// threads per token.
+// rotated q to q_out[t], rotated k and v into the cache row (slot[t], pos[t]).  Grid (tokens,
+// ceil((q_dim + kv_dim) / 2 + kv_dim) / 256)), one item per thread.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ float sum_planes(const float* p, int nsplit, size_t stride) {
   float v = p[0];
@@ -668,7 +672,15 @@ __global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ q
   const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
   const size_t cache = (size_t)slot[t] * slot_stride + (size_t)p * kv_dim;
   const int npairs = (q_dim + kv_dim) / 2;  // rotated pairs (i, i + 32) of the q and k heads
-  for (int j = threadIdx.x; j < npairs; j += blockDim.x) {
+  // items 0 .. npairs-1 rotate a pair, npairs .. npairs+kv_dim-1 copy a v element; the CTAs of
+  // blockIdx.y split them
+  const int j = blockIdx.y * blockDim.x + threadIdx.x;
+  if (j >= npairs) {
+    const int e = j - npairs;
+    if (e < kv_dim) vc[cache + e] = sum_planes(row + q_dim + kv_dim + e, nsplit, split_stride);
+    return;
+  }
+  {
     const int head = j >> 5, i = j & 31;
     const int base = head * LE_HEAD_DIM + i;  // q heads first, then k heads (row offset q_dim)
     const float c = rope_cos[p * 32 + i], s = rope_sin[p * 32 + i];
@@ -684,8 +696,6 @@ __global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ q
       kc[cache + base - q_dim + 32] = o1;
     }
   }
-  for (int j = threadIdx.x; j < kv_dim; j += blockDim.x)
-    vc[cache + j] = sum_planes(row + q_dim + kv_dim + j, nsplit, split_stride);
 }
 
 }  // namespace tc

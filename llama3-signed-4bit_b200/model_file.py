@@ -55,6 +55,10 @@ class ModelShape:
         per_layer = 2 * self.dim * 4 + sum(mat(n, k) for n, k in self.matrix_shapes())
         return 8 + 28 + self.dim * 4 + self.layers * per_layer + mat(self.vocab, self.dim)
 
+    def layer_matrix_params(self) -> int:
+        """Weights of all layers' matrices (the per-token GEMM work of a forward is 2 flops each)."""
+        return sum(n * k for n, k in self.matrix_shapes()) * self.layers
+
     def weight_bytes(self) -> int:
         """Bytes of all matrices (nibbles + step + min) and norms: streamed once per decode step."""
         mats = sum(n * (k // 128) * 68 for n, k in self.matrix_shapes()) * self.layers

@@ -174,3 +174,29 @@ def test_batched_decode_40_rows(pkg, bindings, small_model, oracle_lib):
         for o in orcs.values():
             oracle_lib.orc_free(o)
         eng.close()
+
+
+def test_long_prefill_and_split_attention(pkg, bindings, small_model, oracle_lib):
+    """1040 prompt tokens in two chunks (query-tiled causal attention, the second chunk over 33
+    key tiles), then two batched decode rows at positions 1040 and 1041: their attention is split
+    over position ranges and merged (k_attn_combine)."""
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    o = oracle_lib.orc_create(str(small_model).encode())
+    try:
+        vocab = eng.vocab_size
+        ids = np.random.default_rng(52).integers(0, vocab, 1040).astype(np.int32)
+        eng.prefill([int(t) for t in ids], 0, True)
+        oracle_lib.orc_prefill(o, fptr(ids), len(ids), 0, 1)
+        assert rel_max_err(eng.get_logits(), _oracle_logits(oracle_lib, o, vocab)) <= LOGIT_RTOL
+        tok = eng.sample(0.0, 0.9)
+        assert tok == oracle_lib.orc_sample_engine(o, ctypes.c_float(0.0), ctypes.c_float(0.9))
+        for pos in (1040, 1041):
+            eng.forward_batch([tok], [pos], [0], True)
+            oracle_lib.orc_forward_token(o, tok, pos, 1)
+            ref = _oracle_logits(oracle_lib, o, vocab)
+            assert rel_max_err(eng.get_logits_batch(0), ref) <= LOGIT_RTOL
+            tok = eng.argmax_batch(1)[0]
+            assert tok == int(np.argmax(ref))
+    finally:
+        oracle_lib.orc_free(o)
+        eng.close()
