@@ -392,6 +392,7 @@ def run_batched(args, model, shape, local_rank):
         eng.argmax_batch(B)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("decode64")  # profiling filter (ncu --nvtx-include "decode64/")
     ev0.record(stream)
     w0 = time.perf_counter()
     t = toks
@@ -401,6 +402,7 @@ def run_batched(args, model, shape, local_rank):
     ev1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
+    torch.cuda.nvtx.range_pop()
     ms = ev0.elapsed_time(ev1)
     peak, peak_kind = hbm_peak()
     kv_row = shape.layers * shape.kv_dim * 4 * 2
@@ -416,11 +418,12 @@ def run_batched(args, model, shape, local_rank):
                           "bytes_per_step": int(sum(step_bytes) / steps)},
     })
     # prefill: 8 prompts of 2048 ids, last-position logits
-    n_seq, L = 8, 2048
+    n_seq, L = max(1, args.prefill_seqs), 2048
     pre = rng.integers(0, shape.vocab, (n_seq, L)).astype(np.int32)
     eng.prefill([int(x) for x in pre[0]], 0, True)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("prefill")
     e0.record(stream)
     w0 = time.perf_counter()
     for sq in range(n_seq):
@@ -429,6 +432,7 @@ def run_batched(args, model, shape, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     pwall = time.perf_counter() - w0
+    torch.cuda.nvtx.range_pop()
     pms = e0.elapsed_time(e1)
     flops = n_seq * (2 * shape.layer_matrix_params() * L + shape.layers * 4 * shape.heads * 64 * L * (L + 1) // 2
                      + 2 * shape.vocab * shape.dim)
@@ -488,6 +492,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--b64-steps", type=int, default=1536,
                     help="timed batch-64 decode steps from position 511 (0 = skip the batched measurements)")
+    ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill measurement: sequences of 2048 ids")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's phase timeline")
     ap.add_argument("--layers", type=int, default=16,
                     help="layers of the synthetic model (16 = LLaMA-3.2-1B; fewer only for profiling runs)")
