@@ -16,17 +16,16 @@
 //     each record's nibbles into bf16 codes q (exact: 0..15), write them into tensor memory
 //     (tcgen05.st) as the MMA's A operand, and pass the block's scales and block sums to the
 //     epilogue through a small side ring;
-//   * warps 1 and 2 (one lane each, alternate blocks) issue, per 16-wide K step, one
-//     tcgen05.mma kind::f16 (M = 128, N = 128)
-//     with A = q from tensor memory and B = the 64 tokens' hi rows stacked on their lo rows, into
-//     an fp32 accumulator D in tensor memory (one per K block): D[t] = sum_k q . x_hi[t],
-//     D[64 + t] = sum_k q . x_lo[t]; the MMAs' completion frees the stage, the A buffer and
-//     signals the accumulator;
+//   * warps 1 and 2 (one lane each, alternate blocks) issue, per 16-wide K step, two
+//     tcgen05.mma kind::f16 (M = 128, N = 64) with A = q from tensor memory and B = the 64
+//     tokens' hi rows, then their lo rows, into one fp32 accumulator D in tensor memory per K
+//     block: D[t] = sum_k q . x_hi[t] + q . x_lo[t]; the MMAs' completion frees the stage, the A
+//     buffer and signals the accumulator;
 //   * warps 11..18 (epilogue, thread = weight row, 32 tokens each) read D back (tcgen05.ld) and
-//     apply the block's scales in fp32: acc[t] += min * xs[t] + step * (D[t] + D[64 + t]) (the
-//     reference's factored form); at the end of a unit they store the rows (split-K partials,
+//     apply the block's scales in fp32: acc[t] += min * xs[t] + step * D[t] (the reference's
+//     factored form); at the end of a unit they store the rows (split-K partials,
 //     projections or logits).
-// A codes have three tensor-memory buffers, accumulators two.
+// A codes and accumulators have four tensor-memory buffers each.
 //
 // Products q * x_hi and q * x_lo are exact in fp32; the only rounding beyond fp32 accumulation
 // is lo's own bf16 rounding (relative 2^-17 of x).
@@ -39,8 +38,8 @@
 // Activation images are written by k_tc_stage: per (token tile, K block) 33024 bytes: four
 // 8192-byte atoms (hi k 0..63, lo k 0..63, hi k 64..127, lo k 64..127), each 64 token rows of
 // 128 bytes with 16-byte chunk c of row t at chunk position c ^ (t & 7) (the 128-byte swizzle
-// of the UMMA canonical K-major layout, 8-row groups 1024 bytes apart; a hi atom and the lo
-// atom after it form one 128-row B operand), then the 64 tokens' block sums (fp32).
+// of the UMMA canonical K-major layout, 8-row groups 1024 bytes apart), then the 64 tokens'
+// block sums (fp32).
 //
 // All mbarrier waits are bounded in time: on timeout the kernel records an error word and every
 // role drains, so the host sees an error instead of a hang.
@@ -68,8 +67,8 @@ constexpr int kSide = 8;                 // side ring: per block the rows' scale
 constexpr int kSideBytes = kM * 4 + kTok * 4;
 constexpr int kWarps = 19;               // 0 producer, 1-2 MMA issuers, 3-10 dequantisers, 11-18 epilogue
 constexpr int kThreads = 32 * kWarps;
-constexpr int kBufsA = 3;                // tensor-memory buffers of A codes (64 columns each)
-constexpr int kBufsD = 2;                // accumulator buffers (128 columns: hi | lo tokens)
+constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64 columns each)
+constexpr int kBufsD = 4;                // accumulator buffers (64 columns: one per token)
 constexpr int kTmemCols = 512;
 constexpr int kDCol = kBufsA * 64;
 constexpr int kPrefetch = 8;             // records prefetched into L2 this many blocks ahead
@@ -355,11 +354,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     if (lane == 0) {
       // ---------------- MMA issuers: warp 1 takes the even blocks, warp 2 the odd ones ----------------
       // (two threads on different SM sub-partitions, so one's waits and bookkeeping overlap the
-      // other's MMAs; each commit tracks its own thread's MMAs).  One MMA per 16-wide K step: B
-      // rows 0..63 are the tokens' hi parts, rows 64..127 their lo parts, so D columns 0..63 and
-      // 64..127 accumulate q . x_hi and q . x_lo.  The loop is kept short: it runs on a sub-
+      // other's MMAs; each commit tracks its own thread's MMAs).  Two MMAs (N = 64) per 16-wide K
+      // step, both into the block's accumulator: B = the tokens' hi parts, then their lo parts,
+      // so D[t] = sum_k q . x_hi[t] + q . x_lo[t].  The loop is kept short: it runs on a sub-
       // partition shared with busy dequant and epilogue warps.
-      const uint32_t idesc = idesc_bf16(2 * kTok);
+      const uint32_t idesc = idesc_bf16(kTok);
       const int nblk = cta_blocks(A, n_units);
       const uint32_t desc_hi = (uint32_t)(sw128_desc(0) >> 32);
       const uint32_t desc_lo0 = (uint32_t)sw128_desc(S.base);
@@ -375,12 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         trace_ev(A, 1, g);
         tc_fence_after();
         const uint32_t dl = desc_lo0 + (uint32_t)(s * (kStageBytes >> 4));
-        const uint32_t d = tmem + kDCol + bd * 2 * kTok;
+        const uint32_t d = tmem + kDCol + bd * kTok;
         const uint32_t a_t = tmem + ba * 64;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint64_t bdesc = ((uint64_t)desc_hi << 32) | (dl + (uint32_t)((((k >> 2) * 2 * kAtom) + (k & 3) * 32) >> 4));
-          tc_mma_ts(d, a_t + 8 * k, bdesc, idesc, k > 0);
+          const uint32_t kl = dl + (uint32_t)((((k >> 2) * 2 * kAtom) + (k & 3) * 32) >> 4);
+          tc_mma_ts(d, a_t + 8 * k, ((uint64_t)desc_hi << 32) | kl, idesc, k > 0);
+          tc_mma_ts(d, a_t + 8 * k, ((uint64_t)desc_hi << 32) | (kl + (kAtom >> 4)), idesc, 1);
         }
         trace_ev(A, 6, g);
         tc_commit(bar_done(S, s));
@@ -470,9 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       const float step = bf16_bits_to_f32(sc & 0xFFFFu), mn = bf16_bits_to_f32(sc >> 16);
 #pragma unroll
       for (int cc = 0; cc < kHalf / 16; ++cc) {
-        uint32_t dv[16], dl[16];
-        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kHalf * h + 16 * cc, dv);
-        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kTok + kHalf * h + 16 * cc, dl);
+        uint32_t dv[16];
+        tmem_ld16(tmem + lane_base + kDCol + b * kTok + kHalf * h + 16 * cc, dv);
         tmem_wait_ld();
         if (cc == kHalf / 16 - 1) {
           tc_fence_before();
@@ -487,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             float& a = acc[16 * cc + i + jj];
-            a = fmaf(step, __uint_as_float(dv[i + jj]) + __uint_as_float(dl[i + jj]), fmaf(mn, xs[jj], a));
+            a = fmaf(step, __uint_as_float(dv[i + jj]), fmaf(mn, xs[jj], a));
           }
         }
       }
