@@ -502,10 +502,19 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.impl == "reference":
-        res = run_reference(args, rank)
-    else:
-        res = run_ours(args, rank, world, local_rank)
+    # libraries (NCCL's version banner, for one) may write to stdout; keep it for the JSON line
+    sys.stdout.flush()
+    saved_stdout = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, rank)
+        else:
+            res = run_ours(args, rank, world, local_rank)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_stdout, 1)
+        os.close(saved_stdout)
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
 
