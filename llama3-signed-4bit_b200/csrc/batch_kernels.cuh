@@ -5,6 +5,8 @@
 // the cache only up to its own position).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "decode_kernels.cuh"
 #include "persistent.cuh"
 
@@ -32,7 +34,7 @@ __global__ void k_embed_batch(QMat E, const int32_t* __restrict__ tok, float* __
 // (src/llama_engine.cpp:958-1021: kv_h = h / 4, s = (q . k) * 0.125, softmax over 0..pos,
 // o = sum p v).  The token's own k / v are already in the cache (written by the RoPE / append
 // kernel).  One CTA of 4 warps per (t, g): the CTA streams 32-position K / V tiles through shared
-// memory (coalesced cp.async, double buffered, rows padded to 68 floats so that 16-byte row reads
+// memory (coalesced cp.async, three tiles in a ring, rows padded to 68 floats so that 16-byte row reads
 // of 8 lanes hit distinct banks) and warp h computes q head h against each tile: lane = position
 // for the scores, lane = dimension pair for p . v.  Softmax runs online (running max and sum,
 // rescaled per tile).
@@ -42,6 +44,7 @@ __global__ void k_embed_batch(QMat E, const int32_t* __restrict__ tok, float* __
 // to part[((t * kv_heads + g) * S + z)][4][66]; k_attn_combine merges them.
 constexpr int kAttnPart = 4 * 66;
 constexpr int kAttnRow = 68;
+constexpr int kAttnSmem = 2 * 3 * 32 * kAttnRow * 4;  // dynamic shared memory of k_attn_batch
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -53,8 +56,10 @@ __global__ void __launch_bounds__(128)
     k_attn_batch(const float* __restrict__ q, int q_dim, const float* __restrict__ kc, const float* __restrict__ vc,
                  size_t slot_stride, int kv_dim, const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
                  float* __restrict__ out, float* __restrict__ part) {
-  __shared__ __align__(16) float sk[2][32][kAttnRow];
-  __shared__ __align__(16) float sv[2][32][kAttnRow];
+  // three-stage ring of K / V tiles (two tiles in flight while one is used)
+  extern __shared__ __align__(16) float attn_smem[];
+  float (*sk)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem);
+  float (*sv)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem + 3 * 32 * kAttnRow);
   __shared__ float4 sp[4][32];  // per warp: this tile's softmax numerators (one head per warp)
   const int t = blockIdx.x, g = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -92,26 +97,30 @@ __global__ void __launch_bounds__(128)
   }
   float m = -INFINITY, l = 0.0f, o0 = 0.0f, o1 = 0.0f;
   if (tile0 < tile1) load_tile(tile0, 0);
+  if (tile0 + 1 < tile1) load_tile(tile0 + 1, 1);
   for (int kt = tile0; kt < tile1; ++kt) {
-    const int buf = (kt - tile0) & 1;
-    if (kt + 1 < tile1) {
-      load_tile(kt + 1, buf ^ 1);
+    const int buf = (kt - tile0) % 3;
+    if (kt + 2 < tile1) {
+      load_tile(kt + 2, (kt - tile0 + 2) % 3);
+      cp_async_wait<2>();
+    } else if (kt + 1 < tile1) {
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    // score of position kt*32 + lane for head h
+    // score of position kt*32 + lane for head h (four partial sums over d mod 4, then added)
     const float4* kr = reinterpret_cast<const float4*>(&sk[buf][lane][0]);
-    float dot = 0.0f;
+    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
 #pragma unroll
     for (int d4 = 0; d4 < 16; ++d4) {
       const float4 k4 = kr[d4];
-      dot = fmaf(qv[4 * d4], k4.x, dot);
-      dot = fmaf(qv[4 * d4 + 1], k4.y, dot);
-      dot = fmaf(qv[4 * d4 + 2], k4.z, dot);
-      dot = fmaf(qv[4 * d4 + 3], k4.w, dot);
+      d0 = fmaf(qv[4 * d4], k4.x, d0);
+      d1 = fmaf(qv[4 * d4 + 1], k4.y, d1);
+      d2 = fmaf(qv[4 * d4 + 2], k4.z, d2);
+      d3 = fmaf(qv[4 * d4 + 3], k4.w, d3);
     }
+    const float dot = (d0 + d1) + (d2 + d3);
     const float s = kt * 32 + lane < P ? dot * 0.125f : -INFINITY;
     const float mn = fmaxf(m, warp_max(s));  // finite: the tile holds a position of the range
     const float alpha = expf(m - mn);
@@ -122,15 +131,19 @@ __global__ void __launch_bounds__(128)
     m = mn;
     reinterpret_cast<float*>(sp[h])[lane] = pe;
     __syncwarp();
-    const float* pw = reinterpret_cast<const float*>(sp[h]);
+    const float4* pw4 = reinterpret_cast<const float4*>(sp[h]);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {  // positions past the range have p = 0
-      const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][j][2 * lane]);
-      const float pj = pw[j];
-      o0 = fmaf(pj, v2.x, o0);
-      o1 = fmaf(pj, v2.y, o1);
+    for (int j4 = 0; j4 < 8; ++j4) {  // positions past the range have p = 0
+      const float4 p4 = pw4[j4];
+      const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][4 * j4 + u][2 * lane]);
+        o0 = fmaf(pj[u], v2.x, o0);
+        o1 = fmaf(pj[u], v2.y, o1);
+      }
     }
-    __syncthreads();  // buffer buf is refilled by the next iteration's load
+    __syncthreads();  // buffer buf is refilled by a later iteration's load
   }
   if (gridDim.z > 1) {
     float* pp = part + ((size_t)(t * gridDim.y + g) * gridDim.z + blockIdx.z) * kAttnPart + h * 66;
@@ -169,119 +182,204 @@ __global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ 
   }
 }
 
-// Causal attention of a prefill chunk: T consecutive tokens of one sequence (cache slot `slot`,
-// positions p0 .. p0+T-1, all already in the cache).  Grid (kv heads, 32-token query tiles); one
-// CTA per (kv head g, query tile):
-// thread = (q head h = warp, token = lane), so a warp's lanes share every k / v element (shared-
-// memory broadcast) and each thread keeps its own q row, o accumulator and online-softmax state
-// (src/llama_engine.cpp:958-1021 per token: s = (q . k) * 0.125, softmax over 0..pos, o = sum p v).
-// K / V tiles of 32 positions stream through shared memory with cp.async double buffering, each
-// read once per 32 queries.
-__global__ void __launch_bounds__(128, 2)
-    k_attn_prefill(const float* __restrict__ q, int q_dim, const float* __restrict__ kc, const float* __restrict__ vc,
-                   int kv_dim, int p0, int T, float* __restrict__ out) {
-  __shared__ __align__(16) float sk[2][32][64];
-  __shared__ __align__(16) float sv[2][32][64];
+// Causal attention of a prefill chunk: T consecutive tokens of one sequence, positions p0 ..
+// p0+T-1, all already in the cache of `kc` / `vc` (src/llama_engine.cpp:958-1021 per token:
+// s = (q . k) * 0.125, softmax over 0..pos, o = sum p v), on the tensor cores (mma.sync m16n8k16,
+// bf16 inputs, fp32 accumulation).  Grid (kv heads, 16-token query tiles), 4 warps;
+// warp w computes q head 4g + w for the tile's 16 tokens (16 MMA rows).  Per 32-position K / V
+// tile: S = Q K^T (4 key groups x 4 dim steps) and O += P V (2 key steps x 8 dim groups), each as
+// three MMAs on bf16 hi / lo parts (hi.hi + hi.lo + lo.hi: x = hi + lo with hi = bf16(x),
+// lo = bf16(x - hi)), so every product carries ~2^-16 relative error at most; online softmax on
+// the S fragments in registers (FlashAttention-2 form).  K / V tiles are converted to bf16 hi / lo
+// in shared memory as they are loaded (V transposed, so both B operands are read as bf16 pairs).
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// hi / lo split of a pair: hi = bf16(x), lo = bf16(x - hi)
+__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = pack_bf16(a - __low2float(h), b - __high2float(h));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr int kPfK = 72;   // bf16 per K row in shared memory (64 + 8 pad: conflict-free pair loads)
+constexpr int kPfV = 40;   // bf16 per transposed V row (32 keys + 8 pad)
+
+__global__ void __launch_bounds__(128)
+    k_attn_prefill_tc(const float* __restrict__ q, int q_dim, const float* __restrict__ kc,
+                      const float* __restrict__ vc, int kv_dim, int p0, int T, float* __restrict__ out) {
+  // [hi, lo][32 keys][kPfK] and [hi, lo][64 dims][kPfV]
+  __shared__ __align__(16) __nv_bfloat16 sk[2][32][kPfK];
+  __shared__ __align__(16) __nv_bfloat16 svt[2][64][kPfV];
   const int g = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the last query tiles see the most keys: launch them first (blockIdx.y = 0 is dispatched
-  // first) so the short ones fill the tail
-  const int tok0 = (gridDim.y - 1 - blockIdx.y) * 32;
-  const int t = min(tok0 + lane, T - 1);          // rows past T repeat the last token, unwritten
-  const int pq = p0 + t;                          // this thread's query position
-  const int p_last = p0 + min(tok0 + 31, T - 1);  // last position any thread of the CTA needs
+  const int h = 4 * g + warp;
+  // the last query tiles see the most keys: blockIdx.y = 0 (dispatched first) takes the last one
+  const int tok0 = (gridDim.y - 1 - blockIdx.y) * 16;
+  const int r0 = lane >> 2, cq = lane & 3;          // fragment row (and row + 8), column pair
+  const int qa = p0 + min(tok0 + r0, T - 1);        // query positions of this thread's two rows
+  const int qb = p0 + min(tok0 + r0 + 8, T - 1);
+  const int p_last = p0 + min(tok0 + 15, T - 1);
   const int ntiles = p_last / 32 + 1;
   const float* Kb = kc + (size_t)g * LE_HEAD_DIM;
   const float* Vb = vc + (size_t)g * LE_HEAD_DIM;
-  // tile loader: 32 rows x 256 bytes of k and of v, 128 threads x 4 x 16 bytes each
-  auto load_tile = [&](int kt, int buf) {
+
+  // Q fragments (A operand, 16 x 64 = 4 k-steps), hi and lo, scaled by 0.125 after the MMA
+  uint32_t qh[4][4], ql[4][4];
+  {
+    const float* qra = q + (size_t)min(tok0 + r0, T - 1) * q_dim + (size_t)h * LE_HEAD_DIM;
+    const float* qrb = q + (size_t)min(tok0 + r0 + 8, T - 1) * q_dim + (size_t)h * LE_HEAD_DIM;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int c0 = 16 * ks + 2 * cq;
+      const float2 a0 = *reinterpret_cast<const float2*>(qra + c0);
+      const float2 a1 = *reinterpret_cast<const float2*>(qrb + c0);
+      const float2 a2 = *reinterpret_cast<const float2*>(qra + c0 + 8);
+      const float2 a3 = *reinterpret_cast<const float2*>(qrb + c0 + 8);
+      split_bf16(a0.x, a0.y, qh[ks][0], ql[ks][0]);
+      split_bf16(a1.x, a1.y, qh[ks][1], ql[ks][1]);
+      split_bf16(a2.x, a2.y, qh[ks][2], ql[ks][2]);
+      split_bf16(a3.x, a3.y, qh[ks][3], ql[ks][3]);
+    }
+  }
+  float o[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[n][i] = 0.0f;
+  float ma = -INFINITY, mb = -INFINITY, la = 0.0f, lb = 0.0f;
+
+  for (int kt = 0; kt < ntiles; ++kt) {
+    __syncthreads();  // the previous tile's shared data is no longer read
+    // load + convert: 32 keys x 64 dims of K and V, 128 threads x 4 float4 each
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int c = threadIdx.x + 128 * i;  // 16-byte chunk 0..511 of the tile
-      const int r = c >> 4, d4 = c & 15;
-      // rows past p_last are masked out; read the last needed row in their place
-      const size_t row = (size_t)min(kt * 32 + r, p_last) * kv_dim + 4 * d4;
-      cp_async16(smem_u32(&sk[buf][r][4 * d4]), Kb + row);
-      cp_async16(smem_u32(&sv[buf][r][4 * d4]), Vb + row);
-    }
-    cp_async_commit();
-  };
-  float qv[64], o[64];
-  {
-    const float4* qp = reinterpret_cast<const float4*>(q + (size_t)t * q_dim + (size_t)(4 * g + warp) * LE_HEAD_DIM);
+      const int c = threadIdx.x + 128 * i;  // float4 chunk 0..511
+      const int key = c >> 4, d = 4 * (c & 15);
+      const size_t row = (size_t)min(kt * 32 + key, p_last) * kv_dim + d;  // rows past p_last are masked
+      const float4 k4 = *reinterpret_cast<const float4*>(Kb + row);
+      const float4 v4 = *reinterpret_cast<const float4*>(Vb + row);
+      uint32_t h0, l0, h1, l1;
+      split_bf16(k4.x, k4.y, h0, l0);
+      split_bf16(k4.z, k4.w, h1, l1);
+      *reinterpret_cast<uint2*>(&sk[0][key][d]) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(&sk[1][key][d]) = make_uint2(l0, l1);
+      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-    for (int d4 = 0; d4 < 16; ++d4) {
-      const float4 v = qp[d4];
-      qv[4 * d4] = v.x; qv[4 * d4 + 1] = v.y; qv[4 * d4 + 2] = v.z; qv[4 * d4 + 3] = v.w;
-    }
-  }
-#pragma unroll
-  for (int d = 0; d < 64; ++d) o[d] = 0.0f;
-  float m = -INFINITY, l = 0.0f;
-  load_tile(0, 0);
-  for (int kt = 0; kt < ntiles; ++kt) {
-    const int buf = kt & 1;
-    if (kt + 1 < ntiles) {
-      load_tile(kt + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat16 vh = __float2bfloat16_rn(vv[e]);
+        svt[0][d + e][key] = vh;
+        svt[1][d + e][key] = __float2bfloat16_rn(vv[e] - __bfloat162float(vh));
+      }
     }
     __syncthreads();
-    // 32 independent dot products (d outer, key inner), each still summed over d in order
-    float sc[32];
+    // S = Q K^T: 4 key groups of 8 (n) x 4 dim steps of 16 (k)
+    float sc[4][4];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) sc[j] = 0.0f;
+    for (int n = 0; n < 4; ++n) {
 #pragma unroll
-    for (int d4 = 0; d4 < 16; ++d4) {
+      for (int i = 0; i < 4; ++i) sc[n][i] = 0.0f;
+      const int key = 8 * n + r0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float4 k4 = *reinterpret_cast<const float4*>(&sk[buf][j][4 * d4]);
-        sc[j] = fmaf(qv[4 * d4], k4.x, sc[j]);
-        sc[j] = fmaf(qv[4 * d4 + 1], k4.y, sc[j]);
-        sc[j] = fmaf(qv[4 * d4 + 2], k4.z, sc[j]);
-        sc[j] = fmaf(qv[4 * d4 + 3], k4.w, sc[j]);
+      for (int ks = 0; ks < 4; ++ks) {
+        const int d = 16 * ks + 2 * cq;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&sk[0][key][d]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&sk[0][key][d + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&sk[1][key][d]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&sk[1][key][d + 8]);
+        mma_bf16(sc[n], qh[ks], bh0, bh1);
+        mma_bf16(sc[n], qh[ks], bl0, bl1);
+        mma_bf16(sc[n], ql[ks], bh0, bh1);
       }
     }
-    float mt = -INFINITY;
+    // scale, causal mask, online softmax (rows r0 -> a, r0 + 8 -> b; a quad shares a row)
+    float mta = -INFINITY, mtb = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      sc[j] = kt * 32 + j <= pq ? sc[j] * 0.125f : -INFINITY;
-      mt = fmaxf(mt, sc[j]);
+    for (int n = 0; n < 4; ++n) {
+      const int key = kt * 32 + 8 * n + 2 * cq;
+      sc[n][0] = key <= qa ? sc[n][0] * 0.125f : -INFINITY;
+      sc[n][1] = key + 1 <= qa ? sc[n][1] * 0.125f : -INFINITY;
+      sc[n][2] = key <= qb ? sc[n][2] * 0.125f : -INFINITY;
+      sc[n][3] = key + 1 <= qb ? sc[n][3] * 0.125f : -INFINITY;
+      mta = fmaxf(mta, fmaxf(sc[n][0], sc[n][1]));
+      mtb = fmaxf(mtb, fmaxf(sc[n][2], sc[n][3]));
     }
-    // tile 0 always holds position 0 <= pq, so m is finite from the first tile on
-    const float mn = fmaxf(m, mt);
-    const float alpha = expf(m - mn);
-    float ls = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      sc[j] = expf(sc[j] - mn);
-      ls += sc[j];
+    for (int off = 1; off <= 2; off <<= 1) {
+      mta = fmaxf(mta, __shfl_xor_sync(0xffffffffu, mta, off));
+      mtb = fmaxf(mtb, __shfl_xor_sync(0xffffffffu, mtb, off));
     }
-    l = l * alpha + ls;
-    m = mn;
+    // tile 0 holds key 0 <= every query position, so the running max is finite from there on
+    const float mna = fmaxf(ma, mta), mnb = fmaxf(mb, mtb);
+    const float alpha_a = expf(ma - mna), alpha_b = expf(mb - mnb);
+    float sa = 0.0f, sb = 0.0f;
 #pragma unroll
-    for (int d = 0; d < 64; ++d) o[d] *= alpha;
+    for (int n = 0; n < 4; ++n) {
+      sc[n][0] = expf(sc[n][0] - mna);
+      sc[n][1] = expf(sc[n][1] - mna);
+      sc[n][2] = expf(sc[n][2] - mnb);
+      sc[n][3] = expf(sc[n][3] - mnb);
+      sa += sc[n][0] + sc[n][1];
+      sb += sc[n][2] + sc[n][3];
+    }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float4* vr = reinterpret_cast<const float4*>(&sv[buf][j][0]);
+    for (int off = 1; off <= 2; off <<= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, off);
+      sb += __shfl_xor_sync(0xffffffffu, sb, off);
+    }
+    la = la * alpha_a + sa;
+    lb = lb * alpha_b + sb;
+    ma = mna;
+    mb = mnb;
 #pragma unroll
-      for (int d4 = 0; d4 < 16; ++d4) {
-        const float4 v4 = vr[d4];
-        o[4 * d4] = fmaf(sc[j], v4.x, o[4 * d4]);
-        o[4 * d4 + 1] = fmaf(sc[j], v4.y, o[4 * d4 + 1]);
-        o[4 * d4 + 2] = fmaf(sc[j], v4.z, o[4 * d4 + 2]);
-        o[4 * d4 + 3] = fmaf(sc[j], v4.w, o[4 * d4 + 3]);
+    for (int n = 0; n < 8; ++n) {
+      o[n][0] *= alpha_a;
+      o[n][1] *= alpha_a;
+      o[n][2] *= alpha_b;
+      o[n][3] *= alpha_b;
+    }
+    // O += P V: P as A fragments (2 key steps of 16: S groups 2j, 2j+1), V^T rows as B
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t ph[4], pl[4];
+      split_bf16(sc[2 * j][0], sc[2 * j][1], ph[0], pl[0]);
+      split_bf16(sc[2 * j][2], sc[2 * j][3], ph[1], pl[1]);
+      split_bf16(sc[2 * j + 1][0], sc[2 * j + 1][1], ph[2], pl[2]);
+      split_bf16(sc[2 * j + 1][2], sc[2 * j + 1][3], ph[3], pl[3]);
+      const int key = 16 * j + 2 * cq;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int d = 8 * n + r0;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&svt[0][d][key]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&svt[0][d][key + 8]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&svt[1][d][key]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&svt[1][d][key + 8]);
+        mma_bf16(o[n], ph, bh0, bh1);
+        mma_bf16(o[n], ph, bl0, bl1);
+        mma_bf16(o[n], pl, bh0, bh1);
       }
     }
-    __syncthreads();  // buffer buf is refilled by the next iteration's load
   }
-  if (tok0 + lane < T) {
-    const float inv = 1.0f / l;
-    float4* op = reinterpret_cast<float4*>(out + (size_t)t * q_dim + (size_t)(4 * g + warp) * LE_HEAD_DIM);
+  // out rows: token tok0 + r0 (c0, c1) and tok0 + r0 + 8 (c2, c3)
+  const float inva = 1.0f / la, invb = 1.0f / lb;
+  const int ta = tok0 + r0, tb = tok0 + r0 + 8;
 #pragma unroll
-    for (int d4 = 0; d4 < 16; ++d4)
-      op[d4] = make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
+  for (int n = 0; n < 8; ++n) {
+    const int d = 8 * n + 2 * cq;
+    if (ta < T)
+      *reinterpret_cast<float2*>(out + (size_t)ta * q_dim + (size_t)h * LE_HEAD_DIM + d) =
+          make_float2(o[n][0] * inva, o[n][1] * inva);
+    if (tb < T)
+      *reinterpret_cast<float2*>(out + (size_t)tb * q_dim + (size_t)h * LE_HEAD_DIM + d) =
+          make_float2(o[n][2] * invb, o[n][3] * invb);
   }
 }
 

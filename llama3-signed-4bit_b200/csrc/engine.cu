@@ -636,6 +636,7 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMalloc(&E->tc_err, 16));
   LE_CK(cudaMemsetAsync(E->tc_err, 0, 16, E->stream));
   LE_CK(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  LE_CK(cudaFuncSetAttribute(k_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
   int per_sm = 0;
   LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm, tc::kThreads, kSmemBytes));
   if (per_sm < 1) {
@@ -727,11 +728,11 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     k_rope_append<<<dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), 256, 0, s>>>(
         E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
     if (prefill_p0 >= 0) {
-      k_attn_prefill<<<dim3(E->kv_heads, (n + 31) / 32), 128, 0, s>>>(E->t_q, dim, kc, vc, kvd, prefill_p0, n,
-                                                                      E->t_attn);
+      k_attn_prefill_tc<<<dim3(E->kv_heads, (n + 15) / 16), 128, 0, s>>>(E->t_q, dim, kc, vc, kvd, prefill_p0, n,
+                                                                         E->t_attn);
     } else {
-      k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, 0, s>>>(E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot,
-                                                                      E->t_attn, E->t_attn_part);
+      k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, kAttnSmem, s>>>(E->t_q, dim, kc, vc, slot_stride, kvd,
+                                                                              pos, slot, E->t_attn, E->t_attn_part);
       if (attn_splits > 1) k_attn_combine<<<n, 256, 0, s>>>(E->t_attn_part, E->kv_heads, attn_splits, dim, E->t_attn);
     }
     k_tc_stage<<<dim3(n, dim / 2048), 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);

@@ -16,16 +16,16 @@
 //     each record's nibbles into bf16 codes q (exact: 0..15), write them into tensor memory
 //     (tcgen05.st) as the MMA's A operand, and pass the block's scales and block sums to the
 //     epilogue through a small side ring;
-//   * warps 1 and 2 (one lane each, alternate blocks) issue, per 16-wide K step, two
-//     tcgen05.mma kind::f16 (M = 128, N = 64) with A = q from tensor memory and B = the 64
-//     tokens' hi rows, then their lo rows, into one fp32 accumulator D in tensor memory per K
-//     block: D[t] = sum_k q . x_hi[t] + q . x_lo[t]; the MMAs' completion frees the stage, the A
-//     buffer and signals the accumulator;
+//   * warp 1 (one lane) issues, per 16-wide K step, one tcgen05.mma kind::f16 (M = 128, N = 128)
+//     with A = q from tensor memory and B = the 64 tokens' hi rows stacked on their lo rows, into
+//     an fp32 accumulator D in tensor memory (one per K block): D[t] = sum_k q . x_hi[t],
+//     D[64 + t] = sum_k q . x_lo[t]; the MMAs' completion frees the stage, the A buffer and
+//     signals the accumulator;
 //   * warps 11..18 (epilogue, thread = weight row, 32 tokens each) read D back (tcgen05.ld) and
-//     apply the block's scales in fp32: acc[t] += min * xs[t] + step * D[t] (the reference's
-//     factored form); at the end of a unit they store the rows (split-K partials,
+//     apply the block's scales in fp32: acc[t] += min * xs[t] + step * (D[t] + D[64 + t]) (the
+//     reference's factored form); at the end of a unit they store the rows (split-K partials,
 //     projections or logits).
-// A codes and accumulators have four tensor-memory buffers each.
+// A codes have four tensor-memory buffers, accumulators two.
 //
 // Products q * x_hi and q * x_lo are exact in fp32; the only rounding beyond fp32 accumulation
 // is lo's own bf16 rounding (relative 2^-17 of x).
@@ -38,8 +38,8 @@
 // Activation images are written by k_tc_stage: per (token tile, K block) 33024 bytes: four
 // 8192-byte atoms (hi k 0..63, lo k 0..63, hi k 64..127, lo k 64..127), each 64 token rows of
 // 128 bytes with 16-byte chunk c of row t at chunk position c ^ (t & 7) (the 128-byte swizzle
-// of the UMMA canonical K-major layout, 8-row groups 1024 bytes apart), then the 64 tokens'
-// block sums (fp32).
+// of the UMMA canonical K-major layout, 8-row groups 1024 bytes apart; a hi atom and the lo atom
+// after it form one 128-row B operand), then the 64 tokens' block sums (fp32).
 //
 // All mbarrier waits are bounded in time: on timeout the kernel records an error word and every
 // role drains, so the host sees an error instead of a hang.
@@ -65,10 +65,10 @@ constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
 constexpr int kStages = 5;
 constexpr int kSide = 8;                 // side ring: per block the rows' scales and the block sums
 constexpr int kSideBytes = kM * 4 + kTok * 4;
-constexpr int kWarps = 19;               // 0 producer, 1-2 MMA issuers, 3-10 dequantisers, 11-18 epilogue
+constexpr int kWarps = 19;               // 0 producer, 1 MMA issuer, 2 idle, 3-10 dequantisers, 11-18 epilogue
 constexpr int kThreads = 32 * kWarps;
 constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64 columns each)
-constexpr int kBufsD = 4;                // accumulator buffers (64 columns: one per token)
+constexpr int kBufsD = 2;                // accumulator buffers (128 columns: hi | lo tokens)
 constexpr int kTmemCols = 512;
 constexpr int kDCol = kBufsA * 64;
 constexpr int kPrefetch = 8;             // records prefetched into L2 this many blocks ahead
@@ -277,9 +277,9 @@ __device__ __forceinline__ int cta_blocks(const Args& A, int n_units) {
   return n;
 }
 
-// Warp roles: 0 = bulk-copy producer (one lane), 1 = tensor-memory owner and MMA issuer of the
-// even blocks (one lane), 2 = MMA issuer of the odd blocks, 3..10 = dequantisers, 11..18 =
-// epilogue.  A warp may only touch tensor-memory lanes 32 * (warp % 4) .. +31, so each group of
+// Warp roles: 0 = bulk-copy producer (one lane), 1 = tensor-memory owner and MMA issuer (one
+// lane), 2 = none (keeps the dequantiser and epilogue groups aligned to the lane quadrants),
+// 3..10 = dequantisers, 11..18 = epilogue.  A warp may only touch tensor-memory lanes 32 * (warp % 4) .. +31, so each group of
 // four covers the 128 rows once; the two dequantiser groups take alternate blocks, the two
 // epilogue groups the two halves of the token tile.
 __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       mbar_init(bar_sfull(S, j), 4);
       mbar_init(bar_sempty(S, j), 8);
     }
-    mbar_init(bar_final(S), 2);
+    mbar_init(bar_final(S), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -350,37 +350,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         wait_bar(A, &s_abort, bar_full(S, s), (last / kStages) & 1, 2);
       }
     }
-  } else if (warp == 1 || warp == 2) {
+  } else if (warp == 1) {
     if (lane == 0) {
-      // ---------------- MMA issuers: warp 1 takes the even blocks, warp 2 the odd ones ----------------
-      // (two threads on different SM sub-partitions, so one's waits and bookkeeping overlap the
-      // other's MMAs; each commit tracks its own thread's MMAs).  Two MMAs (N = 64) per 16-wide K
-      // step, both into the block's accumulator: B = the tokens' hi parts, then their lo parts,
-      // so D[t] = sum_k q . x_hi[t] + q . x_lo[t].  The loop is kept short: it runs on a sub-
-      // partition shared with busy dequant and epilogue warps.
-      const uint32_t idesc = idesc_bf16(kTok);
+      // ---------------- MMA issuer (one thread issues every MMA of the CTA) ----------------
+      // Issuing from two threads that take alternate blocks was measured to corrupt an occasional
+      // block, so a single thread issues all MMAs.  One MMA (N = 128) per 16-wide K step: B rows
+      // 0..63 are the tokens' hi parts, rows 64..127 their lo parts (the adjacent atoms), so D
+      // columns 0..63 and 64..127 accumulate q . x_hi and q . x_lo.  The loop is kept short: it
+      // runs on a sub-partition shared with busy dequant and epilogue warps.
+      const uint32_t idesc = idesc_bf16(2 * kTok);
       const int nblk = cta_blocks(A, n_units);
       const uint32_t desc_hi = (uint32_t)(sw128_desc(0) >> 32);
       const uint32_t desc_lo0 = (uint32_t)sw128_desc(S.base);
-      for (int g = warp - 1; g < nblk; g += 2) {
-        const int s = g % kStages;
+      for (int g = 0; g < nblk; ++g) {
+        const int s = g % kStages, n = g / kStages;
         const int ba = g % kBufsA, na = g / kBufsA, bd = g % kBufsD, nd = g / kBufsD;
-        // afull(g) implies full(g): the dequantisers waited for the stage before arriving
+        // The issuer waits for the stage's bulk copies itself: the MMAs read the stage through the
+        // async proxy, and the copies' completion is only guaranteed visible to them through this
+        // thread's own wait on the full barrier (the dequantisers' later hand-off is not enough).
         trace_ev(A, 8, g);
-        bool ok = wait_bar(A, &s_abort, bar_afull(S, ba), na & 1, 4);
+        bool ok = wait_bar(A, &s_abort, bar_full(S, s), n & 1, 3) && wait_bar(A, &s_abort, bar_afull(S, ba), na & 1, 4);
         trace_ev(A, 9, g);
         ok = ok && (g < kBufsD || wait_bar(A, &s_abort, bar_dempty(S, bd), (nd - 1) & 1, 5));
         if (!ok) break;
         trace_ev(A, 1, g);
         tc_fence_after();
         const uint32_t dl = desc_lo0 + (uint32_t)(s * (kStageBytes >> 4));
-        const uint32_t d = tmem + kDCol + bd * kTok;
+        const uint32_t d = tmem + kDCol + bd * 2 * kTok;
         const uint32_t a_t = tmem + ba * 64;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t kl = dl + (uint32_t)((((k >> 2) * 2 * kAtom) + (k & 3) * 32) >> 4);
           tc_mma_ts(d, a_t + 8 * k, ((uint64_t)desc_hi << 32) | kl, idesc, k > 0);
-          tc_mma_ts(d, a_t + 8 * k, ((uint64_t)desc_hi << 32) | (kl + (kAtom >> 4)), idesc, 1);
         }
         trace_ev(A, 6, g);
         tc_commit(bar_done(S, s));
@@ -390,6 +391,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       tc_commit(bar_final(S));
       wait_bar(A, &s_abort, bar_final(S), 0, 6);
     }
+  } else if (warp == 2) {
+    // no role
   } else if (warp < 11) {
     // ---------------- dequantisers: nibbles -> bf16 codes in tensor memory ----------------
     // two sets of four warps take alternate blocks (set h: blocks g with g % 2 == h), so one
@@ -470,8 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       const float step = bf16_bits_to_f32(sc & 0xFFFFu), mn = bf16_bits_to_f32(sc >> 16);
 #pragma unroll
       for (int cc = 0; cc < kHalf / 16; ++cc) {
-        uint32_t dv[16];
-        tmem_ld16(tmem + lane_base + kDCol + b * kTok + kHalf * h + 16 * cc, dv);
+        uint32_t dv[16], dw[16];
+        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kHalf * h + 16 * cc, dv);
+        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kTok + kHalf * h + 16 * cc, dw);
         tmem_wait_ld();
         if (cc == kHalf / 16 - 1) {
           tc_fence_before();
@@ -486,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             float& a = acc[16 * cc + i + jj];
-            a = fmaf(step, __uint_as_float(dv[i + jj]), fmaf(mn, xs[jj], a));
+            a = fmaf(step, __uint_as_float(dv[i + jj]) + __uint_as_float(dw[i + jj]), fmaf(mn, xs[jj], a));
           }
         }
       }
