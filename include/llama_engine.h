@@ -149,6 +149,20 @@ int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uin
 int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
                     int N, int K, const float* x, int M, float* y, void* stream);
 
+/* Log-likelihood of a token run, for scoring consumers such as the reference's lm-eval adapter
+ * (tests/lm_eval_adapter.py:111-229, which calls forward_token + get_logits per token and forms
+ * log_softmax on the host).  Runs tokens[0..n) through slot 0 at positions start_pos.. (in
+ * chunks of up to 256 on the tensor-core batched path, else token by token), and for
+ * i in [0, n-1) writes out_logprobs[i] = log P(tokens[i+1] | tokens[..i]) computed on the device as
+ * (l[t] - max l) - log(sum exp(l - max l)) over the fp32 logits, and, when out_greedy is not
+ * NULL, out_greedy[i] = 1 if tokens[i+1] is the greedy id of those logits (first index among
+ * equal maxima), else 0.  Afterwards the current logits are those of tokens[n-1], as after
+ * prefill(..., compute_last_logits = 1).  Out-of-range ids count as id 0, as in forward_token.
+ * Returns 0, or -1 on bad arguments (NULL pointers, n < 2, start_pos + n > max_seq_len) or a
+ * device error. */
+int llama_engine_score_tokens(llama_engine_t engine, const int32_t* tokens, size_t n, size_t start_pos,
+                              float* out_logprobs, int32_t* out_greedy);
+
 /* Which implementation runs the slot-0 token steps: 1 = the persistent token-step kernel (one
  * cooperative launch per forward_token, or per whole generate_greedy call; used for dim 2048
  * and ffn_dim in {2048, 4096, 8192}), 0 = the per-phase kernel chain in a CUDA graph (any other

@@ -407,6 +407,61 @@ __global__ void k_argmax_rows_batch(const float* __restrict__ logits, int vocab,
   }
 }
 
+// Log-probability of a target id under one logits row (the lm-eval consumer's formula,
+// tests/lm_eval_adapter.py:175-181: (l[t] - max) - log(sum exp(l - max))) and whether the target
+// is the greedy id (first index among equal maxima).  One CTA of 1024 threads per row; rows with
+// target < 0 are skipped.
+__global__ void __launch_bounds__(1024) k_logprob_rows(const float* __restrict__ logits, int vocab, size_t ld,
+                                                       const int32_t* __restrict__ target,
+                                                       float* __restrict__ out_lp, int32_t* __restrict__ out_greedy) {
+  __shared__ float s_v[32];
+  __shared__ int s_i[32];
+  __shared__ float s_sum[32];
+  const int row = blockIdx.x;
+  const int tgt = target[row];
+  if (tgt < 0) return;
+  const float* l = logits + (size_t)row * ld;
+  float bv = -INFINITY;
+  int bi = kNoIndex;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = l[i];
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) { s_v[wid] = bv; s_i[wid] = bi; }
+  __syncthreads();
+  if (wid == 0) {
+    bv = lane < (int)(blockDim.x >> 5) ? s_v[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x >> 5) ? s_i[lane] : kNoIndex;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { s_v[0] = bv; s_i[0] = bi; }
+  }
+  __syncthreads();
+  const float mx = s_v[0];
+  float se = 0.0f;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) se += expf(l[i] - mx);
+  se = warp_sum(se);
+  if (lane == 0) s_sum[wid] = se;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += s_sum[w];
+    out_lp[row] = (l[tgt] - mx) - logf(tot);
+    if (out_greedy) out_greedy[row] = s_i[0] == tgt ? 1 : 0;
+  }
+}
+
 // result[row] = greedy id of row blockIdx.x from its nparts candidates (0 if none beats -1e30).
 __global__ void k_argmax_finish_batch(const ArgmaxPart* __restrict__ part, int nparts, int32_t* __restrict__ result) {
   __shared__ float s_bv[32];

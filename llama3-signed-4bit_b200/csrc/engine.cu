@@ -141,6 +141,7 @@ struct TcLayer {
 };
 constexpr int kTcMaxSplits = 8;
 constexpr int kAttnMaxSplits = 8;
+constexpr int kScoreRows = 256;  // rows of logits held at once by llama_engine_score_tokens
 
 struct Engine {
   int device = 0;
@@ -225,6 +226,11 @@ struct Engine {
   ArgmaxPart* t_am = nullptr;  // [tc_T][tc_am_parts]
   int tc_am_parts = 0;
   uint32_t* tc_err = nullptr;  // device error word of the tensor-core GEMM
+  // token scoring (llama_engine_score_tokens): logits of a chunk's rows, targets, results
+  float* sc_logits = nullptr;   // [kScoreRows][vocab], allocated on first use
+  int32_t* sc_target = nullptr; // [kScoreRows]
+  float* sc_lp = nullptr;       // [kScoreRows]
+  int32_t* sc_greedy = nullptr; // [kScoreRows]
 
   cudaGraphExec_t g_fwd[2] = {nullptr, nullptr};  // [compute_logits]
   cudaGraphExec_t g_gen = nullptr;                // forward + greedy + advance
@@ -693,7 +699,9 @@ static bool tc_upload_rows(Engine* E, const int32_t* tok, const int32_t* pos, co
 // rows [lrow0, lrow0 + nlog) into logits rows 0..nlog-1 and am_result[0..nlog-1].
 // With prefill_p0 >= 0 the rows are consecutive positions prefill_p0 .. of slot 0 (a prefill
 // chunk) and attention runs query-tiled.
-static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int prefill_p0 = -1) {
+static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int prefill_p0 = -1,
+                    float* logits_out = nullptr) {
+  float* const lg_out = logits_out ? logits_out : E->logits;
   using namespace tc;
   const int dim = (int)E->dim, ffn = (int)E->ffn, kvd = (int)E->kv_dim;
   const size_t layer_stride = (size_t)E->max_seq * kvd;
@@ -745,9 +753,11 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
   if (nlog > 0) {
     k_tc_stage<<<nlog, 256, 0, s>>>(E->t_x + (size_t)lrow0 * dim, dim, E->t_part + (size_t)lrow0 * dim, d_splits,
                                      part_stride, E->final_norm, 0, dim, E->img_d);
-    tc_launch(E, E->tc_lm, E->img_d, nlog, 1, rows(E->logits, (int)E->vocab, (int)E->vocab, 0));
-    k_argmax_rows_batch<<<dim3(E->tc_am_parts, nlog), 256, 0, s>>>(E->logits, (int)E->vocab, E->vocab, E->t_am);
-    k_argmax_finish_batch<<<nlog, 256, 0, s>>>(E->t_am, E->tc_am_parts, E->am_result);
+    tc_launch(E, E->tc_lm, E->img_d, nlog, 1, rows(lg_out, (int)E->vocab, (int)E->vocab, 0));
+    if (!logits_out) {
+      k_argmax_rows_batch<<<dim3(E->tc_am_parts, nlog), 256, 0, s>>>(E->logits, (int)E->vocab, E->vocab, E->t_am);
+      k_argmax_finish_batch<<<nlog, 256, 0, s>>>(E->t_am, E->tc_am_parts, E->am_result);
+    }
   }
   LE_CK(cudaGetLastError());
   return true;
@@ -907,7 +917,8 @@ static void destroy(Engine* E) {
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
   void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_qkv, E->t_gu, E->t_part,
-                  E->t_idx, E->t_am, E->tc_err, E->t_attn_part};
+                  E->t_idx, E->t_am, E->tc_err, E->t_attn_part, E->sc_logits, E->sc_target, E->sc_lp,
+                  E->sc_greedy};
   for (void* p : tdev) if (p) cudaFree(p);
   if (E->h_idx) cudaFreeHost(E->h_idx);
   if (E->idx_ev) cudaEventDestroy(E->idx_ev);
@@ -1316,6 +1327,74 @@ LE_API const float* llama_engine_get_logits_batch(llama_engine_t engine, int row
   if (cudaStreamSynchronize(E->stream) != cudaSuccess) return nullptr;
   if (row == 0) E->logits_on_host_fresh = true;
   return h;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Token scoring for log-likelihood consumers (the lm-eval adapter pattern,
+// tests/lm_eval_adapter.py:111-229): one pass over a token run on slot 0, log-probabilities of
+// each next token computed on the device.
+// ---------------------------------------------------------------------------------------------
+static bool score_alloc(Engine* E) {
+  if (E->sc_logits) return true;
+  LE_CK(cudaMalloc(&E->sc_logits, (size_t)kScoreRows * E->vocab * 4));
+  LE_CK(cudaMalloc(&E->sc_target, kScoreRows * 4));
+  LE_CK(cudaMalloc(&E->sc_lp, kScoreRows * 4));
+  LE_CK(cudaMalloc(&E->sc_greedy, kScoreRows * 4));
+  return true;
+}
+
+LE_API int llama_engine_score_tokens(llama_engine_t engine, const int32_t* tokens, size_t n, size_t start_pos,
+                                     float* out_logprobs, int32_t* out_greedy) {
+  if (!engine || !tokens || !out_logprobs || n < 2) return -1;
+  Engine* E = H(engine);
+  if (start_pos + n > (size_t)E->max_seq) { E->err = "score_tokens: positions exceed max_seq_len"; return -1; }
+  DeviceGuard dg(E->device);
+  if (!score_alloc(E)) return -1;
+  std::vector<int32_t> ids(n), pos(n), slot(n, 0), tgt(kScoreRows);
+  for (size_t i = 0; i < n; ++i) {
+    ids[i] = (tokens[i] < 0 || tokens[i] >= (int32_t)E->vocab) ? 0 : tokens[i];
+    pos[i] = (int32_t)(start_pos + i);
+  }
+  const int chunk = E->tc ? std::min(E->tc_T, kScoreRows) : 1;
+  for (size_t c0 = 0; c0 < n; c0 += (size_t)chunk) {
+    const int m = (int)std::min<size_t>((size_t)chunk, n - c0);
+    if (E->tc) {
+      if (!tc_upload_rows(E, ids.data() + c0, pos.data() + c0, slot.data(), m)) return -1;
+      if (!tc_step(E, m, 0, m, pos[c0 + m - 1], pos[c0], E->sc_logits)) return -1;
+    } else {
+      if (!forward_token(E, ids[c0], (size_t)pos[c0], true)) return -1;
+      if (cudaMemcpyAsync(E->sc_logits, E->logits, (size_t)E->vocab * 4, cudaMemcpyDeviceToDevice, E->stream) !=
+          cudaSuccess)
+        return -1;
+    }
+    // row i scores token c0 + i + 1 (the run's last token has no successor)
+    for (int i = 0; i < m; ++i) tgt[i] = c0 + i + 1 < n ? ids[c0 + i + 1] : -1;
+    if (cudaMemcpyAsync(E->sc_target, tgt.data(), (size_t)m * 4, cudaMemcpyHostToDevice, E->stream) != cudaSuccess)
+      return -1;
+    k_logprob_rows<<<m, 1024, 0, E->stream>>>(E->sc_logits, (int)E->vocab, E->vocab, E->sc_target, E->sc_lp,
+                                                E->sc_greedy);
+    const int k = (int)std::min<size_t>((size_t)m, n - 1 - c0);
+    if (k > 0) {
+      if (cudaMemcpyAsync(out_logprobs + c0, E->sc_lp, (size_t)k * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess)
+        return -1;
+      if (out_greedy &&
+          cudaMemcpyAsync(out_greedy + c0, E->sc_greedy, (size_t)k * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess)
+        return -1;
+    }
+    if (c0 + m == n) {  // the last token's logits become the current logits (as after prefill)
+      if (cudaMemcpyAsync(E->logits, E->sc_logits + (size_t)(m - 1) * E->vocab, (size_t)E->vocab * 4,
+                          cudaMemcpyDeviceToDevice, E->stream) != cudaSuccess)
+        return -1;
+    }
+    // tgt and the host outputs are reused / read by the caller: finish the chunk
+    cudaError_t ce = cudaStreamSynchronize(E->stream);
+    if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
+  }
+  if (!persistent_ok(E)) return -1;
+  E->logits_on_host_fresh = false;
+  E->argmax_valid = false;
+  E->have_logits = true;
+  return 0;
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -89,6 +89,8 @@ class LlamaEngineBindings:
         lib.llama_engine_argmax_batch.restype = ctypes.c_int
         lib.llama_engine_get_logits_batch.argtypes = [_P, ctypes.c_int]
         lib.llama_engine_get_logits_batch.restype = _FP
+        lib.llama_engine_score_tokens.argtypes = [_P, _I32P, ctypes.c_size_t, ctypes.c_size_t, _FP, _I32P]
+        lib.llama_engine_score_tokens.restype = ctypes.c_int
         lib.llama_b128_gemv.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P]
         lib.llama_b128_gemv.restype = ctypes.c_int
         lib.llama_b128_gemm.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P]
@@ -225,6 +227,20 @@ class LlamaEngine:
         if not ptr:
             raise RuntimeError("get_logits_batch failed")
         return np.ctypeslib.as_array(ptr, shape=(self.vocab_size,)).copy()
+
+    def score_tokens(self, tokens, start_pos: int = 0) -> tuple[np.ndarray, np.ndarray]:
+        """Log P(tokens[i+1] | tokens[..i]) for i < len(tokens)-1 and the per-position greedy
+        flags, computed on the device (the scoring loop of the reference's
+        tests/lm_eval_adapter.py:160-190 without a logits copy per token)."""
+        n = len(tokens)
+        t = (ctypes.c_int32 * n)(*tokens)
+        lp = np.zeros(max(n - 1, 1), dtype=np.float32)
+        gr = np.zeros(max(n - 1, 1), dtype=np.int32)
+        self._check(self.bindings.lib.llama_engine_score_tokens(self.handle, t, n, start_pos,
+                                                                lp.ctypes.data_as(_FP),
+                                                                gr.ctypes.data_as(_I32P)),
+                    "score_tokens")
+        return lp[:n - 1], gr[:n - 1].astype(bool)
 
     @property
     def decode_path(self) -> str:
