@@ -8,7 +8,7 @@ build and weight-file tooling.
 The directory name is not a Python identifier; import it as ``llama3_signed_4bit_b200`` through
 ``load_package()`` in ``__graft_entry__.py`` or the test suite's conftest.
 """
-from . import build, model_file, scoring, trace  # noqa: F401
+from . import build, convert, model_file, scoring, trace  # noqa: F401
 from .engine import (  # noqa: F401
     LlamaEngine,
     LlamaEngineBindings,

@@ -110,10 +110,12 @@ static void quantise_row(const float* w, int K, uint8_t* nib, uint16_t* step, ui
 }
 
 /* Weight distributions */
-enum { DIST_NORMAL = 0, DIST_UNIFORM_CODES = 1 };
+enum { DIST_NORMAL = 0, DIST_UNIFORM_CODES = 1, DIST_SOURCE = 2 };
 
 typedef struct {
-    int dist;          /* DIST_NORMAL: w ~ N(0, sigma) then quantised; DIST_UNIFORM_CODES: see below */
+    int dist;          /* DIST_NORMAL: w ~ N(0, sigma) then quantised; DIST_UNIFORM_CODES: see below;
+                          DIST_SOURCE: rows of src quantised */
+    const float* src;  /* DIST_SOURCE: N x K row-major weights */
     double sigma;
     uint64_t seed, tensor;
     int N, K;
@@ -133,7 +135,9 @@ static void* mat_worker(void* arg) {
         uint8_t* nib = j->nib + (size_t)n * (j->K / 2);
         uint16_t* st = j->step + (size_t)n * nb;
         uint16_t* mn = j->mn + (size_t)n * nb;
-        if (j->dist == DIST_NORMAL) {
+        if (j->dist == DIST_SOURCE) {
+            quantise_row(j->src + (size_t)n * j->K, j->K, nib, st, mn);
+        } else if (j->dist == DIST_NORMAL) {
             for (int k = 0; k < j->K; ++k) w[k] = (float)(rng_normal(&g) * j->sigma);
             quantise_row(w, j->K, nib, st, mn);
         } else {
@@ -163,18 +167,23 @@ static int n_threads_default(void) {
     return (int)n;
 }
 
-static void gen_matrix(int dist, double sigma, uint64_t seed, uint64_t tensor, int N, int K,
-                       uint8_t* nib, uint16_t* step, uint16_t* mn, int threads) {
+static void gen_matrix_src(int dist, const float* src, double sigma, uint64_t seed, uint64_t tensor, int N,
+                           int K, uint8_t* nib, uint16_t* step, uint16_t* mn, int threads) {
     if (threads <= 0) threads = n_threads_default();
     if (threads > N) threads = N > 0 ? N : 1;
     pthread_t tid[64];
     mat_job_t jobs[64];
     for (int t = 0; t < threads; ++t) {
-        jobs[t] = (mat_job_t){dist, sigma, seed, tensor, N, K, nib, step, mn,
+        jobs[t] = (mat_job_t){dist, src, sigma, seed, tensor, N, K, nib, step, mn,
                               (int)((int64_t)N * t / threads), (int)((int64_t)N * (t + 1) / threads)};
         pthread_create(&tid[t], NULL, mat_worker, &jobs[t]);
     }
     for (int t = 0; t < threads; ++t) pthread_join(tid[t], NULL);
+}
+
+static void gen_matrix(int dist, double sigma, uint64_t seed, uint64_t tensor, int N, int K,
+                       uint8_t* nib, uint16_t* step, uint16_t* mn, int threads) {
+    gen_matrix_src(dist, NULL, sigma, seed, tensor, N, K, nib, step, mn, threads);
 }
 
 /* ---------------------------------------------------------------------------------------- */
@@ -186,6 +195,14 @@ int llm4s128_gen_matrix(int dist, double sigma, uint64_t seed, uint64_t tensor, 
                         uint8_t* nib, uint16_t* step, uint16_t* mn) {
     if (N <= 0 || K <= 0 || K % 128 != 0 || !nib || !step || !mn) return -1;
     gen_matrix(dist, sigma, seed, tensor, N, K, nib, step, mn, 0);
+    return 0;
+}
+
+/* Quantises an N x K row-major fp32 matrix (K % 128 == 0) with the affine block rule above,
+ * rows spread over threads (the output does not depend on the thread count). */
+int llm4s128_quantize(const float* w, int N, int K, uint8_t* nib, uint16_t* step, uint16_t* mn) {
+    if (!w || N <= 0 || K <= 0 || K % 128 != 0 || !nib || !step || !mn) return -1;
+    gen_matrix_src(DIST_SOURCE, w, 0.0, 0, 0, N, K, nib, step, mn, 0);
     return 0;
 }
 

@@ -84,6 +84,9 @@ def _gen_lib():
                                             ctypes.c_uint64, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.llm4s128_gen_matrix.restype = ctypes.c_int
+        lib.llm4s128_quantize.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_void_p]
+        lib.llm4s128_quantize.restype = ctypes.c_int
         _lib = lib
     return _lib
 
@@ -128,6 +131,26 @@ def gen_matrix(N: int, K: int, seed: int, tensor: int = 0, uniform_codes: bool =
     if rc != 0:
         raise RuntimeError("llm4s128_gen_matrix failed")
     return nib, step, mn
+
+
+def quantize(w: np.ndarray) -> dict:
+    """Affine block-128 quantisation of an N x K fp32 matrix (K % 128 == 0): per block of 128
+    weights of a row, min = block minimum and step = (max - min)/15, both rounded to bf16 (nearest
+    even), q = clamp(rint((w - min)/step), 0, 15).  Returns the matrix record of the file
+    ({"N", "K", "nib", "step", "min"})."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    if w.ndim != 2 or w.shape[1] % 128 != 0 or w.shape[0] == 0:
+        raise ValueError(f"quantize: need an N x K matrix with K % 128 == 0, got {w.shape}")
+    if not np.isfinite(w).all():
+        raise ValueError("quantize: non-finite weights")
+    N, K = w.shape
+    nb = N * (K // 128)
+    nib = np.empty(nb * 64, dtype=np.uint8)
+    step = np.empty(nb, dtype=np.uint16)
+    mn = np.empty(nb, dtype=np.uint16)
+    if _gen_lib().llm4s128_quantize(w.ctypes.data, N, K, nib.ctypes.data, step.ctypes.data, mn.ctypes.data) != 0:
+        raise RuntimeError("llm4s128_quantize failed")
+    return {"N": N, "K": K, "nib": nib, "step": step, "min": mn}
 
 
 def bf16_to_f32(a: np.ndarray) -> np.ndarray:
