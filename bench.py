@@ -319,7 +319,7 @@ def run_ours(args, rank, world, local_rank):
     trace = None
     if persistent and rank == 0 and args.trace:
         tr = load_package().trace
-        trace = tr.capture(eng, first, start)
+        trace = tr.capture(eng, first, start, args.trace_raw)
     result = None
     if rank == 0:
         kernels_per_token = 1 + 5 * shape.layers + 2
@@ -494,6 +494,7 @@ def main():
                     help="timed batch-64 decode steps from position 511 (0 = skip the batched measurements)")
     ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill measurement: sequences of 2048 ids")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's phase timeline")
+    ap.add_argument("--trace-raw", default=None, help="with --trace: save the raw trace array (.npy) here")
     ap.add_argument("--layers", type=int, default=16,
                     help="layers of the synthetic model (16 = LLaMA-3.2-1B; fewer only for profiling runs)")
     args = ap.parse_args()

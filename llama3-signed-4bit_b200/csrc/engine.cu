@@ -375,12 +375,16 @@ static bool init_persistent(Engine* E) {
   if (!persistent_supported(E)) return true;
   const int L = (int)E->layers, G = E->num_sms;
   const size_t smem = persistent_smem();
-  LE_CK(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  LE_CK(cudaFuncSetAttribute(k_decode_persistent<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  LE_CK(cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, kPThreads, smem));
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent<false>, kPThreads, smem));
+  int per_sm_trace = 0;
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_trace, k_decode_persistent<true>, kPThreads, smem));
+  per_sm = std::min(per_sm, per_sm_trace);
   if (per_sm < 1) {  // keep the kernel-chain path, and say why
     cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, k_decode_persistent);
+    cudaFuncGetAttributes(&fa, k_decode_persistent<false>);
     E->err = "persistent kernel declined: 0 resident CTAs per SM (regs " + std::to_string(fa.numRegs) +
              ", static smem " + std::to_string(fa.sharedSizeBytes) + ", dynamic smem " + std::to_string(smem) +
              ", max threads " + std::to_string(fa.maxThreadsPerBlock) + ")";
@@ -418,6 +422,20 @@ static bool init_persistent(Engine* E) {
 
   // ---- static schedule ----
   struct CtaLists { std::vector<PSeg> segs; std::vector<PItem> items; std::vector<uint32_t> recs; };
+  // Work units per record for a segment of n_rec records: the split (block ranges of 16/split
+  // blocks) that minimises the busiest warp's (units x (blocks per unit + 2)), the 2 standing
+  // for a unit's fixed cost, within the shared-memory room for unit partials.
+  auto choose_split = [](int n_rec) -> int {
+    int best = 1, best_cost = 1 << 30;
+    for (int sp = 1; sp <= 16; sp *= 2) {
+      if (n_rec * sp > kMaxUnits) break;
+      const int units_per_warp = (n_rec * sp + kPConsumerWarps - 1) / kPConsumerWarps;
+      const int cost = units_per_warp * (16 / sp + 2);
+      if (cost < best_cost) { best_cost = cost; best = sp; }
+    }
+    return best;
+  };
+  bool split_ok = true;
   std::vector<CtaLists> C(G);
   std::vector<int> warp_rr(G, 0);
   int rot = 0;
@@ -442,6 +460,9 @@ static bool init_persistent(Engine* E) {
         C[c].items.push_back(it);
       }
       sg.item_end = (uint16_t)C[c].items.size();
+      const int n_rec = (int)per[c].size() * nrec_per_item;
+      sg.split = (uint8_t)choose_split(n_rec);
+      if (n_rec * sg.split > kMaxUnits) split_ok = false;
       C[c].segs.push_back(sg);
     }
   };
@@ -479,7 +500,7 @@ static bool init_persistent(Engine* E) {
     for (const auto& sg : C[c].segs)
       if (sg.kind == PK_LMHEAD) ++n_lm_ctas;
   for (int c = 0; c < G; ++c) {
-    if (C[c].recs.size() > (size_t)kMaxRecs || C[c].items.size() > (size_t)kMaxItems ||
+    if (!split_ok || C[c].recs.size() > (size_t)kMaxRecs || C[c].items.size() > (size_t)kMaxItems ||
         C[c].segs.size() > (size_t)kMaxSegs) {
       E->err = "persistent kernel declined: a CTA's schedule exceeds its shared-memory capacity";
       cudaFree(E->rec_arena);
@@ -554,7 +575,8 @@ static bool launch_persistent(Engine* E, int n_tokens, bool logits) {
   A.n_tokens = n_tokens;
   A.do_logits = logits ? 1 : 0;
   void* args[] = {&A};
-  LE_CK(cudaLaunchCooperativeKernel((const void*)k_decode_persistent, dim3(E->p_grid), dim3(kPThreads), args,
+  const void* fn = A.trace ? (const void*)k_decode_persistent<true> : (const void*)k_decode_persistent<false>;
+  LE_CK(cudaLaunchCooperativeKernel(fn, dim3(E->p_grid), dim3(kPThreads), args,
                                     persistent_smem(), E->stream));
   return true;
 }

@@ -41,7 +41,9 @@ constexpr int kRecNibBytes = 16384;
 constexpr int kPConsumerWarps = 16;
 constexpr int kPThreads = 32 * kPConsumerWarps;
 constexpr int kRingSlots = 10;
-constexpr int kMiscFloats = 2304;          // attention scratch (q, k, v, reductions, 32x64 partials)
+constexpr int kMiscFloats = 2304;          // attention scratch (q, k, v, reductions, 32x64 partials),
+                                           // or the row partials of a segment's work units
+constexpr int kMaxUnits = kMiscFloats / 16;  // work units per segment
 constexpr int kImageBytes = 32768 + 1024;  // digit fragments for K <= 8192, or attention scores
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every wait
 constexpr int kTraceCap = 1024;
@@ -60,7 +62,8 @@ struct PItem {
 };
 
 struct PSeg {
-  uint8_t kind, pad;
+  uint8_t kind;
+  uint8_t split;      // work units per record (1, 2, 4, 8 or 16 block ranges)
   uint16_t layer;
   uint16_t item_begin, item_end;
 };
@@ -140,9 +143,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
 }
 __device__ __forceinline__ void mbar_arrive_n(uint32_t a, uint32_t n) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(n) : "memory");
-}
-__device__ __forceinline__ void group_sync(int group, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(2 + group), "r"(nthreads) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
   uint32_t ok;
@@ -270,6 +270,38 @@ __device__ __forceinline__ void ld_tagged(const PArgs& A, const unsigned long lo
   for (int i = 0; i < 2 * N2; ++i) out[i] = tag_val(w[i]);
 }
 
+// Two groups of 8 tagged words (p and q) loaded together, so both take one round trip.
+__device__ __forceinline__ void ld_tagged2x(const PArgs& A, const unsigned long long* p, const unsigned long long* q,
+                                            uint32_t tag, float* out0, float* out1, uint32_t where) {
+  unsigned long long w[16];
+  auto load = [&]() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ld_tag2(p + 2 * i, w[2 * i], w[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ld_tag2(q + 2 * i, w[8 + 2 * i], w[8 + 2 * i + 1]);
+  };
+  auto all_ok = [&]() {
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ok &= tag_of(w[i]) == tag;
+    return ok;
+  };
+  load();
+  if (!all_ok()) {
+    const unsigned long long t0 = gtimer();
+    while (true) {
+      load();
+      if (all_ok() || failed(A)) break;
+      if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    out0[i] = tag_val(w[i]);
+    out1[i] = tag_val(w[8 + i]);
+  }
+}
+
 __device__ __forceinline__ float ld_tagged1(const PArgs& A, const unsigned long long* p, uint32_t tag, uint32_t where) {
   unsigned long long w = ld_tag(p);
   if (tag_of(w) != tag) {
@@ -394,8 +426,8 @@ __device__ __forceinline__ void stage_plain(const PArgs& A, const unsigned long 
   const int tid = threadIdx.x;
   const int ngroups = K / 8;
   float v0[8], v1[8];
-  if (tid < ngroups) ld_tagged<4>(A, x + 8 * tid, tag, v0, where);
-  if (tid + 512 < ngroups) ld_tagged<4>(A, x + 8 * (tid + 512), tag, v1, where);
+  if (tid + 512 < ngroups) ld_tagged2x(A, x + 8 * tid, x + 8 * (tid + 512), tag, v0, v1, where);
+  else if (tid < ngroups) ld_tagged<4>(A, x + 8 * tid, tag, v0, where);
   if (tid < ngroups) stage_group(v0, tid, S);
   if (tid + 512 < ngroups) stage_group(v1, tid + 512, S);
   consumer_sync();
@@ -483,137 +515,181 @@ __device__ __forceinline__ void record_blocks(int F, const uint8_t* rec, int kq,
   }
 }
 
+// Trace entry: (%globaltimer ns or `value`, tag | low 32 bits of the SM clock << 32).  The clock
+// gives cycle-exact intervals within a CTA; the global timer orders events across CTAs.
+template <bool kTrace>
+__device__ __forceinline__ void trace_mark(const PArgs& A, int& n, int tok, uint32_t tag,
+                                           unsigned long long value = 0ull) {
+  if (kTrace && A.trace != nullptr && tok == 0 && n < kTraceCap) {
+    unsigned long long* tr = A.trace + ((size_t)blockIdx.x * kTraceCap + n) * 2;
+    tr[0] = value ? value : gtimer();
+    tr[1] = (unsigned long long)tag | ((unsigned long long)(uint32_t)clock64() << 32);
+    ++n;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Attention of one head on the CTA (src/llama_engine.cpp:953-1021): RoPE from the table, KV
 // append at pos (by the first q head of each kv group), softmax over 0..pos, PV.
+// Flash-decoding inside the CTA: warp w takes positions base + w + 16 i (i < kAttnP) of each
+// 64-position chunk, lane d holds dims 2d and 2d+1; every warp keeps a running max, sum and
+// output row, and the 16 warps are merged at the end.  The cached K and V rows do not depend on
+// this step, so before the wait for q, k and v the first chunk's rows are loaded into registers
+// and the second chunk's into shared memory (cp.async); later chunks are prefetched into L2.
 // ---------------------------------------------------------------------------------------------
-__device__ void attention_head(const PArgs& A, int l, int h, int pos, uint32_t s, float* scores, float* sm) {
-  const int tid = threadIdx.x;
+constexpr int kAttnP = 4;                           // positions per warp per chunk
+constexpr int kAttnChunk = kAttnP * kPConsumerWarps;
+
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+template <bool kTrace>
+__device__ void attention_head(const PArgs& A, int l, int h, int pos, uint32_t s, float* sm, float* img, int& ntr,
+                               int tok) {
+  const bool fine = kTrace && threadIdx.x == 0 && (l == 1 || l == 2);
+  const uint32_t ftag = ((uint32_t)PK_ATTN << 8) | (uint32_t)l;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   constexpr int NT = kPThreads;
   const int group = A.heads / A.kv_heads, kvh = h / group;
   const int kv_dim = A.kv_heads * LE_HEAD_DIM, q_dim = A.heads * LE_HEAD_DIM;
-  float* sq = sm;            // 64
-  float* sk = sm + 64;       // 64
-  float* sv = sm + 128;      // 64
-  float* red = sm + 192;     // 32
-  float* pv = sm + 256;      // 32 x 64 partial outputs
-  float* kc = A.kcache + (size_t)l * A.max_seq * kv_dim + kvh * LE_HEAD_DIM;
-  float* vc = A.vcache + (size_t)l * A.max_seq * kv_dim + kvh * LE_HEAD_DIM;
+  float* sq = sm;           // 64: q after RoPE
+  float* sk = sm + 64;      // 64: k after RoPE
+  float* sv = sm + 128;     // 64
+  float* raw = sm + 192;    // 192: q, k, v as loaded
+  float* wm = sm + 384;     // 16: per-warp running max
+  float* wl = sm + 400;     // 16: per-warp sum
+  float* wacc = sm + 448;   // 16 x 64: per-warp output rows
+  const float* kc = A.kcache + (size_t)l * A.max_seq * kv_dim + kvh * LE_HEAD_DIM;
+  const float* vc = A.vcache + (size_t)l * A.max_seq * kv_dim + kvh * LE_HEAD_DIM;
   const uint32_t tq = phase_tag(s, A.layers, l, TG_QKV);
 
-  // The K and V rows of positions < pos do not depend on this step: pull this head's rows into
-  // L2 before its q/k/v are ready (bulk prefetches, 256 bytes per row).
-  for (int t = tid; t < pos; t += NT) {
+  float2 kr[kAttnP], vr[kAttnP];
+  auto load_chunk = [&](int base) {
+#pragma unroll
+    for (int i = 0; i < kAttnP; ++i) {
+      const int t = base + w + kPConsumerWarps * i;
+      if (t < pos) {
+        kr[i] = __ldcg(reinterpret_cast<const float2*>(kc + (size_t)t * kv_dim) + lane);
+        vr[i] = __ldcg(reinterpret_cast<const float2*>(vc + (size_t)t * kv_dim) + lane);
+      }
+    }
+  };
+  load_chunk(0);
+  // second chunk: rows [kAttnChunk, 2 kAttnChunk) as [row][K 64 | V 64] floats in `img`
+  const int c1 = min(pos, 2 * kAttnChunk) - kAttnChunk;
+  for (int pc = tid; pc < c1 * 32; pc += NT) {
+    const int r = pc >> 5, part = pc & 31;  // parts 0..15: K, 16..31: V (16 bytes each)
+    const float* src = (part < 16 ? kc : vc) + (size_t)(kAttnChunk + r) * kv_dim + (part & 15) * 4;
+    cp_async16_s(smem_u32(img + r * 128 + (part & 16) * 4 + (part & 15) * 4), src);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // rows of later chunks: into L2 meanwhile
+  for (int t = 2 * kAttnChunk + tid; t < pos; t += NT) {
     prefetch_l2(kc + (size_t)t * kv_dim, 256);
     prefetch_l2(vc + (size_t)t * kv_dim, 256);
   }
-  // a thread pair owns one position: thread 2t+hf holds dims 32*hf .. 32*hf+31 of K row t
-  const int hf = tid & 1, tp = tid >> 1;
-  if (tid < 32) {
-    const float c = A.rope_cos[pos * 32 + tid], sn = A.rope_sin[pos * 32 + tid];
-    const float r0 = ld_tagged1(A, A.qkv + h * LE_HEAD_DIM + tid, tq, 100 + l);
-    const float r1 = ld_tagged1(A, A.qkv + h * LE_HEAD_DIM + tid + 32, tq, 100 + l);
-    sq[tid] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, sn));
-    sq[tid + 32] = __fadd_rn(__fmul_rn(r0, sn), __fmul_rn(r1, c));
-  } else if (tid < 64) {
-    const int i = tid - 32;
+  // q, k, v of this step: one 16-byte tagged load (two elements) per thread
+  if (tid < 96) {
+    const unsigned long long* src = tid < 32   ? A.qkv + h * LE_HEAD_DIM + 2 * tid
+                                    : tid < 64 ? A.qkv + q_dim + kvh * LE_HEAD_DIM + 2 * (tid - 32)
+                                               : A.qkv + q_dim + kv_dim + kvh * LE_HEAD_DIM + 2 * (tid - 64);
+    float v2[2];
+    ld_tagged<1>(A, src, tq, v2, 100 + l);
+    raw[2 * tid] = v2[0];
+    raw[2 * tid + 1] = v2[1];
+  }
+  consumer_sync();
+  if (tid < 64) {  // RoPE of q (tid < 32) and k: pairs (i, i + 32)
+    const int i = tid & 31;
+    const float* r = raw + (tid < 32 ? 0 : 64);
+    float* o = tid < 32 ? sq : sk;
     const float c = A.rope_cos[pos * 32 + i], sn = A.rope_sin[pos * 32 + i];
-    const unsigned long long* kh = A.qkv + q_dim + kvh * LE_HEAD_DIM;
-    const float r0 = ld_tagged1(A, kh + i, tq, 100 + l), r1 = ld_tagged1(A, kh + i + 32, tq, 100 + l);
-    sk[i] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, sn));
-    sk[i + 32] = __fadd_rn(__fmul_rn(r0, sn), __fmul_rn(r1, c));
+    const float r0 = r[i], r1 = r[i + 32];
+    o[i] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, sn));
+    o[i + 32] = __fadd_rn(__fmul_rn(r0, sn), __fmul_rn(r1, c));
   } else if (tid < 128) {
-    sv[tid - 64] = ld_tagged1(A, A.qkv + q_dim + kv_dim + kvh * LE_HEAD_DIM + tid - 64, tq, 100 + l);
+    sv[tid - 64] = raw[128 + tid - 64];
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   consumer_sync();
-  if (h % group == 0 && tid < 64) {
-    kc[(size_t)pos * kv_dim + tid] = sk[tid];
-    vc[(size_t)pos * kv_dim + tid] = sv[tid];
+  if (fine) trace_mark<kTrace>(A, ntr, tok, ftag | 0xA0000u);
+  // KV append by the last two warps; their fence orders the rows before everything this CTA
+  // publishes after its next barrier
+  if (h % group == 0 && tid >= NT - 64) {
+    const int i = tid - (NT - 64);
+    A.kcache[(size_t)l * A.max_seq * kv_dim + (size_t)pos * kv_dim + kvh * LE_HEAD_DIM + i] = sk[i];
+    A.vcache[(size_t)l * A.max_seq * kv_dim + (size_t)pos * kv_dim + kvh * LE_HEAD_DIM + i] = sv[i];
+    __threadfence();
   }
-  // scores: one position per thread pair
-  float mx = -INFINITY;
-  for (int t0 = 0; t0 <= pos; t0 += NT / 2) {
-    const int t = t0 + tp;
-    float dot = 0.0f;
-    if (t < pos) {
-      float4 k0[8];
-      const float4* kt = reinterpret_cast<const float4*>(kc + (size_t)t * kv_dim) + 8 * hf;
+  const float2 q2 = reinterpret_cast<const float2*>(sq)[lane];
+  const float2 kcur = reinterpret_cast<const float2*>(sk)[lane];
+  const float2 vcur = reinterpret_cast<const float2*>(sv)[lane];
+  float m = -INFINITY, lsum = 0.0f;
+  float2 acc = make_float2(0.0f, 0.0f);
+  for (int base = 0; base <= pos; base += kAttnChunk) {
+    const bool from_img = base == kAttnChunk;
+    if (base >= 2 * kAttnChunk) load_chunk(base);
+    float sc[kAttnP];
+    float cm = -INFINITY;
 #pragma unroll
-      for (int d4 = 0; d4 < 8; ++d4) k0[d4] = __ldcg(kt + d4);
-      const float* qh = sq + 32 * hf;
+    for (int i = 0; i < kAttnP; ++i) {
+      const int t = base + w + kPConsumerWarps * i;
+      const float2 kk = t >= pos   ? kcur
+                        : from_img ? reinterpret_cast<const float2*>(img + (t - base) * 128)[lane]
+                                   : kr[i];
+      const float d = warp_allsum(fmaf(q2.x, kk.x, q2.y * kk.y));
+      sc[i] = t <= pos ? d * 0.125f : -INFINITY;
+      cm = fmaxf(cm, sc[i]);
+    }
+    if (cm == -INFINITY) continue;  // no position of this chunk on this warp (warp-uniform)
+    const float mn = fmaxf(m, cm);
+    const float r = expf(m - mn);
+    lsum *= r;
+    acc.x *= r;
+    acc.y *= r;
 #pragma unroll
-      for (int d4 = 0; d4 < 8; ++d4) {
-        dot = fmaf(qh[4 * d4], k0[d4].x, dot);
-        dot = fmaf(qh[4 * d4 + 1], k0[d4].y, dot);
-        dot = fmaf(qh[4 * d4 + 2], k0[d4].z, dot);
-        dot = fmaf(qh[4 * d4 + 3], k0[d4].w, dot);
+    for (int i = 0; i < kAttnP; ++i) {
+      const int t = base + w + kPConsumerWarps * i;
+      if (t <= pos) {
+        const float e = expf(sc[i] - mn);
+        const float2 vv = t >= pos   ? vcur
+                          : from_img ? reinterpret_cast<const float2*>(img + (t - base) * 128 + 64)[lane]
+                                     : vr[i];
+        lsum += e;
+        acc.x = fmaf(e, vv.x, acc.x);
+        acc.y = fmaf(e, vv.y, acc.y);
       }
-    } else if (t == pos) {
-#pragma unroll
-      for (int d = 0; d < 32; ++d) dot = fmaf(sq[32 * hf + d], sk[32 * hf + d], dot);
     }
-    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-    if (t <= pos) {
-      const float sc = dot * 0.125f;
-      if (hf == 0) scores[t] = sc;
-      mx = fmaxf(mx, sc);
-    }
+    m = mn;
   }
-  mx = warp_max(mx);
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
-  consumer_sync();
-  mx = red[0];
-#pragma unroll
-  for (int w = 1; w < kPConsumerWarps; ++w) mx = fmaxf(mx, red[w]);
-  float se = 0.0f;
-  for (int t = tid; t <= pos; t += NT) {
-    const float e = expf(scores[t] - mx);
-    scores[t] = e;
-    se += e;
+  if (fine) trace_mark<kTrace>(A, ntr, tok, ftag | 0xB0000u);
+  if (lane == 0) {
+    wm[w] = m;
+    wl[w] = lsum;
   }
-  se = warp_sum(se);
-  consumer_sync();  // everyone has read red[0..15] and written scores[]
-  if ((tid & 31) == 0) red[16 + (tid >> 5)] = se;
-  consumer_sync();
-  float tot = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kPConsumerWarps; ++w) tot += red[16 + w];
-  const float inv = 1.0f / tot;
-  // PV: thread = (4 dims d4, position group tg of 32); loads unrolled by 4
-  const int d4 = tid & 15, tg = tid >> 4;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  const float4 svn = reinterpret_cast<const float4*>(sv)[d4];
-  int t = tg;
-  for (; t + 96 < pos; t += 128) {  // rows < pos only: row pos may still be in flight
-    float4 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(vc + (size_t)(t + 32 * u) * kv_dim) + d4);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float p = scores[t + 32 * u] * inv;
-      acc.x = fmaf(p, v[u].x, acc.x);
-      acc.y = fmaf(p, v[u].y, acc.y);
-      acc.z = fmaf(p, v[u].z, acc.z);
-      acc.w = fmaf(p, v[u].w, acc.w);
-    }
-  }
-  for (; t <= pos; t += 32) {
-    const float4 v = t == pos ? svn : __ldcg(reinterpret_cast<const float4*>(vc + (size_t)t * kv_dim) + d4);
-    const float p = scores[t] * inv;
-    acc.x = fmaf(p, v.x, acc.x);
-    acc.y = fmaf(p, v.y, acc.y);
-    acc.z = fmaf(p, v.z, acc.z);
-    acc.w = fmaf(p, v.w, acc.w);
-  }
-  reinterpret_cast<float4*>(pv)[tg * 16 + d4] = acc;
+  reinterpret_cast<float2*>(wacc + w * 64)[lane] = acc;
   consumer_sync();
   if (tid < 64) {
-    float o = 0.0f;
+    float M = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 32; ++k) o += pv[k * 64 + tid];
-    st_tag(A.attn + h * LE_HEAD_DIM + tid, o, phase_tag(s, A.layers, l, TG_ATTN));
-    __threadfence();  // orders this thread's KV-cache stores before its later releases
+    for (int v = 0; v < kPConsumerWarps; ++v) M = fmaxf(M, wm[v]);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int v = 0; v < kPConsumerWarps; ++v) {
+      const float f = wm[v] == -INFINITY ? 0.0f : expf(wm[v] - M);
+      L = fmaf(wl[v], f, L);
+      o = fmaf(wacc[v * 64 + tid], f, o);
+    }
+    st_tag(A.attn + h * LE_HEAD_DIM + tid, o / L, phase_tag(s, A.layers, l, TG_ATTN));
   }
+  if (fine) trace_mark<kTrace>(A, ntr, tok, ftag | 0xC0000u);
   consumer_sync();
 }
 
@@ -635,16 +711,9 @@ __device__ __forceinline__ void embed_group(const PArgs& A, int token, float (&v
 // ---------------------------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void trace_mark(const PArgs& A, int& n, int tok, uint32_t tag,
-                                           unsigned long long value = 0ull) {
-  if (A.trace != nullptr && tok == 0 && n < kTraceCap) {
-    unsigned long long* tr = A.trace + ((size_t)blockIdx.x * kTraceCap + n) * 2;
-    tr[0] = value ? value : gtimer();
-    tr[1] = tag;
-    ++n;
-  }
-}
-
+// kTrace = true builds the variant that records the phase trace (llama_engine_trace); the
+// production variant carries no trace code.
+template <bool kTrace>
 __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid_constant__ PArgs A) {
   extern __shared__ __align__(1024) uint8_t psmem[];
   uint8_t* ring = psmem;                                          // kRingSlots * kRecBytes
@@ -654,8 +723,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   uint32_t* s_recs = reinterpret_cast<uint32_t*>(bars + kRingSlots);                     // kMaxRecs
   PItem* s_items = reinterpret_cast<PItem*>(s_recs + kMaxRecs);                          // kMaxItems
   PSeg* s_segs = reinterpret_cast<PSeg*>(s_items + kMaxItems);                           // kMaxSegs
-  __shared__ float s_part[2][kPConsumerWarps][16];
   __shared__ unsigned long long s_best[kPConsumerWarps];
+  __shared__ int s_slot_cnt[kRingSlots];  // units done with the record in each slot
   __shared__ int s_token;
   // record index currently issued into each ring slot.  A consumer of record q first waits until
   // its slot holds q: only then does the slot's mbarrier parity refer unambiguously to q (a
@@ -686,6 +755,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
     for (int s = 0; s < kRingSlots; ++s) {
       mbar_init(full0 + 8 * s, 1);
       s_slot_rec[s] = -1;
+      s_slot_cnt[s] = 0;
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -699,18 +769,16 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   S.bsum = reinterpret_cast<float*>(image + 32768);
   S.escl = S.bsum + 64;
   S.red = S.escl + 64;
-  float* scores = reinterpret_cast<float*>(image);  // attention reuses the image buffer
   int token = A.prm->token;
   const int pos0 = A.prm->pos;
   const int L = A.layers;
   int ntr = 0;
-  int buf = 0;
 
   for (int tok = 0; tok < A.n_tokens; ++tok) {
     const uint32_t s = step_seq + (uint32_t)tok;
     const int pos = pos0 + tok;
     const uint32_t rec_base = per_tok * (uint32_t)tok;
-    if (tid == 0) trace_mark(A, ntr, tok, 0xFFFF0000u);
+    if (tid == 0) trace_mark<kTrace>(A, ntr, tok, 0xFFFF0000u);
     if (tok > 0) {
       // next token = greedy id of the previous step (all CTAs' lm_head work done)
       if (tid == 0) {
@@ -721,10 +789,11 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
       consumer_sync();
       token = s_token;
     }
-    // threads 0..255 dequantise the embedding row (layer-0 input); CTA 0 also publishes it as x
-    float emb[8];
-    embed_group(A, token, emb);
+    // CTA 0 publishes the embedding row as the layer-0 residual x (every CTA dequantises it
+    // again for its layer-0 QKV staging, so no register holds it across the segment loop)
     if (blockIdx.x == 0 && tid < 256) {
+      float emb[8];
+      embed_group(A, token, emb);
       const uint32_t tx = phase_tag(s, L, 0, TG_XIN);
 #pragma unroll
       for (int k = 0; k < 8; ++k) st_tag(A.x + 8 * tid + k, emb[k], tx);
@@ -739,13 +808,20 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
       const int l = sg.layer;
       if (sg.kind == PK_LMHEAD && !A.do_logits) continue;
       const uint32_t tag = ((uint32_t)sg.kind << 8) | (uint32_t)l;
-      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x10000u);
+      if (tid == 0) trace_mark<kTrace>(A, ntr, tok, tag | 0x10000u);
       consumer_sync();  // previous segment's readers of the image are done
-      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x20000u);
+      if (tid == 0) trace_mark<kTrace>(A, ntr, tok, tag | 0x20000u);
+      // o-proj / down: the residual rows were final before this phase; fetch their words now and
+      // check the tags in the epilogue
+      unsigned long long resw = 0ull;
+      if ((sg.kind == PK_O || sg.kind == PK_DOWN) && tid < 16 * (int)(sg.item_end - sg.item_begin))
+        resw = ld_tag(A.x + (int)s_items[sg.item_begin + (tid >> 4)].tile * 16 + (tid & 15));
       // ---- staging (the tagged loads are the dependency waits) ----
       switch (sg.kind) {
         case PK_QKV:
           if (l == 0) {
+            float emb[8];
+            embed_group(A, token, emb);
             float4 gm[2];
             load_gamma(A.norms, gm);
             stage_norm2048_vals(emb, gm, S);
@@ -767,90 +843,104 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
           stage_norm2048(A, A.x, phase_tag(s, L, L, TG_XIN), A.norms + (size_t)(2 * L) * 2048, S, 500);
           break;
       }
-      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x30000u);
+      if (tid == 0) trace_mark<kTrace>(A, ntr, tok, tag | 0x30000u);
       // ---- work ----
       if (sg.kind == PK_ATTN) {
         for (uint32_t it = sg.item_begin; it < sg.item_end; ++it)
-          attention_head(A, l, (int)s_items[it].tile, pos, s, scores, misc);
-        if (tid == 0) trace_mark(A, ntr, tok, tag | 0x40000u);
+          attention_head<kTrace>(A, l, (int)s_items[it].tile, pos, s, misc, reinterpret_cast<float*>(image), ntr, tok);
+        if (tid == 0) trace_mark<kTrace>(A, ntr, tok, tag | 0x40000u);
         continue;
       }
-      // Split factor F: groups of F warps share one item, each warp reducing 16/F blocks of every
-      // record of it.  Streaming phases keep pairs of warps per record.
+      // Work units: the segment's records (consecutive in the CTA's stream, items in order, nrec
+      // per item) each split into sg.split block ranges; unit u = (record u / split, range
+      // u % split) runs on warp u % 16.  No barrier per record: each unit leaves its 16 row
+      // partials in shared memory, and the last unit to finish a ring slot refills it.
+      const int SP = sg.split;
       const int n_items = (int)(sg.item_end - sg.item_begin);
-      const int F = n_items >= 8 ? 2 : n_items >= 4 ? 4 : n_items >= 2 ? 8 : 16;
-      const int n_groups = kPConsumerWarps / F, gi = cw / F, mi = cw % F;
+      const PItem it0 = s_items[sg.item_begin];
+      const int nrec_item = it0.nrec;
+      const int n_units = n_items * nrec_item * SP;
+      const uint32_t q0 = rec_base + it0.rec;
+      float* s_unit = misc;  // [n_units][16]
       // output tags of this phase
       const uint32_t t_out = sg.kind == PK_QKV      ? phase_tag(s, L, l, TG_QKV)
                              : sg.kind == PK_O      ? phase_tag(s, L, l, TG_XO)
                              : sg.kind == PK_GATEUP ? phase_tag(s, L, l, TG_ACT)
                                                     : phase_tag(s, L, l + 1, TG_XIN);
       const uint32_t t_res = sg.kind == PK_O ? phase_tag(s, L, l, TG_XIN) : phase_tag(s, L, l, TG_XO);
-      unsigned long long best = 0ull;
       unsigned long long wait_cycles = 0;
-      for (int ii = gi; ii < n_items; ii += n_groups) {
-        const PItem item = s_items[sg.item_begin + ii];
-        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [record kind: gate/up][row g, g+8]
-        // residual rows of o-proj / down: ready before this phase started; fetch them now
-        float res0 = 0.f, res1 = 0.f;
-        const bool owner = mi == 0 && (lane & 3) == 0;
-        if (owner && (item.kind == PK_O || item.kind == PK_DOWN)) {
-          const int r0 = (int)item.tile * 16 + (lane >> 2);
-          res0 = ld_tagged1(A, A.x + r0, t_res, 700 + l);
-          res1 = ld_tagged1(A, A.x + r0 + 8, t_res, 700 + l);
+      const bool fine = kTrace && tid == 0 && (l == 1 || l == 2);
+      for (int u = cw; u < n_units; u += kPConsumerWarps) {
+        const int rl = u / SP, sub = u - rl * SP;
+        const uint32_t q = q0 + (uint32_t)rl;
+        const uint32_t slot = q % kRingSlots;
+        const long long w0 = kTrace ? clock64() : 0;
+        wait_slot(A, s_slot_rec, slot, q, 650 + sg.kind);
+        wait_mbar(A, full0 + 8 * slot, (q / kRingSlots) & 1, 600 + sg.kind);
+        if (kTrace) wait_cycles += (unsigned long long)(clock64() - w0);
+        if (fine) trace_mark<kTrace>(A, ntr, tok, tag | 0x70000u);
+        float p0, p1;
+        record_blocks(SP, ring + (size_t)slot * kRecBytes, sg.kind == PK_DOWN ? rl % nrec_item : 0, sub, S, p0, p1);
+        if ((lane & 3) == 0) {
+          s_unit[u * 16 + (lane >> 2)] = p0;
+          s_unit[u * 16 + (lane >> 2) + 8] = p1;
         }
-        for (int rr = 0; rr < item.nrec; ++rr) {
-          const uint32_t q = rec_base + item.rec + rr;
-          const uint32_t slot = q % kRingSlots;
-          const long long w0 = clock64();
-          wait_slot(A, s_slot_rec, slot, q, 650 + item.kind);
-          wait_mbar(A, full0 + 8 * slot, (q / kRingSlots) & 1, 600 + item.kind);
-          wait_cycles += (unsigned long long)(clock64() - w0);
-          float p0, p1;
-          record_blocks(F, ring + (size_t)slot * kRecBytes, item.kind == PK_DOWN ? rr : 0, mi, S, p0, p1);
-          const int k = item.kind == PK_GATEUP ? rr : 0;
-          if ((lane & 3) == 0) {
-            s_part[buf][cw][lane >> 2] = p0;
-            s_part[buf][cw][(lane >> 2) + 8] = p1;
+        if (fine) trace_mark<kTrace>(A, ntr, tok, tag | 0x80000u);
+        __syncwarp();  // every lane's reads of the slot have completed
+        if (lane == 0) {
+          bool last = true;
+          if (SP > 1) {
+            last = atomicAdd(&s_slot_cnt[slot], 1) == SP - 1;
+            if (last) atomicExch(&s_slot_cnt[slot], 0);  // atomic: ordered with the next record's adds
           }
-          if (F == 1) __syncwarp(); else group_sync(gi, 32 * F);
-          // every warp of the group is done with the slot: refill it with the record ten ahead
-          if (mi == 0 && lane == 0 && q + kRingSlots < total) issue(q + kRingSlots);
-          if (owner) {
-            float v0 = 0.f, v1 = 0.f;
-            for (int w = 0; w < F; ++w) {
-              v0 += s_part[buf][gi * F + w][lane >> 2];
-              v1 += s_part[buf][gi * F + w][(lane >> 2) + 8];
-            }
-            acc[k][0] += v0;
-            acc[k][1] += v1;
-          }
-          buf ^= 1;
+          if (last && q + kRingSlots < total) issue(q + kRingSlots);
         }
-        // epilogue: lanes t == 0 of the group's first warp own rows g and g+8
-        if (owner) {
-          const int r0 = (int)item.tile * 16 + (lane >> 2), r1 = r0 + 8;
-          switch (item.kind) {
-            case PK_QKV:
-              st_tag(A.qkv + r0, acc[0][0], t_out);
-              st_tag(A.qkv + r1, acc[0][1], t_out);
-              break;
-            case PK_O:
-            case PK_DOWN:
-              st_tag(A.x + r0, res0 + acc[0][0], t_out);
-              st_tag(A.x + r1, res1 + acc[0][1], t_out);
-              break;
-            case PK_GATEUP:
-              st_tag(A.act + r0, (acc[0][0] / (1.0f + expf(-acc[0][0]))) * acc[1][0], t_out);
-              st_tag(A.act + r1, (acc[0][1] / (1.0f + expf(-acc[0][1]))) * acc[1][1], t_out);
-              break;
-            case PK_LMHEAD:
-              A.logits[r0] = acc[0][0];
-              A.logits[r1] = acc[0][1];
-              if (acc[0][0] > -1e30f) best = max(best, argmax_key(acc[0][0], r0));
-              if (acc[0][1] > -1e30f) best = max(best, argmax_key(acc[0][1], r1));
-              break;
+        if (fine) trace_mark<kTrace>(A, ntr, tok, tag | 0x90000u);
+      }
+      consumer_sync();  // all units' partials are in s_unit
+      // epilogue: one thread per (item, row); the residual word was fetched before staging
+      unsigned long long best = 0ull;
+      for (int e = tid; e < n_items * 16; e += kPThreads) {
+        const int i = e >> 4, r = e & 15;
+        const int row = (int)s_items[sg.item_begin + i].tile * 16 + r;
+        const float* pu = s_unit + (size_t)i * nrec_item * SP * 16 + r;
+        if (sg.kind == PK_GATEUP) {  // records: gate, up
+          float g = 0.f, up = 0.f;
+          for (int v = 0; v < SP; ++v) {
+            g += pu[v * 16];
+            up += pu[(SP + v) * 16];
           }
+          st_tag(A.act + row, (g / (1.0f + expf(-g))) * up, t_out);
+          continue;
+        }
+        float a = 0.f;
+        const int nv = nrec_item * SP;
+        if (nv == 16) {
+          float t[16];
+#pragma unroll
+          for (int v = 0; v < 16; ++v) t[v] = pu[v * 16];
+#pragma unroll
+          for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+            for (int v = 0; v < w; ++v) t[v] += t[v + w];
+          a = t[0];
+        } else {
+          for (int v = 0; v < nv; ++v) a += pu[v * 16];
+        }
+        switch (sg.kind) {
+          case PK_QKV:
+            st_tag(A.qkv + row, a, t_out);
+            break;
+          case PK_O:
+          case PK_DOWN: {
+            const float res = (e == tid && tag_of(resw) == t_res) ? tag_val(resw) : ld_tagged1(A, A.x + row, t_res, 700 + l);
+            st_tag(A.x + row, res + a, t_out);
+            break;
+          }
+          case PK_LMHEAD:
+            A.logits[row] = a;
+            if (a > -1e30f) best = max(best, argmax_key(a, row));
+            break;
         }
       }
       if (sg.kind == PK_LMHEAD) {
@@ -866,8 +956,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
           atomicAdd(&A.ctrl->lm_ctr, 1u);
         }
       }
-      if (cw == 0 && lane == 0) trace_mark(A, ntr, tok, tag | 0x50000u, wait_cycles | 1ull);
-      if (tid == 0) trace_mark(A, ntr, tok, tag | 0x40000u);
+      if (cw == 0 && lane == 0) trace_mark<kTrace>(A, ntr, tok, tag | 0x50000u, wait_cycles | 1ull);
+      if (tid == 0) trace_mark<kTrace>(A, ntr, tok, tag | 0x40000u);
     }
   }
 

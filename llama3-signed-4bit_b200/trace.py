@@ -18,8 +18,9 @@ KINDS = {0: "qkv", 1: "attn", 2: "oproj", 3: "gateup", 4: "down", 5: "lmhead"}
 CAP = 1024
 
 
-def capture(engine, token: int, pos: int) -> dict:
-    """Runs one traced forward_token (with logits) and returns the phase breakdown."""
+def capture(engine, token: int, pos: int, raw_path: str | None = None) -> dict:
+    """Runs one traced forward_token (with logits) and returns the phase breakdown; with
+    ``raw_path`` the raw [cta][entry][(time, word)] array is also saved there (numpy .npy)."""
     lib = engine.bindings.lib
     h = engine.handle
     if lib.llama_engine_trace(h, 1, None, 0) != 0:
@@ -32,16 +33,53 @@ def capture(engine, token: int, pos: int) -> dict:
     lib.llama_engine_trace(h, 0, None, 0)
     if n <= 0:
         raise RuntimeError("trace read failed")
-    return analyse(buf[: 2 * n].reshape(-1, CAP, 2))
+    tr = buf[: 2 * n].reshape(-1, CAP, 2)
+    if raw_path:
+        np.save(raw_path, tr)
+    out = analyse(tr)
+    out["fine_cycles"] = analyse_fine(tr)
+    return out
+
+
+# events: 1 segment start, 2 after the CTA barrier, 3 input staged, 4 end, 5 ring-wait cycles,
+# 6 residual loaded, 7 record data ready, 8 record reduced, 9 partials accumulated (layers 1-2);
+# attention (layers 1-2): 10 q/k/v loaded, 11 scores, 12 softmax, 13 PV partials
+EVENT_NAMES = {1: "start", 2: "barrier", 3: "staged", 4: "end", 6: "residual", 7: "rec_ready", 8: "rec_reduced",
+               9: "rec_accumulated", 10: "qkv_loaded", 11: "scores", 12: "softmax", 13: "pv"}
+
+
+def analyse_fine(tr: np.ndarray) -> dict:
+    """SM-clock intervals between consecutive events of one CTA inside the segments of layers 1
+    and 2: mean cycles per occurrence of each (kind, from -> to) transition, and its count."""
+    acc = defaultdict(list)
+    for c in range(tr.shape[0]):
+        prev = None
+        for time_ns, word in tr[c]:
+            time_ns, word = int(time_ns), int(word)
+            if time_ns == 0:
+                break
+            tag, clk = word & 0xFFFFFFFF, word >> 32
+            if tag == 0xFFFF0000:
+                prev = None
+                continue
+            ev, kind, layer = tag >> 16, (tag >> 8) & 0xFF, tag & 0xFF
+            if ev == 5:
+                continue
+            if layer in (1, 2) and prev is not None and prev[0] == (kind, layer):
+                acc[(KINDS.get(kind, str(kind)), EVENT_NAMES.get(prev[1], str(prev[1])),
+                     EVENT_NAMES.get(ev, str(ev)))].append((clk - prev[2]) & 0xFFFFFFFF)
+            prev = ((kind, layer), ev, clk)
+    return {f"{k} {a}->{b}": {"mean_cyc": round(float(np.mean(v)), 1), "max_cyc": int(np.max(v)), "n": len(v)}
+            for (k, a, b), v in sorted(acc.items())}
 
 
 def analyse(tr: np.ndarray) -> dict:
-    """tr: [cta][CAP][(time_ns, tag)]"""
+    """tr: [cta][CAP][(time_ns, tag | clock << 32)]"""
     t0 = None
     per_seg = defaultdict(dict)  # (kind, layer, cta) -> {event: t}
     for c in range(tr.shape[0]):
         for time_ns, tag in tr[c]:
-            time_ns, tag = int(time_ns), int(tag)
+            time_ns, tag = int(time_ns), int(tag) & 0xFFFFFFFF
             if time_ns == 0:
                 break
             if tag == 0xFFFF0000:
