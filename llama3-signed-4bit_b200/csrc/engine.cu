@@ -425,9 +425,9 @@ static bool init_persistent(Engine* E) {
   // Work units per record for a segment of n_rec records: the split (block ranges of 16/split
   // blocks) that minimises the busiest warp's (units x (blocks per unit + 2)), the 2 standing
   // for a unit's fixed cost, within the shared-memory room for unit partials.
-  auto choose_split = [](int n_rec) -> int {
-    int best = 1, best_cost = 1 << 30;
-    for (int sp = 1; sp <= 16; sp *= 2) {
+  auto choose_split = [](int n_rec) -> int {  // splits 2..16 (a unit covers at most 8 blocks)
+    int best = 2, best_cost = 1 << 30;
+    for (int sp = 2; sp <= 16; sp *= 2) {
       if (n_rec * sp > kMaxUnits) break;
       const int units_per_warp = (n_rec * sp + kPConsumerWarps - 1) / kPConsumerWarps;
       const int cost = units_per_warp * (16 / sp + 2);

@@ -46,6 +46,7 @@ constexpr int kMiscFloats = 2304;          // attention scratch (q, k, v, reduct
 constexpr int kMaxUnits = kMiscFloats / 16;  // work units per segment
 constexpr int kImageBytes = 32768 + 1024;  // digit fragments for K <= 8192, or attention scores
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every wait
+constexpr unsigned kPollNs = 20;  // pause between polls of tagged activations
 constexpr int kTraceCap = 1024;
 
 enum PKind : uint16_t { PK_QKV = 0, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN, PK_LMHEAD };
@@ -263,7 +264,7 @@ __device__ __forceinline__ void ld_tagged(const PArgs& A, const unsigned long lo
       for (int i = 0; i < 2 * N2; ++i) ok &= tag_of(w[i]) == tag;
       if (ok || failed(A)) break;
       if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
-      __nanosleep(20);
+      __nanosleep(kPollNs);
     }
   }
 #pragma unroll
@@ -293,6 +294,7 @@ __device__ __forceinline__ void ld_tagged2x(const PArgs& A, const unsigned long 
       load();
       if (all_ok() || failed(A)) break;
       if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+      __nanosleep(kPollNs);
     }
   }
 #pragma unroll
@@ -310,7 +312,7 @@ __device__ __forceinline__ float ld_tagged1(const PArgs& A, const unsigned long 
       w = ld_tag(p);
       if (tag_of(w) == tag || failed(A)) break;
       if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
-      __nanosleep(20);
+      __nanosleep(kPollNs);
     }
   }
   return tag_val(w);
@@ -453,8 +455,14 @@ __device__ __forceinline__ void record_chunk(uint32_t r_nib, uint32_t r_sc, uint
     const uint4 wa = lds128(r_nib + 1024u * j);
     const uint4 wb = lds128(r_nib + 1024u * j + 512u);
     const uint32_t bfa = s_bf + 512u * b;
-    uint2 b0 = lds64(bfa), b1 = lds64(bfa + 128u), b2 = lds64(bfa + 256u), b3 = lds64(bfa + 384u);
-    if (!bl) b0 = b1 = b2 = b3 = make_uint2(0u, 0u);
+    // lanes 16..31 hold the zero columns 4..7 of B: only the low half-warp reads shared memory
+    uint2 b0 = make_uint2(0u, 0u), b1 = b0, b2 = b0, b3 = b0;
+    if (bl) {
+      b0 = lds64(bfa);
+      b1 = lds64(bfa + 128u);
+      b2 = lds64(bfa + 256u);
+      b3 = lds64(bfa + 384u);
+    }
     int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
     // low K-half: raw bytes (q_even + 16 q_odd); high K-half: q_odd (see stage_group)
     mma_u8s8(c0, wa.x, wb.x, (wa.x >> 4) & 0x0F0F0F0Fu, (wb.x >> 4) & 0x0F0F0F0Fu, b0.x, b0.y);
