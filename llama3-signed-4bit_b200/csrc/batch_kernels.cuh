@@ -32,12 +32,17 @@ __global__ void k_embed_batch(QMat E, const int32_t* __restrict__ tok, float* __
 
 // Attention of token t (position pos[t], sequence slot[t]) for the 4 q heads of kv head g
 // (src/llama_engine.cpp:958-1021: kv_h = h / 4, s = (q . k) * 0.125, softmax over 0..pos,
-// o = sum p v).  The token's own k / v are already in the cache (written by the RoPE / append
-// kernel).  One CTA of 4 warps per (t, g): the CTA streams 32-position K / V tiles through shared
-// memory (coalesced cp.async, three tiles in a ring, rows padded to 68 floats so that 16-byte row reads
-// of 8 lanes hit distinct banks) and warp h computes q head h against each tile: lane = position
-// for the scores, lane = dimension pair for p . v.  Softmax runs online (running max and sum,
-// rescaled per tile).
+// o = sum p v).  With qkv == nullptr, q comes rotated in `q` and the token's own k / v are
+// already in the cache (RoPE / append kernel).  With qkv set, the CTA builds them itself from
+// the q | k | v GEMM output (the sum of its nsplit split-K planes, rotated with the RoPE table
+// as in k_rope_append, src/llama_engine.cpp:953-956), uses the token's k / v for position pos
+// in place of the cache row, and the CTA whose range holds pos appends them to the cache.  One CTA of 4 warps per (t, g): the CTA streams 32-position K / V tiles through shared
+// memory (coalesced cp.async, three tiles in a ring, rows padded to 68 floats so that 16-byte row
+// reads of 8 lanes hit distinct banks).  Each tile is read once for all four heads: for the
+// scores warp w takes dimensions 16w .. 16w+15 of every head (lane = position) and the four
+// warps' partial dot products meet in shared memory; warp h then runs the online softmax of head
+// h (running max and sum, rescaled per tile); for p . v warp w takes dimensions 16w .. 16w+15
+// of every head (lane = head x dimension pair).
 //
 // With gridDim.z = S > 1 the positions of each (t, g) are split into S contiguous ranges, one
 // CTA each, and the CTA writes its unnormalised partial (running max m, sum l and o per head)
@@ -52,18 +57,27 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+__device__ __forceinline__ float attn_sum_planes(const float* p, int nsplit, size_t stride) {
+  float v = p[0];
+  for (int s = 1; s < nsplit; ++s) v += p[s * stride];
+  return v;
+}
+
 __global__ void __launch_bounds__(128)
-    k_attn_batch(const float* __restrict__ q, int q_dim, const float* __restrict__ kc, const float* __restrict__ vc,
+    k_attn_batch(const float* __restrict__ q, int q_dim, float* __restrict__ kc, float* __restrict__ vc,
                  size_t slot_stride, int kv_dim, const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
-                 float* __restrict__ out, float* __restrict__ part) {
+                 float* __restrict__ out, float* __restrict__ part, const float* __restrict__ qkv, int nsplit,
+                 size_t split_stride, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin) {
   // three-stage ring of K / V tiles (two tiles in flight while one is used)
   extern __shared__ __align__(16) float attn_smem[];
   float (*sk)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem);
   float (*sv)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem + 3 * 32 * kAttnRow);
-  __shared__ float4 sp[4][32];  // per warp: this tile's softmax numerators (one head per warp)
+  __shared__ float sd[4][4][33];           // partial dots [warp][head][position]
+  __shared__ __align__(16) float sp[4][32];  // softmax numerators [head][position] of this tile
+  __shared__ float salpha[4], sl[4], sm[4];  // per head: rescale of this tile, final sum and max
+  __shared__ __align__(16) float sqkv[6][64];  // with qkv: q of the 4 heads, k and v of this token
   const int t = blockIdx.x, g = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = warp;
   const int P_all = pos[t] + 1;
   // this CTA's position range [tile0 * 32, P): whole 32-position tiles, split z of gridDim.z
   const int tiles = (P_all + 31) >> 5;
@@ -74,6 +88,25 @@ __global__ void __launch_bounds__(128)
   const size_t base = (size_t)slot[t] * slot_stride + (size_t)g * LE_HEAD_DIM;
   const float* Kb = kc + base;
   const float* Vb = vc + base;
+  const int p_tok = P_all - 1;
+  if (qkv != nullptr) {  // rows: q heads 4g .. 4g+3, k head g, v head g
+    const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
+    for (int j = threadIdx.x; j < 5 * 32 + 64; j += blockDim.x) {
+      if (j < 5 * 32) {  // rotated pair (i, i + 32) of q head j / 32 (4 = the k head)
+        const int hh = j >> 5, i = j & 31;
+        const int off = hh < 4 ? (4 * g + hh) * LE_HEAD_DIM + i : q_dim + g * LE_HEAD_DIM + i;
+        const float c = rope_cos[p_tok * 32 + i], sn = rope_sin[p_tok * 32 + i];
+        const float r0 = attn_sum_planes(row + off, nsplit, split_stride);
+        const float r1 = attn_sum_planes(row + off + 32, nsplit, split_stride);
+        sqkv[hh][i] = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, sn));
+        sqkv[hh][i + 32] = __fadd_rn(__fmul_rn(r0, sn), __fmul_rn(r1, c));
+      } else {
+        const int e = j - 5 * 32;
+        sqkv[5][e] = attn_sum_planes(row + q_dim + kv_dim + g * LE_HEAD_DIM + e, nsplit, split_stride);
+      }
+    }
+    __syncthreads();
+  }
   auto load_tile = [&](int kt, int buf) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -86,16 +119,24 @@ __global__ void __launch_bounds__(128)
     }
     cp_async_commit();
   };
-  float qv[64];
+  // q slices: dims 16 warp .. 16 warp + 15 of the four heads
+  float qv[4][16];
   {
-    const float4* qp = reinterpret_cast<const float4*>(q + (size_t)t * q_dim + (size_t)(4 * g + h) * LE_HEAD_DIM);
+    const float* qt = qkv != nullptr ? &sqkv[0][16 * warp] : q + (size_t)t * q_dim + (size_t)(4 * g) * LE_HEAD_DIM + 16 * warp;
 #pragma unroll
-    for (int d4 = 0; d4 < 16; ++d4) {
-      const float4 v = qp[d4];
-      qv[4 * d4] = v.x; qv[4 * d4 + 1] = v.y; qv[4 * d4 + 2] = v.z; qv[4 * d4 + 3] = v.w;
+    for (int h = 0; h < 4; ++h) {
+      const float4* qp = reinterpret_cast<const float4*>(qt + h * LE_HEAD_DIM);
+#pragma unroll
+      for (int d4 = 0; d4 < 4; ++d4) {
+        const float4 v = qp[d4];
+        qv[h][4 * d4] = v.x; qv[h][4 * d4 + 1] = v.y; qv[h][4 * d4 + 2] = v.z; qv[h][4 * d4 + 3] = v.w;
+      }
     }
   }
-  float m = -INFINITY, l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+  // softmax state of head `warp` (all lanes hold it); p . v accumulators of (head ph, dims 16 warp + 2 dp)
+  float m = -INFINITY, l = 0.0f;
+  const int ph = lane >> 3, dp = lane & 7;
+  float o0 = 0.0f, o1 = 0.0f;
   if (tile0 < tile1) load_tile(tile0, 0);
   if (tile0 + 1 < tile1) load_tile(tile0 + 1, 1);
   for (int kt = tile0; kt < tile1; ++kt) {
@@ -109,51 +150,84 @@ __global__ void __launch_bounds__(128)
       cp_async_wait<0>();
     }
     __syncthreads();
-    // score of position kt*32 + lane for head h (four partial sums over d mod 4, then added)
-    const float4* kr = reinterpret_cast<const float4*>(&sk[buf][lane][0]);
-    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
-#pragma unroll
-    for (int d4 = 0; d4 < 16; ++d4) {
-      const float4 k4 = kr[d4];
-      d0 = fmaf(qv[4 * d4], k4.x, d0);
-      d1 = fmaf(qv[4 * d4 + 1], k4.y, d1);
-      d2 = fmaf(qv[4 * d4 + 2], k4.z, d2);
-      d3 = fmaf(qv[4 * d4 + 3], k4.w, d3);
+    if (qkv != nullptr && p_tok >= kt * 32 && p_tok < kt * 32 + 32) {  // this step's own k / v
+      const int r = p_tok - kt * 32;
+      if (threadIdx.x < 64) sk[buf][r][threadIdx.x] = sqkv[4][threadIdx.x];
+      else sv[buf][r][threadIdx.x - 64] = sqkv[5][threadIdx.x - 64];
+      __syncthreads();
     }
-    const float dot = (d0 + d1) + (d2 + d3);
-    const float s = kt * 32 + lane < P ? dot * 0.125f : -INFINITY;
-    const float mn = fmaxf(m, warp_max(s));  // finite: the tile holds a position of the range
-    const float alpha = expf(m - mn);
-    const float pe = expf(s - mn);
-    l = l * alpha + warp_sum(pe);
-    o0 *= alpha;
-    o1 *= alpha;
-    m = mn;
-    reinterpret_cast<float*>(sp[h])[lane] = pe;
-    __syncwarp();
-    const float4* pw4 = reinterpret_cast<const float4*>(sp[h]);
+    // partial dots of position kt*32 + lane over this warp's 16 dimensions, for the four heads
+    {
+      const float4* kr = reinterpret_cast<const float4*>(&sk[buf][lane][16 * warp]);
+      float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int j4 = 0; j4 < 8; ++j4) {  // positions past the range have p = 0
-      const float4 p4 = pw4[j4];
-      const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+      for (int d4 = 0; d4 < 4; ++d4) {
+        const float4 k4 = kr[d4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][4 * j4 + u][2 * lane]);
-        o0 = fmaf(pj[u], v2.x, o0);
-        o1 = fmaf(pj[u], v2.y, o1);
+        for (int h = 0; h < 4; ++h) {
+          d[h] = fmaf(qv[h][4 * d4], k4.x, d[h]);
+          d[h] = fmaf(qv[h][4 * d4 + 1], k4.y, d[h]);
+          d[h] = fmaf(qv[h][4 * d4 + 2], k4.z, d[h]);
+          d[h] = fmaf(qv[h][4 * d4 + 3], k4.w, d[h]);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) sd[warp][h][lane] = d[h];
+    }
+    __syncthreads();
+    // warp h: scores and online softmax of head h
+    {
+      const int h = warp;
+      const float dot = (sd[0][h][lane] + sd[1][h][lane]) + (sd[2][h][lane] + sd[3][h][lane]);
+      const float s = kt * 32 + lane < P ? dot * 0.125f : -INFINITY;
+      const float mn = fmaxf(m, warp_max(s));  // finite: the tile holds a position of the range
+      const float alpha = expf(m - mn);
+      const float pe = expf(s - mn);
+      l = l * alpha + warp_sum(pe);
+      m = mn;
+      sp[h][lane] = pe;
+      if (lane == 0) salpha[h] = alpha;
+    }
+    __syncthreads();
+    // p . v for (head ph, dims 16 warp + 2 dp, +1): positions past the range have p = 0
+    {
+      const float alpha = salpha[ph];
+      o0 *= alpha;
+      o1 *= alpha;
+      const float4* pw4 = reinterpret_cast<const float4*>(sp[ph]);
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 p4 = pw4[j4];
+        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][4 * j4 + u][16 * warp + 2 * dp]);
+          o0 = fmaf(pj[u], v2.x, o0);
+          o1 = fmaf(pj[u], v2.y, o1);
+        }
       }
     }
-    __syncthreads();  // buffer buf is refilled by a later iteration's load
+    __syncthreads();  // buffer buf and sd / sp are rewritten by the next iteration
   }
+  if (lane == 0) {
+    sm[warp] = m;
+    sl[warp] = l;
+  }
+  if (qkv != nullptr && p_tok >= tile0 * 32 && p_tok < P) {  // append k / v at (slot, pos)
+    const size_t crow = base + (size_t)p_tok * kv_dim;
+    if (threadIdx.x < 64) kc[crow + threadIdx.x] = sqkv[4][threadIdx.x];
+    else vc[crow + threadIdx.x - 64] = sqkv[5][threadIdx.x - 64];
+  }
+  __syncthreads();
   if (gridDim.z > 1) {
-    float* pp = part + ((size_t)(t * gridDim.y + g) * gridDim.z + blockIdx.z) * kAttnPart + h * 66;
-    if (lane == 0) { pp[0] = m; pp[1] = l; }
-    pp[2 + 2 * lane] = o0;
-    pp[3 + 2 * lane] = o1;
+    float* pp = part + ((size_t)(t * gridDim.y + g) * gridDim.z + blockIdx.z) * kAttnPart + ph * 66;
+    if (warp == 0 && dp == 0) { pp[0] = sm[ph]; pp[1] = sl[ph]; }
+    pp[2 + 16 * warp + 2 * dp] = o0;
+    pp[3 + 16 * warp + 2 * dp] = o1;
     return;
   }
-  const float inv = 1.0f / l;
-  float* op = out + (size_t)t * q_dim + (size_t)(4 * g + h) * LE_HEAD_DIM + 2 * lane;
+  const float inv = 1.0f / sl[ph];
+  float* op = out + (size_t)t * q_dim + (size_t)(4 * g + ph) * LE_HEAD_DIM + 16 * warp + 2 * dp;
   *reinterpret_cast<float2*>(op) = make_float2(o0 * inv, o1 * inv);
 }
 

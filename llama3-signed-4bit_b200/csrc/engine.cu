@@ -755,14 +755,16 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
                              rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
-    k_rope_append<<<dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), 256, 0, s>>>(
-        E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
     if (prefill_p0 >= 0) {
+      k_rope_append<<<dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), 256, 0, s>>>(
+          E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
       k_attn_prefill_tc<<<dim3(E->kv_heads, (n + 15) / 16), 128, 0, s>>>(E->t_q, dim, kc, vc, kvd, prefill_p0, n,
                                                                          E->t_attn);
     } else {
-      k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, kAttnSmem, s>>>(E->t_q, dim, kc, vc, slot_stride, kvd,
-                                                                              pos, slot, E->t_attn, E->t_attn_part);
+      // decode rows: RoPE and the KV append run inside the attention kernel
+      k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, kAttnSmem, s>>>(
+          E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn, E->t_attn_part, E->t_qkv, sq, qkv_stride,
+          E->rope_cos, E->rope_sin);
       if (attn_splits > 1) k_attn_combine<<<n, 256, 0, s>>>(E->t_attn_part, E->kv_heads, attn_splits, dim, E->t_attn);
     }
     k_tc_stage<<<dim3(n, dim / 2048), 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
