@@ -226,6 +226,10 @@ struct Engine {
   ArgmaxPart* t_am = nullptr;  // [tc_T][tc_am_parts]
   int tc_am_parts = 0;
   uint32_t* tc_err = nullptr;  // device error word of the tensor-core GEMM
+  // decode steps of the batched path replayed as CUDA graphs, one per (rows, logits rows,
+  // attention splits); the rows' ids, positions and slots are read from t_idx
+  struct TcGraph { int n, nlog, splits; cudaGraphExec_t exec; };
+  std::vector<TcGraph> tc_graphs;
   // token scoring (llama_engine_score_tokens): logits of a chunk's rows, targets, results
   float* sc_logits = nullptr;   // [kScoreRows][vocab], allocated on first use
   int32_t* sc_target = nullptr; // [kScoreRows]
@@ -787,6 +791,33 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
   return true;
 }
 
+// A decode step (rows already uploaded) through a cached CUDA graph of tc_step's launches.
+static bool tc_step_graph(Engine* E, int n, int nlog, int max_pos) {
+  const int splits = std::max(1, std::min(kAttnMaxSplits, (max_pos + 1) / 1024));
+  for (const auto& g : E->tc_graphs)
+    if (g.n == n && g.nlog == nlog && g.splits == splits) {
+      LE_CK(cudaGraphLaunch(g.exec, E->stream));
+      return true;
+    }
+  if (E->tc_graphs.size() >= 64) return tc_step(E, n, 0, nlog, max_pos);  // plenty of shapes: launch directly
+  LE_CK(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
+  const bool ok = tc_step(E, n, 0, nlog, max_pos);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(E->stream, &graph);
+  if (!ok || ce != cudaSuccess || graph == nullptr) {
+    if (graph) cudaGraphDestroy(graph);
+    E->err = std::string("batched step capture failed: ") + cudaGetErrorString(ce);
+    return false;
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) { E->err = cudaGetErrorString(ie); return false; }
+  E->tc_graphs.push_back({n, nlog, splits, exec});
+  LE_CK(cudaGraphLaunch(exec, E->stream));
+  return true;
+}
+
 // Chunked prefill of `count` tokens of slot 0 at positions start .. start+count-1.
 static bool tc_prefill(Engine* E, const int32_t* ids, size_t count, size_t start, bool last_logits) {
   std::vector<int32_t> pos(E->tc_T), slot(E->tc_T, 0);
@@ -935,6 +966,7 @@ static void destroy(Engine* E) {
   DeviceGuard dg(E->device);
   if (E->stream) cudaStreamSynchronize(E->stream);
   for (auto& g : E->g_fwd) if (g) cudaGraphExecDestroy(g);
+  for (auto& g : E->tc_graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
   if (E->g_gen) cudaGraphExecDestroy(E->g_gen);
   for (auto& ev : E->ring_ev) if (ev) cudaEventDestroy(ev);
   void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged, E->d_ctrl};
@@ -1231,7 +1263,7 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
   DeviceGuard dg(E->device);
   if (E->tc) {
     if (!tc_upload_rows(E, tokens, positions, slots, n)) return -1;
-    if (!tc_step(E, n, 0, compute_logits ? n : 0, *std::max_element(positions, positions + n))) return -1;
+    if (!tc_step_graph(E, n, compute_logits ? n : 0, *std::max_element(positions, positions + n))) return -1;
     if (!persistent_ok(E)) return -1;
     E->logits_on_host_fresh = false;
     if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
