@@ -119,11 +119,14 @@ int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_token, siz
  * cache up to its own position, including rows of the same call.  n <= max_batch, or, on the
  * tensor-core batched path (llama_engine_batch_path() == 1) and without logits, up to
  * max(max_batch, prefill chunk) rows, e.g. several prompt positions of many slots at once.
- * compute_logits != 0 also runs the lm_head for every row.  Returns 0 or -1. */
+ * compute_logits != 0 also runs the lm_head for every row.  Stream-ordered: returns once the
+ * step is queued (0), or -1 on bad arguments; a device error of the step is reported by the next
+ * call that waits for it (argmax_batch, get_logits_batch). */
 int llama_engine_forward_batch(llama_engine_t engine, const int32_t* tokens, const int32_t* positions,
                                const int32_t* slots, int n, int compute_logits);
 
-/* Greedy ids (first index among equal maxima) of the n rows of the last forward_batch. */
+/* Greedy ids (first index among equal maxima) of the n rows of the last forward_batch.
+ * Waits for the step; -1 on bad arguments or a device error. */
 int llama_engine_argmax_batch(llama_engine_t engine, int32_t* out_tokens, int n);
 
 /* Host pointer to the logits of row `row` of the last forward_batch (vocab_size floats,

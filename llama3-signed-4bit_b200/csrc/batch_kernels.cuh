@@ -9,6 +9,7 @@
 
 #include "decode_kernels.cuh"
 #include "persistent.cuh"
+#include "tc_gemm.cuh"
 
 namespace le {
 
@@ -67,7 +68,8 @@ __global__ void __launch_bounds__(128)
     k_attn_batch(const float* __restrict__ q, int q_dim, float* __restrict__ kc, float* __restrict__ vc,
                  size_t slot_stride, int kv_dim, const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
                  float* __restrict__ out, float* __restrict__ part, const float* __restrict__ qkv, int nsplit,
-                 size_t split_stride, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin) {
+                 size_t split_stride, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
+                 uint8_t* __restrict__ img) {
   // three-stage ring of K / V tiles (two tiles in flight while one is used)
   extern __shared__ __align__(16) float attn_smem[];
   float (*sk)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem);
@@ -76,6 +78,7 @@ __global__ void __launch_bounds__(128)
   __shared__ __align__(16) float sp[4][32];  // softmax numerators [head][position] of this tile
   __shared__ float salpha[4], sl[4], sm[4];  // per head: rescale of this tile, final sum and max
   __shared__ __align__(16) float sqkv[6][64];  // with qkv: q of the 4 heads, k and v of this token
+  __shared__ float sbs[4][2];                  // with img: per warp, partial sums of the two blocks
   const int t = blockIdx.x, g = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P_all = pos[t] + 1;
@@ -227,8 +230,35 @@ __global__ void __launch_bounds__(128)
     return;
   }
   const float inv = 1.0f / sl[ph];
+  const float a0 = o0 * inv, a1 = o1 * inv;
+  if (img != nullptr) {
+    // the o-proj GEMM input, written directly in the k_tc_stage image layout: bf16 hi / lo parts
+    // of the element pair at its place in the 8-element run, and the 128-block sums
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(a0, a1);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(a0 - __low2float(hh), a1 - __high2float(hh));
+    const int e = (4 * g + ph) * LE_HEAD_DIM + 16 * warp + 2 * dp;
+    const int i0 = e & ~7, j = (e & 7) >> 1;
+    const int tt = t / tc::kTok, tr = t % tc::kTok, kbt = q_dim >> 7;
+    const int kb = i0 >> 7, kk = i0 & 127, atom = kk >> 6, c = (kk & 63) >> 3;
+    uint8_t* im = img + ((size_t)tt * kbt + kb) * tc::kImgBytes;
+    const size_t o = (size_t)atom * 2 * tc::kAtom + tr * 128 + ((c ^ (tr & 7)) << 4) + 4 * j;
+    *reinterpret_cast<__nv_bfloat162*>(im + o) = hh;
+    *reinterpret_cast<__nv_bfloat162*>(im + tc::kAtom + o) = ll;
+    // lanes 0..15 hold heads 4g, 4g+1 (block 2g), lanes 16..31 heads 4g+2, 4g+3 (block 2g+1)
+    float bs = a0 + a1;
+#pragma unroll
+    for (int o2 = 8; o2 > 0; o2 >>= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o2);
+    if ((lane & 15) == 0) sbs[warp][lane >> 4] = bs;
+    __syncthreads();
+    if (threadIdx.x < 2) {
+      const int b = threadIdx.x;
+      const float tot = (sbs[0][b] + sbs[1][b]) + (sbs[2][b] + sbs[3][b]);
+      reinterpret_cast<float*>(img + ((size_t)tt * kbt + 2 * g + b) * tc::kImgBytes + tc::kOffXs)[tr] = tot;
+    }
+    return;
+  }
   float* op = out + (size_t)t * q_dim + (size_t)(4 * g + ph) * LE_HEAD_DIM + 16 * warp + 2 * dp;
-  *reinterpret_cast<float2*>(op) = make_float2(o0 * inv, o1 * inv);
+  *reinterpret_cast<float2*>(op) = make_float2(a0, a1);
 }
 
 // Merges the S position-range partials of k_attn_batch: out = sum_z o_z e^(m_z - M) / sum_z

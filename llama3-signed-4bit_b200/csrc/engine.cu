@@ -766,12 +766,14 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
                                                                          E->t_attn);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
+      // without position splits the attention kernel writes the o-proj input image itself
       k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, kAttnSmem, s>>>(
           E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn, E->t_attn_part, E->t_qkv, sq, qkv_stride,
-          E->rope_cos, E->rope_sin);
+          E->rope_cos, E->rope_sin, attn_splits == 1 ? E->img_d : nullptr);
       if (attn_splits > 1) k_attn_combine<<<n, 256, 0, s>>>(E->t_attn_part, E->kv_heads, attn_splits, dim, E->t_attn);
     }
-    k_tc_stage<<<dim3(n, dim / 2048), 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
+    if (prefill_p0 >= 0 || attn_splits > 1)
+      k_tc_stage<<<dim3(n, dim / 2048), 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
     const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
     k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, so, part_stride, D.post_norm, 0, dim, E->img_d);
     tc_launch(E, Y.gu, E->img_d, n, 1, rows(E->t_gu, 2 * ffn, 2 * ffn, 0));
@@ -828,6 +830,15 @@ static bool tc_prefill(Engine* E, const int32_t* ids, size_t count, size_t start
     const bool lg = last_logits && c0 + n == count;
     if (!tc_step(E, n, n - 1, lg ? 1 : 0, (int)(start + c0) + n - 1, (int)(start + c0))) return false;
   }
+  return true;
+}
+
+static bool persistent_ok(Engine* E);
+// Synchronises the stream and reports a device error recorded by the last steps.
+static bool sync_ok(Engine* E) {
+  if (E->persist || E->tc) return persistent_ok(E);
+  const cudaError_t ce = cudaStreamSynchronize(E->stream);
+  if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return false; }
   return true;
 }
 
@@ -1263,8 +1274,9 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
   DeviceGuard dg(E->device);
   if (E->tc) {
     if (!tc_upload_rows(E, tokens, positions, slots, n)) return -1;
+    // stream-ordered: a device error (the GEMM's bounded waits) is reported by the next call
+    // that synchronises (argmax_batch, get_logits_batch, get_logits, sample)
     if (!tc_step_graph(E, n, compute_logits ? n : 0, *std::max_element(positions, positions + n))) return -1;
-    if (!persistent_ok(E)) return -1;
     E->logits_on_host_fresh = false;
     if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
     return 0;
@@ -1368,7 +1380,7 @@ LE_API int llama_engine_argmax_batch(llama_engine_t engine, int32_t* out_tokens,
   if (n > E->max_batch) return -1;
   DeviceGuard dg(E->device);
   if (cudaMemcpyAsync(out_tokens, E->am_result, (size_t)n * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess) return -1;
-  return cudaStreamSynchronize(E->stream) == cudaSuccess ? 0 : -1;
+  return sync_ok(E) ? 0 : -1;  // reports a device error of the step
 }
 
 LE_API const float* llama_engine_get_logits_batch(llama_engine_t engine, int row) {
@@ -1380,7 +1392,7 @@ LE_API const float* llama_engine_get_logits_batch(llama_engine_t engine, int row
   if (cudaMemcpyAsync(h, E->logits + (size_t)row * E->vocab, (size_t)E->vocab * 4, cudaMemcpyDeviceToHost,
                       E->stream) != cudaSuccess)
     return nullptr;
-  if (cudaStreamSynchronize(E->stream) != cudaSuccess) return nullptr;
+  if (!sync_ok(E)) return nullptr;  // reports a device error of the step
   if (row == 0) E->logits_on_host_fresh = true;
   return h;
 }
