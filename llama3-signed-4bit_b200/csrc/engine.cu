@@ -228,7 +228,7 @@ struct Engine {
   uint32_t* tc_err = nullptr;  // device error word of the tensor-core GEMM
   // decode steps of the batched path replayed as CUDA graphs, one per (rows, logits rows,
   // attention splits); the rows' ids, positions and slots are read from t_idx
-  struct TcGraph { int n, nlog, splits; cudaGraphExec_t exec; };
+  struct TcGraph { int n, nlog, splits; bool fold; cudaGraphExec_t exec; };
   std::vector<TcGraph> tc_graphs;
   // token scoring (llama_engine_score_tokens): logits of a chunk's rows, targets, results
   float* sc_logits = nullptr;   // [kScoreRows][vocab], allocated on first use
@@ -725,8 +725,10 @@ static bool tc_upload_rows(Engine* E, const int32_t* tok, const int32_t* pos, co
 // rows [lrow0, lrow0 + nlog) into logits rows 0..nlog-1 and am_result[0..nlog-1].
 // With prefill_p0 >= 0 the rows are consecutive positions prefill_p0 .. of slot 0 (a prefill
 // chunk) and attention runs query-tiled.
+// fold: every row is a different slot, so no row reads another row's new k / v; RoPE and the
+// KV append then run inside the decode attention kernel.
 static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int prefill_p0 = -1,
-                    float* logits_out = nullptr) {
+                    float* logits_out = nullptr, bool fold = false) {
   float* const lg_out = logits_out ? logits_out : E->logits;
   using namespace tc;
   const int dim = (int)E->dim, ffn = (int)E->ffn, kvd = (int)E->kv_dim;
@@ -759,17 +761,18 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
                              rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
-    if (prefill_p0 >= 0) {
+    if (prefill_p0 >= 0 || !fold)
       k_rope_append<<<dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), 256, 0, s>>>(
           E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
+    if (prefill_p0 >= 0) {
       k_attn_prefill_tc<<<dim3(E->kv_heads, (n + 15) / 16), 128, 0, s>>>(E->t_q, dim, kc, vc, kvd, prefill_p0, n,
                                                                          E->t_attn);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
       // without position splits the attention kernel writes the o-proj input image itself
       k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, kAttnSmem, s>>>(
-          E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn, E->t_attn_part, E->t_qkv, sq, qkv_stride,
-          E->rope_cos, E->rope_sin, attn_splits == 1 ? E->img_d : nullptr);
+          E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn, E->t_attn_part, fold ? E->t_qkv : nullptr,
+          sq, qkv_stride, E->rope_cos, E->rope_sin, attn_splits == 1 ? E->img_d : nullptr);
       if (attn_splits > 1) k_attn_combine<<<n, 256, 0, s>>>(E->t_attn_part, E->kv_heads, attn_splits, dim, E->t_attn);
     }
     if (prefill_p0 >= 0 || attn_splits > 1)
@@ -794,16 +797,16 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
 }
 
 // A decode step (rows already uploaded) through a cached CUDA graph of tc_step's launches.
-static bool tc_step_graph(Engine* E, int n, int nlog, int max_pos) {
+static bool tc_step_graph(Engine* E, int n, int nlog, int max_pos, bool fold) {
   const int splits = std::max(1, std::min(kAttnMaxSplits, (max_pos + 1) / 1024));
   for (const auto& g : E->tc_graphs)
-    if (g.n == n && g.nlog == nlog && g.splits == splits) {
+    if (g.n == n && g.nlog == nlog && g.splits == splits && g.fold == fold) {
       LE_CK(cudaGraphLaunch(g.exec, E->stream));
       return true;
     }
-  if (E->tc_graphs.size() >= 64) return tc_step(E, n, 0, nlog, max_pos);  // plenty of shapes: launch directly
+  if (E->tc_graphs.size() >= 64) return tc_step(E, n, 0, nlog, max_pos, -1, nullptr, fold);  // launch directly
   LE_CK(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
-  const bool ok = tc_step(E, n, 0, nlog, max_pos);
+  const bool ok = tc_step(E, n, 0, nlog, max_pos, -1, nullptr, fold);
   cudaGraph_t graph = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(E->stream, &graph);
   if (!ok || ce != cudaSuccess || graph == nullptr) {
@@ -815,7 +818,7 @@ static bool tc_step_graph(Engine* E, int n, int nlog, int max_pos) {
   const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
   if (ie != cudaSuccess) { E->err = cudaGetErrorString(ie); return false; }
-  E->tc_graphs.push_back({n, nlog, splits, exec});
+  E->tc_graphs.push_back({n, nlog, splits, fold, exec});
   LE_CK(cudaGraphLaunch(exec, E->stream));
   return true;
 }
@@ -1276,7 +1279,13 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
     if (!tc_upload_rows(E, tokens, positions, slots, n)) return -1;
     // stream-ordered: a device error (the GEMM's bounded waits) is reported by the next call
     // that synchronises (argmax_batch, get_logits_batch, get_logits, sample)
-    if (!tc_step_graph(E, n, compute_logits ? n : 0, *std::max_element(positions, positions + n))) return -1;
+    // RoPE / KV append inside attention only when no slot repeats (a row may read the k / v
+    // that an earlier row of the same call appends)
+    std::vector<uint8_t> seen(E->max_batch, 0);
+    bool distinct = true;
+    for (int i = 0; i < n && distinct; ++i) distinct = !seen[slots[i]]++;
+    if (!tc_step_graph(E, n, compute_logits ? n : 0, *std::max_element(positions, positions + n), distinct))
+      return -1;
     E->logits_on_host_fresh = false;
     if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
     return 0;

@@ -200,3 +200,38 @@ def test_long_prefill_and_split_attention(pkg, bindings, small_model, oracle_lib
     finally:
         oracle_lib.orc_free(o)
         eng.close()
+
+
+def test_forward_batch_several_positions_per_slot(pkg, bindings, small_model, oracle_lib):
+    """Calls that carry 8 consecutive positions of each of 8 slots (64 rows; later rows read the
+    k / v that earlier rows of the same call append), then decode steps with one row per slot
+    (k / v appended by the attention kernel itself); two slots replayed on the oracle."""
+    n, L, per = 8, 40, 8
+    eng = pkg.LlamaEngine(str(small_model), bindings, device=0, max_batch=n, max_seq_len=256)
+    check = (0, 5)
+    orcs = {i: oracle_lib.orc_create(str(small_model).encode()) for i in check}
+    try:
+        assert eng.batch_path == "tensor-core"
+        vocab = eng.vocab_size
+        prompts = np.random.default_rng(123).integers(0, vocab, (n, L)).astype(np.int32)
+        for p0 in range(0, L - 1, per):
+            ps = list(range(p0, min(L - 1, p0 + per)))
+            eng.forward_batch([int(prompts[s, p]) for p in ps for s in range(n)], [p for p in ps for s in range(n)],
+                              [s for p in ps for s in range(n)], False)
+        for i in check:
+            oracle_lib.orc_prefill(orcs[i], fptr(prompts[i]), L - 1, 0, 0)
+        toks = [int(t) for t in prompts[:, -1]]
+        for step in range(3):
+            pos = L - 1 + step
+            eng.forward_batch(toks, [pos] * n, list(range(n)), True)
+            am = eng.argmax_batch(n)
+            for i in check:
+                oracle_lib.orc_forward_token(orcs[i], toks[i], pos, 1)
+                ref = _oracle_logits(oracle_lib, orcs[i], vocab)
+                assert rel_max_err(eng.get_logits_batch(i), ref) <= LOGIT_RTOL, (step, i)
+                assert am[i] == int(np.argmax(ref)), (step, i)
+            toks = am
+    finally:
+        for o in orcs.values():
+            oracle_lib.orc_free(o)
+        eng.close()
