@@ -73,8 +73,10 @@ int llama_engine_prefill(llama_engine_t engine, const int32_t* token_ids, size_t
 
 /* src/llama_engine.h:47, impl :1129-1133 and :784-839.  temperature <= 0.01: greedy argmax
  * (first index among equal maxima).  Otherwise the logits are overwritten in place with
- * probabilities (temperature, softmax), the 64 most probable ids are kept in descending order,
- * and libc rand() draws within the top_p mass, as in the reference.  0 for a NULL handle. */
+ * probabilities (temperature, softmax) on the device, 64 candidates are chosen by the
+ * reference's insertion walk (ids 0..63 first, then every id that beats the list's last entry,
+ * replayed on the device), and libc rand() draws within the top_p mass on the host, as in the
+ * reference.  0 for a NULL handle. */
 int32_t llama_engine_sample(llama_engine_t engine, float temperature, float top_p);
 
 /* src/llama_engine.h:50, impl :1135-1138.  Host pointer to vocab_size floats (see top). */

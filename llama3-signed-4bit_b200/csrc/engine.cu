@@ -1093,6 +1093,18 @@ static bool sync_logits(Engine* E) {
 
 // Temperature / top-p sampling.  The probabilities are formed on the device; the candidate walk of
 // sample_top_p (src/llama_engine.cpp:808-838) runs over the host mirror, with libc rand().
+// The draw over the candidates (src/llama_engine.cpp:824-838): the shortest prefix whose mass
+// reaches top_p, a libc rand() point in it, the first candidate whose running mass reaches it.
+static int32_t draw_top_p(const int32_t* ids, const float* vals, size_t k, float top_p) {
+  float cum = 0.0f;
+  size_t last = 0;
+  for (size_t i = 0; i < k; ++i) { cum += vals[i]; last = i; if (cum >= top_p) break; }
+  const float r = (static_cast<float>(rand()) / static_cast<float>(RAND_MAX)) * cum;
+  float run = 0.0f;
+  for (size_t i = 0; i <= last; ++i) { run += vals[i]; if (run >= r) return ids[i]; }
+  return ids[0];
+}
+
 static int32_t sample_top_p_host(float* p, size_t vocab, float top_p) {
   const size_t k = std::min<size_t>(64, vocab);
   int32_t ids[64];
@@ -1106,13 +1118,7 @@ static int32_t sample_top_p_host(float* p, size_t vocab, float top_p) {
       vals[q] = v; ids[q] = (int32_t)i;
     }
   }
-  float cum = 0.0f;
-  size_t last = 0;
-  for (size_t i = 0; i < k; ++i) { cum += vals[i]; last = i; if (cum >= top_p) break; }
-  const float r = (static_cast<float>(rand()) / static_cast<float>(RAND_MAX)) * cum;
-  float run = 0.0f;
-  for (size_t i = 0; i <= last; ++i) { run += vals[i]; if (run >= r) return ids[i]; }
-  return ids[0];
+  return draw_top_p(ids, vals, k, top_p);
 }
 
 }  // namespace le
@@ -1190,8 +1196,18 @@ LE_API int32_t llama_engine_sample(llama_engine_t engine, float temperature, flo
     return id;
   }
   if (!softmax_in_place(E, temperature)) return 0;
-  if (!sync_logits(E)) return 0;
-  return sample_top_p_host(E->h_logits, E->vocab, top_p);
+  if (E->vocab < 64) {
+    if (!sync_logits(E)) return 0;
+    return sample_top_p_host(E->h_logits, E->vocab, top_p);
+  }
+  // the 64 candidates on the device; the draw (libc rand(), :824-838) on the host
+  int32_t* d_ids = reinterpret_cast<int32_t*>(E->red + 1536);
+  float* d_vals = E->red + 1600;
+  k_topk64_walk<<<1, 256, 0, E->stream>>>(E->logits, (int)E->vocab, d_ids, d_vals);
+  if (cudaGetLastError() != cudaSuccess) return 0;
+  if (cudaMemcpyAsync(E->h_small, d_ids, 128 * 4, cudaMemcpyDeviceToHost, E->stream) != cudaSuccess) return 0;
+  if (!sync_ok(E)) return 0;
+  return draw_top_p(E->h_small, reinterpret_cast<const float*>(E->h_small + 64), 64, top_p);
 }
 
 LE_API const float* llama_engine_get_logits(llama_engine_t engine) {

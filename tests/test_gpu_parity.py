@@ -310,3 +310,69 @@ def test_persistent_matches_kernel_chain(pkg, bindings, small_model, monkeypatch
     finally:
         a.close()
         b.close()
+
+
+def _reference_walk(p, top_p, r_int):
+    """sample_top_p's candidate walk and draw (src/llama_engine.cpp:808-838) in float32 over the
+    probabilities p, with the libc rand() value r_int."""
+    k = min(64, len(p))
+    pl = [float(v) for v in p]  # float32 values compare the same as doubles
+    vals = pl[:k]
+    ids = list(range(k))
+    for i in range(k, len(pl)):
+        v = pl[i]
+        if v > vals[k - 1]:
+            q = k - 1
+            while q > 0 and v > vals[q - 1]:
+                vals[q], ids[q] = vals[q - 1], ids[q - 1]
+                q -= 1
+            vals[q], ids[q] = v, i
+    cum = np.float32(0.0)
+    last = 0
+    for i in range(k):
+        cum = np.float32(cum + np.float32(vals[i]))
+        last = i
+        if cum >= np.float32(top_p):
+            break
+    r = np.float32(np.float32(r_int) / np.float32(2147483647)) * cum
+    run = np.float32(0.0)
+    for i in range(last + 1):
+        run = np.float32(run + np.float32(vals[i]))
+        if run >= r:
+            return ids[i]
+    return ids[0]
+
+
+def test_temperature_sampling_matches_walk(small_engine):
+    """The 64 candidates are built on the device and the draw runs on the host: for several
+    temperatures, top_p values and rand() seeds the sampled id equals the reference's walk and
+    draw restated over the same probabilities (the ones get_logits returns after sampling)."""
+    eng = small_engine
+    libc = ctypes.CDLL(None)
+    libc.rand.restype = ctypes.c_int
+    cases = [(0.8, 0.9), (1.3, 0.95), (0.3, 0.5), (2.0, 1.0), (1.0, 0.2)]
+    for j, (temp, top_p) in enumerate(cases):
+        for seed in (1, 7, 12345):
+            eng.forward_token(100 + j, 5, True)
+            libc.srand(seed)
+            sid = eng.sample(temp, top_p)
+            probs = eng.get_logits()
+            libc.srand(seed)
+            assert sid == _reference_walk(probs, top_p, libc.rand()), (temp, top_p, seed)
+
+
+def test_temperature_sampling_full_vocab(pkg, bindings, full_model):
+    """The device candidate walk over the 1B model's 128,256 probabilities (32 staged tiles)."""
+    eng = pkg.LlamaEngine(str(full_model), bindings)
+    try:
+        libc = ctypes.CDLL(None)
+        libc.rand.restype = ctypes.c_int
+        for temp, top_p, seed in [(0.8, 0.9, 3), (1.5, 0.99, 11), (0.6, 0.7, 29)]:
+            eng.forward_token(1000, 0, True)
+            libc.srand(seed)
+            sid = eng.sample(temp, top_p)
+            probs = eng.get_logits()
+            libc.srand(seed)
+            assert sid == _reference_walk(probs, top_p, libc.rand()), (temp, top_p, seed)
+    finally:
+        eng.close()
