@@ -59,9 +59,7 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ float attn_sum_planes(const float* p, int nsplit, size_t stride) {
-  float v = p[0];
-  for (int s = 1; s < nsplit; ++s) v += p[s * stride];
-  return v;
+  return tc::sum_planes(p, nsplit, stride);
 }
 
 __global__ void __launch_bounds__(128)

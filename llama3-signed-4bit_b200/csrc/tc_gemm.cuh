@@ -596,7 +596,22 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
           const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
           s8[0] = p0.x; s8[1] = p0.y; s8[2] = p0.z; s8[3] = p0.w; s8[4] = p1.x; s8[5] = p1.y; s8[6] = p1.z; s8[7] = p1.w;
         }
-        for (int sp = 1; sp < nsplit; ++sp) {
+        // planes in order, three planes' loads in flight at a time
+        int sp = 1;
+        for (; sp + 2 < nsplit; sp += 3) {
+          float4 q[3][2];
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            q[j][0] = *reinterpret_cast<const float4*>(pp + (sp + j) * split_stride);
+            q[j][1] = *reinterpret_cast<const float4*>(pp + (sp + j) * split_stride + 4);
+          }
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            s8[0] += q[j][0].x; s8[1] += q[j][0].y; s8[2] += q[j][0].z; s8[3] += q[j][0].w;
+            s8[4] += q[j][1].x; s8[5] += q[j][1].y; s8[6] += q[j][1].z; s8[7] += q[j][1].w;
+          }
+        }
+        for (; sp < nsplit; ++sp) {
           const float4 p0 = *reinterpret_cast<const float4*>(pp + sp * split_stride);
           const float4 p1 = *reinterpret_cast<const float4*>(pp + sp * split_stride + 4);
           s8[0] += p0.x; s8[1] += p0.y; s8[2] += p0.z; s8[3] += p0.w;
@@ -660,9 +675,18 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
 // rotated q to q_out[t], rotated k and v into the cache row (slot[t], pos[t]).  Grid (tokens,
 // ceil((q_dim + kv_dim) / 2 + kv_dim) / 256)), one item per thread.
 // ---------------------------------------------------------------------------------------------
+// Sum of the nsplit planes in plane order; four loads in flight at a time.
 __device__ __forceinline__ float sum_planes(const float* p, int nsplit, size_t stride) {
   float v = p[0];
-  for (int s = 1; s < nsplit; ++s) v += p[s * stride];
+  int s = 1;
+  for (; s + 3 < nsplit; s += 4) {
+    const float a = p[s * stride], b = p[(s + 1) * stride], c = p[(s + 2) * stride], d = p[(s + 3) * stride];
+    v += a;
+    v += b;
+    v += c;
+    v += d;
+  }
+  for (; s < nsplit; ++s) v += p[s * stride];
   return v;
 }
 __global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ qkv, int nsplit, size_t split_stride,
