@@ -226,6 +226,7 @@ struct Engine {
   ArgmaxPart* t_am = nullptr;  // [tc_T][tc_am_parts]
   int tc_am_parts = 0;
   uint32_t* tc_err = nullptr;  // device error word of the tensor-core GEMM
+  bool tc_dirty = true;        // a batched step ran since tc_err was last read
   // decode steps of the batched path replayed as CUDA graphs, one per (rows, logits rows,
   // attention splits); the rows' ids, positions and slots are read from t_idx
   struct TcGraph { int n, nlog, splits; bool fold; cudaGraphExec_t exec; };
@@ -793,6 +794,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     }
   }
   LE_CK(cudaGetLastError());
+  E->tc_dirty = true;
   return true;
 }
 
@@ -802,6 +804,7 @@ static bool tc_step_graph(Engine* E, int n, int nlog, int max_pos, bool fold) {
   for (const auto& g : E->tc_graphs)
     if (g.n == n && g.nlog == nlog && g.splits == splits && g.fold == fold) {
       LE_CK(cudaGraphLaunch(g.exec, E->stream));
+      E->tc_dirty = true;
       return true;
     }
   if (E->tc_graphs.size() >= 64) return tc_step(E, n, 0, nlog, max_pos, -1, nullptr, fold);  // launch directly
@@ -845,23 +848,36 @@ static bool sync_ok(Engine* E) {
   return true;
 }
 
-// Reads the persistent kernel's error word (after the stream has been synchronised).
-// Also reads the tensor-core GEMM's error word.
-static bool persistent_ok(Engine* E) {
-  if (!E->persist && !E->tc) return true;
+// Device error words of the persistent kernel and of the tensor-core GEMM: the copies are queued
+// behind the work (the GEMM's only when a batched step ran since it was last read) and checked
+// after the caller's synchronisation, so that a token id and its status cost one wait.
+static bool enqueue_status(Engine* E) {
   if (E->persist)
     LE_CK(cudaMemcpyAsync(E->h_err, &E->d_ctrl->error, 2 * sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
-  if (E->tc) LE_CK(cudaMemcpyAsync(E->h_err + 2, E->tc_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
-  LE_CK(cudaStreamSynchronize(E->stream));
+  if (E->tc && E->tc_dirty)
+    LE_CK(cudaMemcpyAsync(E->h_err + 2, E->tc_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, E->stream));
+  return true;
+}
+static bool check_status(Engine* E) {
+  const bool tc_read = E->tc && E->tc_dirty;
+  E->tc_dirty = false;
   if (E->persist && E->h_err[0] != 0) {
     E->err = "persistent decode kernel: a dependency wait timed out (code " + std::to_string(E->h_err[1]) + ")";
     return false;
   }
-  if (E->tc && E->h_err[2] != 0) {
+  if (tc_read && E->h_err[2] != 0) {
     E->err = "tensor-core GEMM: a pipeline wait timed out (code " + std::to_string(E->h_err[2]) + ")";
+    E->tc_dirty = true;  // keep reporting it
     return false;
   }
   return true;
+}
+
+static bool persistent_ok(Engine* E) {
+  if (!E->persist && !E->tc) return true;
+  if (!enqueue_status(E)) return false;
+  LE_CK(cudaStreamSynchronize(E->stream));
+  return check_status(E);
 }
 
 static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
@@ -1075,8 +1091,9 @@ static bool greedy(Engine* E, int32_t* out) {
     E->argmax_valid = true;
   }
   LE_CK(cudaMemcpyAsync(E->h_small, E->am_result, 4, cudaMemcpyDeviceToHost, E->stream));
-  LE_CK(cudaStreamSynchronize(E->stream));
-  if (!persistent_ok(E)) return false;
+  if (!enqueue_status(E)) return false;
+  LE_CK(cudaStreamSynchronize(E->stream));  // one wait for the id and the error words
+  if (!check_status(E)) return false;
   *out = E->h_small[0];
   return true;
 }
