@@ -10,6 +10,10 @@ steps.  With N GPUs every rank decodes its own sequence (independent replicas, w
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+The same line carries ``batch64`` (64 sequences decoded from position 511, and 8 x 2048-id
+prefills; rank 0 of a 1-GPU run) and ``box256`` (256 sequences per GPU with KV for 4096 positions,
+greedy steps timed near position 1023 and near 4095; every rank, weak scaling).
+
 Prints one JSON line on rank 0.  ``value`` is device-resident throughput (CUDA events around K
 graph steps fed by the on-device argmax), ``e2e`` is the same loop through the reference C ABI
 (forward_token + sample per step from the host).  ``--impl reference`` times the reference
@@ -316,6 +320,9 @@ def run_ours(args, rank, world, local_rank):
         eng_b1 = eng
         batched = run_batched(args, model, shape, local_rank)
         eng = eng_b1
+    box = None
+    if args.box_steps > 0:  # every rank: its own 256 sequences
+        box = run_box(args, model, shape, local_rank, world)
     trace = None
     if persistent and rank == 0 and args.trace:
         tr = load_package().trace
@@ -346,6 +353,7 @@ def run_ours(args, rank, world, local_rank):
                     "wall_s": round(wall, 4)},
             "gpu_launches": launches_timed, "decode_path": eng.decode_path, "clocks": clocks,
             **({"batch64": batched} if batched else {}),
+            **({"box256": box} if box else {}),
             **({"phase_trace": trace} if trace else {}),
         }
     eng.close()
@@ -444,6 +452,109 @@ def run_batched(args, model, shape, local_rank):
     return out
 
 
+def run_box(args, model, shape, local_rank, world):
+    """Box-scale decode, one engine per rank: 256 sequences per GPU (KV for 4096 positions each,
+    68.7 GB), 1024-id prompts fed through forward_batch (4 positions x 256 sequences per call),
+    then greedy steps of all 256 sequences through forward_batch + argmax_batch.  Two windows of
+    box_steps steps are timed: one from position 1023 and one ending at position 4094, after the
+    KV of every sequence has been filled up to it by the same batched forward (random ids).  A
+    step's bytes are affine in the position (weights + 256 * 64 KiB per position), so the mean of
+    the two windows is the mean step of the whole 1024 -> 4096 decode.  Every rank runs the same
+    collective steps; times are the max over ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    pkg = load_package()
+    B, P, MAXS = 256, 1024, 4096
+    S = max(1, min(args.box_steps, 256))
+    bindings = pkg.LlamaEngineBindings()
+    eng = pkg.LlamaEngine(str(model), bindings, device=local_rank, max_batch=B, max_seq_len=MAXS)
+    out = {"batch_path": eng.batch_path}
+    if eng.batch_path != "tensor-core":
+        eng.close()
+        return out
+    lib = bindings.lib
+    stream = torch.cuda.ExternalStream(lib.llama_engine_get_stream(eng.handle))
+    rank = dist.get_rank() if world > 1 else 0
+    rng = np.random.default_rng(4000 + rank)
+    slots = list(range(B))
+    per = 1024 // B
+
+    def fill(p_begin, p_end, ids):
+        """KV of positions [p_begin, p_end) of every sequence, ids[s, p] at (s, p).  Rows are
+        sequence-major, so the rows of one sequence read its K / V rows as neighbouring CTAs."""
+        for p0 in range(p_begin, p_end, per):
+            ps = list(range(p0, min(p_end, p0 + per)))
+            eng.forward_batch([int(ids[s, p]) for s in range(B) for p in ps], [p for s in range(B) for p in ps],
+                              [s for s in range(B) for p in ps], False)
+
+    def window(pos0, toks):
+        """3 warm-up steps, then S timed greedy steps from pos0; returns (ms, next ids)."""
+        for w in range(3):
+            eng.forward_batch(toks, [pos0 + w] * B, slots, True)
+            eng.argmax_batch(B)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        w0 = time.perf_counter()
+        t = toks
+        for i in range(S):
+            eng.forward_batch(t, [pos0 + i] * B, slots, True)
+            t = eng.argmax_batch(B)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times = [e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3]
+        if world > 1:
+            tt = torch.tensor(times, device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            times = [float(x) for x in tt.tolist()]
+        return times, t
+
+    ids = rng.integers(0, shape.vocab, (B, MAXS)).astype(np.int32)
+    f0 = time.perf_counter()
+    fill(0, P - 1, ids)
+    torch.cuda.synchronize()
+    fill_s = time.perf_counter() - f0
+    early_pos = P - 1
+    (ms_a, wall_a), _ = window(early_pos, [int(x) for x in ids[:, P - 1]])
+    late_pos = MAXS - 1 - S
+    f0 = time.perf_counter()
+    fill(early_pos + S, late_pos, ids)
+    torch.cuda.synchronize()
+    fill_s += time.perf_counter() - f0
+    (ms_b, wall_b), _ = window(late_pos, [int(x) for x in ids[:, late_pos]])
+    eng.close()
+    peak, peak_kind = hbm_peak()
+    kv_row = shape.layers * shape.kv_dim * 4 * 2
+
+    def step_bytes(p):
+        return shape.weight_bytes() + B * kv_row * (p + 2)
+
+    bytes_a = sum(step_bytes(early_pos + i) for i in range(S))
+    bytes_b = sum(step_bytes(late_pos + i) for i in range(S))
+    mean_ms = (ms_a + ms_b) / (2 * S)
+    mean_wall = (wall_a + wall_b) / (2 * S)
+    gbs = (bytes_a + bytes_b) / ((ms_a + ms_b) / 1e3) / 1e9
+    out.update({
+        "value": round(world * B / (mean_ms / 1e3), 1), "unit": "tok/s", "n_gpus": world, "scaling": "weak",
+        "ms_per_step": round(mean_ms, 4),
+        "workload": (f"decode-b256 box scale: {B} sequences per GPU, 1024-id prompts, KV for {MAXS} positions; "
+                     f"greedy steps at positions {early_pos}..{early_pos + S - 1} and {late_pos}..{late_pos + S - 1} "
+                     f"(mean = mean step of the 1024 -> 4096 decode)"),
+        "windows_ms_per_step": {str(early_pos): round(ms_a / S, 4), str(late_pos): round(ms_b / S, 4)},
+        "e2e": {"value": round(world * B / (mean_wall / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 12,
+                "d2h_bytes_per_step": B * 4, "api": "llama_engine_forward_batch + llama_engine_argmax_batch per step"},
+        "step_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(gbs / peak, 4), "peak_source": peak_kind,
+                          "bytes_per_step": int((bytes_a + bytes_b) / (2 * S))},
+        "fill_s": round(fill_s, 2),
+    })
+    return out
+
+
 def read_traffic(kernel_phase: str):
     """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic_per_launch.txt"
@@ -492,6 +603,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--b64-steps", type=int, default=1536,
                     help="timed batch-64 decode steps from position 511 (0 = skip the batched measurements)")
+    ap.add_argument("--box-steps", type=int, default=32,
+                    help="box-scale decode (256 sequences per GPU, 1024 -> 4096): timed steps per window (0 = skip)")
     ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill measurement: sequences of 2048 ids")
     ap.add_argument("--trace", action="store_true", help="add the persistent kernel's phase timeline")
     ap.add_argument("--trace-raw", default=None, help="with --trace: save the raw trace array (.npy) here")
