@@ -12,7 +12,8 @@ steps.  With N GPUs every rank decodes its own sequence (independent replicas, w
 
 The same line carries ``batch64`` (64 sequences decoded from position 511, and 8 x 2048-id
 prefills; rank 0 of a 1-GPU run) and ``box256`` (256 sequences per GPU with KV for 4096 positions,
-greedy steps timed near position 1023 and near 4095; every rank, weak scaling).
+greedy steps timed near position 1023 and near 4095; every rank, weak scaling) and
+``gemv_sweep`` (the isolated block-128 GEMV at the model's five K x N shapes, M = 1 and 4).
 
 Prints one JSON line on rank 0.  ``value`` is device-resident throughput (CUDA events around K
 graph steps fed by the on-device argmax), ``e2e`` is the same loop through the reference C ABI
@@ -320,6 +321,7 @@ def run_ours(args, rank, world, local_rank):
         eng_b1 = eng
         batched = run_batched(args, model, shape, local_rank)
         eng = eng_b1
+    gemv = run_gemv_sweep(local_rank) if (rank == 0 and world == 1 and args.gemv_sweep) else None
     box = None
     if args.box_steps > 0:  # every rank: its own 256 sequences
         box = run_box(args, model, shape, local_rank, world)
@@ -354,6 +356,7 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": launches_timed, "decode_path": eng.decode_path, "clocks": clocks,
             **({"batch64": batched} if batched else {}),
             **({"box256": box} if box else {}),
+            **({"gemv_sweep": gemv} if gemv else {}),
             **({"phase_trace": trace} if trace else {}),
         }
     eng.close()
@@ -555,6 +558,71 @@ def run_box(args, model, shape, local_rank, world):
     return out
 
 
+def run_gemv_sweep(local_rank, reps=200):
+    """Isolated block-128 GEMV (llama_b128_gemv) at the model's five K x N shapes, M = 1 and 4:
+    nibbles uniform 0..15, step ~U(1e-3, 2e-2) and min = -8 step U(0.8, 1.2) as bf16, x ~N(0, 1).
+    Each shape cycles through enough copies of its matrix to pass 256 MB, so every call streams
+    its weights from HBM rather than L2; algorithmic bytes N*K/128*68 + M*K*4 + M*N*4 per call."""
+    import torch
+
+    pkg = load_package()
+    lib = pkg.LlamaEngineBindings().lib
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(11)
+    peak, peak_kind = hbm_peak()
+    stream = torch.cuda.current_stream(dev)
+    rows = []
+    for K, N in ((2048, 2048), (2048, 512), (2048, 8192), (8192, 2048), (2048, 128256)):
+        mat = N * K // 128 * 68
+        copies = max(1, -(-256 * 2**20 // mat))
+        mats = []
+        for _ in range(copies):
+            nib = torch.randint(0, 256, (N * K // 2,), dtype=torch.uint8, device=dev, generator=g)
+            step = torch.empty(N * K // 128, device=dev).uniform_(1e-3, 2e-2, generator=g)
+            mn = -8.0 * step * torch.empty_like(step).uniform_(0.8, 1.2, generator=g)
+            mats.append((nib, step.to(torch.bfloat16).view(torch.int16), mn.to(torch.bfloat16).view(torch.int16)))
+        for M in (1, 4):
+            x = torch.randn(M, K, device=dev, generator=g)
+            y = torch.empty(M, N, device=dev)
+
+            def call(i, st_handle):
+                nib, st, mi = mats[i % copies]
+                rc = lib.llama_b128_gemv(ctypes.c_void_p(nib.data_ptr()), ctypes.c_void_p(st.data_ptr()),
+                                         ctypes.c_void_p(mi.data_ptr()), N, K, ctypes.c_void_p(x.data_ptr()), M,
+                                         ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(st_handle))
+                if rc != 0:
+                    raise RuntimeError(f"llama_b128_gemv failed at K={K} N={N} M={M}")
+
+            for i in range(min(2 * copies, 64)):
+                call(i, stream.cuda_stream)
+            torch.cuda.synchronize()
+            # the launches are captured into a graph, so the timing is the kernels' back-to-back
+            # device time and not the host's per-call cost
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                cap = torch.cuda.current_stream().cuda_stream
+                for i in range(reps):
+                    call(i, cap)
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(3):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (3 * reps)
+            del graph
+            gbs = (mat + M * K * 4 + M * N * 4) / (us * 1e-6) / 1e9
+            rows.append({"K": K, "N": N, "M": M, "us": round(us, 2), "gbs": round(gbs, 1),
+                         "frac": round(gbs / peak, 4)})
+        del mats
+    torch.cuda.empty_cache()
+    return {"kernel": "k_gemv_mma (llama_b128_gemv)", "unit": "GB/s", "peak": peak, "peak_source": peak_kind,
+            "timing": f"CUDA graph of {reps} launches per shape, replayed 3 times, CUDA events",
+            "l2": "matrix copies cycled past 256 MB per shape", "shapes": rows}
+
+
 def read_traffic(kernel_phase: str):
     """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic_per_launch.txt"
@@ -603,6 +671,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--b64-steps", type=int, default=1536,
                     help="timed batch-64 decode steps from position 511 (0 = skip the batched measurements)")
+    ap.add_argument("--no-gemv-sweep", dest="gemv_sweep", action="store_false",
+                    help="skip the isolated GEMV sweep (five K x N shapes, M = 1 and 4)")
     ap.add_argument("--box-steps", type=int, default=32,
                     help="box-scale decode (256 sequences per GPU, 1024 -> 4096): timed steps per window (0 = skip)")
     ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill measurement: sequences of 2048 ids")

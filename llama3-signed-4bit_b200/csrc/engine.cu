@@ -1541,6 +1541,19 @@ static int launch_gemv_mma(int mx, const QMat& W, const float* x, float* y, cuda
       cudaFuncSetAttribute(k_gemv_mma<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return -1;
   const int ntiles = (W.N + 15) / 16;
+  // few tiles: split K over the warps of one CTA per tile, so that about 16 warps per SM are
+  // streaming (up to 16 warps per tile, at least one K block each); with two n-tiles (3-4
+  // vectors) only while the tiles fit one wave, past that the grid-stride form measured faster
+  int kw = 1;
+  if (NT == 1 || ntiles <= num_sms)
+    while (kw < 16 && 2 * kw <= W.K / 128 && ntiles * kw * 2 <= num_sms * 16) kw *= 2;
+  if (kw > 1) {
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(k_gemv_mma_sk<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return -1;
+    k_gemv_mma_sk<NT><<<ntiles, 32 * kw, smem, s>>>(x, mx, W, y);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  }
   const int grid = std::min<int>((ntiles + 7) / 8, num_sms * 4);
   k_gemv_mma<NT><<<grid, 256, smem, s>>>(x, mx, W, y);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;

@@ -113,10 +113,12 @@ struct TileAcc {
   float y[NT][2];
 };
 
-// Accumulates the tile (16 rows starting at row0 of W) over all K blocks.
-// `scale_rows` loads step/min for rows (row0+g, row0+g+8) at block b.
-template <int NT>
-__device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitImage& img, int MX, TileAcc<NT>& acc) {
+// Accumulates the tile (16 rows starting at row0 of W) over K blocks [b0, b1).  Block b+1's
+// nibbles are requested before block b is computed; with kScalesAhead its scales too (pays when
+// few warps share an SM, as in the split-K form, and costs when many do).
+template <int NT, bool kScalesAhead>
+__device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitImage& img, int MX, TileAcc<NT>& acc,
+                                         int b0 = 0, int b1 = -1) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int nb = W.K >> 7;
   const uint8_t* ra = W.nib + (size_t)(row0 + g) * (W.K >> 1) + 16 * t;
@@ -130,12 +132,27 @@ __device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitIma
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc.y[j][0] = acc.y[j][1] = 0.0f;
 
-  uint4 wa = ld_stream_u4(ra), wb = ld_stream_u4(rb);
-  for (int b = 0; b < nb; ++b) {
+  if (b1 < 0) b1 = nb;
+  if (b0 >= b1) return;
+  auto scales = [&](int b, float (&sc)[4]) {
+    sc[0] = sc[1] = sc[2] = sc[3] = 0.f;
+    if (owner) {
+      sc[0] = bf16_bits_to_f32(__ldg(sa + b));
+      sc[1] = bf16_bits_to_f32(__ldg(ma + b));
+      sc[2] = bf16_bits_to_f32(__ldg(sb + b));
+      sc[3] = bf16_bits_to_f32(__ldg(mb + b));
+    }
+  };
+  uint4 wa = ld_stream_u4(ra + (size_t)b0 * 64), wb = ld_stream_u4(rb + (size_t)b0 * 64);
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (kScalesAhead) scales(b0, sc);
+  for (int b = b0; b < b1; ++b) {
     uint4 na = wa, nbw = wb;
-    if (b + 1 < nb) {
+    float nsc[4] = {sc[0], sc[1], sc[2], sc[3]};
+    if (b + 1 < b1) {
       na = ld_stream_u4(ra + (size_t)(b + 1) * 64);
       nbw = ld_stream_u4(rb + (size_t)(b + 1) * 64);
+      if (kScalesAhead) scales(b + 1, nsc);
     }
     int c[NT][4];
 #pragma unroll
@@ -149,18 +166,12 @@ __device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitIma
       const uint32_t a1 = xb & 0x0F0F0F0Fu, a3 = (xb >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
-        const uint2 bb = bf[(i * NT + j) * 32];
-        mma_u8s8(c[j], a0, a1, a2, a3, bb.x, bb.y);
+        const uint2 bq = bf[(i * NT + j) * 32];
+        mma_u8s8(c[j], a0, a1, a2, a3, bq.x, bq.y);
       }
     }
+    if (!kScalesAhead) scales(b, sc);
     // epilogue of block b: lanes t and t^1 hold digit planes {0,1} and {2,3}
-    float st0 = 0.f, mn0 = 0.f, st1 = 0.f, mn1 = 0.f;
-    if (owner) {
-      st0 = bf16_bits_to_f32(__ldg(sa + b));
-      mn0 = bf16_bits_to_f32(__ldg(ma + b));
-      st1 = bf16_bits_to_f32(__ldg(sb + b));
-      mn1 = bf16_bits_to_f32(__ldg(mb + b));
-    }
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       const int p2 = __shfl_xor_sync(0xffffffffu, c[j][0], 1);
@@ -178,12 +189,14 @@ __device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitIma
         v1 = fmaf(v1, 256.0f, (float)q2);
         v1 = fmaf(v1, 256.0f, (float)c[j][3]);
         v1 = fmaf(v1, 256.0f, (float)c[j][2]);
-        acc.y[j][0] += fmaf(st0 * es, v0, mn0 * xsb);
-        acc.y[j][1] += fmaf(st1 * es, v1, mn1 * xsb);
+        acc.y[j][0] += fmaf(sc[0] * es, v0, sc[1] * xsb);
+        acc.y[j][1] += fmaf(sc[2] * es, v1, sc[3] * xsb);
       }
     }
     wa = na;
     wb = nbw;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sc[q] = nsc[q];
   }
 }
 
@@ -210,7 +223,7 @@ __global__ void __launch_bounds__(256) k_gemv_mma(const float* __restrict__ x, i
     QMat Wt = W;
     if (row0 + 16 > W.N) row0 = W.N - 16;  // N >= 16 is required by the launcher
     TileAcc<NT> acc;
-    mma_tile<NT>(Wt, row0, img, MX, acc);
+    mma_tile<NT, false>(Wt, row0, img, MX, acc);
     if ((t & 1) == 0) {
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
@@ -222,6 +235,52 @@ __global__ void __launch_bounds__(256) k_gemv_mma(const float* __restrict__ x, i
         }
       }
     }
+  }
+}
+
+
+// Split-K form for matrices with few 16-row tiles (N up to a few thousand rows), where one warp
+// per tile would leave most SMs idle and walk every K block in series: one CTA per tile, its KW
+// warps take consecutive block ranges, and the CTA adds the KW partial rows in shared memory in
+// warp order.  The digit image is staged by every CTA, as in k_gemv_mma.
+template <int NT>
+__global__ void __launch_bounds__(512) k_gemv_mma_sk(const float* __restrict__ x, int MX, QMat W,
+                                                      float* __restrict__ y) {
+  extern __shared__ float4 smem4[];
+  __shared__ float red[16][4][16];  // [warp][sequence][row]
+  const int nb = W.K / 128;
+  DigitImage img;
+  img.bfrag = reinterpret_cast<uint2*>(smem4);
+  img.bsum = reinterpret_cast<float*>(img.bfrag + (size_t)nb * 4 * NT * 32);
+  img.escl = img.bsum + MX * nb;
+  stage_digits(x, MX, W.K, img);
+  const int KW = blockDim.x >> 5, w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tile = blockIdx.x;
+  int row0 = tile * 16;
+  if (row0 + 16 > W.N) row0 = W.N - 16;  // N >= 16 is required by the launcher
+  const int per = (nb + KW - 1) / KW;
+  const int b0 = min(nb, w * per), b1 = min(nb, b0 + per);
+  TileAcc<NT> acc;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc.y[j][0] = acc.y[j][1] = 0.0f;
+  mma_tile<NT, NT == 1>(W, row0, img, MX, acc, b0, b1);
+  if ((t & 1) == 0) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int m = 2 * j + (t >> 1);
+      if (m < MX) {
+        red[w][m][g] = acc.y[j][0];
+        red[w][m][g + 8] = acc.y[j][1];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 16 * MX) {
+    const int m = threadIdx.x >> 4, r = threadIdx.x & 15;
+    float v = 0.0f;
+    for (int k = 0; k < KW; ++k) v += red[k][m][r];
+    if (row0 + r >= tile * 16) y[(size_t)m * W.N + row0 + r] = v;
   }
 }
 

@@ -79,6 +79,31 @@ def test_gemv_sweep(pkg, bindings, oracle_lib, torch_cuda, K, N, M):
     assert (err <= GEMV_TOL * scale).all(), f"max err/scale {float((err / scale).max()):.3e}"
 
 
+@pytest.mark.parametrize("K,N,M", [(384, 40, 3), (2048, 1000, 5), (8192, 24, 8), (128, 16, 1), (6144, 2056, 2),
+                                   (2048, 4100, 1)])
+def test_gemv_ragged(pkg, bindings, oracle_lib, torch_cuda, K, N, M):
+    """Shapes off the model's grid: N not a multiple of 16 (the last tile overlaps the previous
+    one and stores only its own rows), K blocks that do not divide evenly over the warps of the
+    split-K form, one K block, and M > 4 (two launches)."""
+    torch = torch_cuda
+    nib, step, mn = pkg.model_file.gen_matrix(N, K, seed=7 + K + N, tensor=3, uniform_codes=True)
+    X = np.random.default_rng(K + 3 * N + M).standard_normal((M, K)).astype(np.float32)
+    d_nib = torch.from_numpy(nib).cuda()
+    d_step = torch.from_numpy(step.view(np.int16)).cuda()
+    d_min = torch.from_numpy(mn.view(np.int16)).cuda()
+    d_x = torch.from_numpy(X).cuda()
+    d_y = torch.full((M, N), float("nan"), device="cuda")
+    rc = bindings.lib.llama_b128_gemv(d_nib.data_ptr(), d_step.data_ptr(), d_min.data_ptr(), N, K,
+                                      d_x.data_ptr(), M, d_y.data_ptr(), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    y = d_y.cpu().numpy()
+    ref = _gemv_ref(oracle_lib, nib, step, mn, N, K, X)
+    scale = _abs_scale(pkg, step, mn, N, K, X)
+    assert np.isfinite(y).all()
+    assert (np.abs(y.astype(np.float64) - ref) <= GEMV_TOL * scale).all()
+
+
 def test_gemv_rejects_bad_args(bindings, torch_cuda):
     lib = bindings.lib
     assert lib.llama_b128_gemv(None, None, None, 8, 2048, None, 1, None, None) == -1
