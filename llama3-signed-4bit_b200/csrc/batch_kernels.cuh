@@ -16,6 +16,7 @@ namespace le {
 // x[t] = dequantised row tok[t] of the tied lm_head (dequantize_embedding_row,
 // src/llama_engine.cpp:182-220).
 __global__ void k_embed_batch(QMat E, const int32_t* __restrict__ tok, float* __restrict__ x, int ldx) {
+  grid_dep_begin();
   const int t = blockIdx.x;
   const int token = tok[t];
   const int K = E.K, nb = K >> 7;
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(128)
                  float* __restrict__ out, float* __restrict__ part, const float* __restrict__ qkv, int nsplit,
                  size_t split_stride, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
                  uint8_t* __restrict__ img) {
+  grid_dep_begin();
   // three-stage ring of K / V tiles (two tiles in flight while one is used)
   extern __shared__ __align__(16) float attn_smem[];
   float (*sk)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem);
@@ -263,6 +265,7 @@ __global__ void __launch_bounds__(128)
 // l_z e^(m_z - M).  One CTA of 256 threads per token: thread = (head, dimension pair) slice.
 __global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ part, int kv_heads, int S,
                                                       int q_dim, float* __restrict__ out) {
+  grid_dep_begin();
   const int t = blockIdx.x;
   for (int i = threadIdx.x; i < kv_heads * 4 * 32; i += blockDim.x) {
     const int g = i >> 7, h = (i >> 5) & 3, dp = i & 31;
@@ -318,6 +321,7 @@ constexpr int kPfV = 40;   // bf16 per transposed V row (32 keys + 8 pad)
 __global__ void __launch_bounds__(128)
     k_attn_prefill_tc(const float* __restrict__ q, int q_dim, const float* __restrict__ kc,
                       const float* __restrict__ vc, int kv_dim, int p0, int T, float* __restrict__ out) {
+  grid_dep_begin();
   // [hi, lo][32 keys][kPfK] and [hi, lo][64 dims][kPfV]
   __shared__ __align__(16) __nv_bfloat16 sk[2][32][kPfK];
   __shared__ __align__(16) __nv_bfloat16 svt[2][64][kPfV];
@@ -488,6 +492,7 @@ __global__ void __launch_bounds__(128)
 // Greedy candidates of logits row blockIdx.y (ld floats apart) into part[row * gridDim.x + x].
 __global__ void k_argmax_rows_batch(const float* __restrict__ logits, int vocab, size_t ld,
                                     ArgmaxPart* __restrict__ part) {
+  grid_dep_begin();
   __shared__ float s_bv[32];
   __shared__ int s_bi[32];
   const float* row = logits + (size_t)blockIdx.y * ld;
@@ -516,6 +521,7 @@ __global__ void k_argmax_rows_batch(const float* __restrict__ logits, int vocab,
 __global__ void __launch_bounds__(1024) k_logprob_rows(const float* __restrict__ logits, int vocab, size_t ld,
                                                        const int32_t* __restrict__ target,
                                                        float* __restrict__ out_lp, int32_t* __restrict__ out_greedy) {
+  grid_dep_begin();
   __shared__ float s_v[32];
   __shared__ int s_i[32];
   __shared__ float s_sum[32];
@@ -566,6 +572,7 @@ __global__ void __launch_bounds__(1024) k_logprob_rows(const float* __restrict__
 
 // result[row] = greedy id of row blockIdx.x from its nparts candidates (0 if none beats -1e30).
 __global__ void k_argmax_finish_batch(const ArgmaxPart* __restrict__ part, int nparts, int32_t* __restrict__ result) {
+  grid_dep_begin();
   __shared__ float s_bv[32];
   __shared__ int s_bi[32];
   const ArgmaxPart* pr = part + (size_t)blockIdx.x * nparts;

@@ -20,6 +20,18 @@ struct QMat {
 // bf16 -> fp32 is a 16-bit shift (src/llama_engine.cpp:28-33).
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
 
+// Programmatic dependent launch (kernels of one batched step, launched with the programmatic
+// stream-serialisation attribute): the kernel lets the next one in the stream be scheduled as
+// soon as all of its CTAs are running, then waits until the previous kernel has completed and
+// its memory is visible.  Without the attribute both instructions are no-ops.  A kernel must
+// not touch memory that an earlier kernel of the stream writes or reads before the wait.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_begin() {
+  grid_dep_launch();
+  grid_dep_wait();
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

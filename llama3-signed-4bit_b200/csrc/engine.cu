@@ -690,6 +690,24 @@ static int tc_splits(const Engine* E, const TcMat& W, int tok_tiles) {
   return std::max(1, s);
 }
 
+// Launch with programmatic stream serialisation: the kernel may be scheduled while the previous
+// kernel of the stream is still finishing (it waits for it with griddepcontrol.wait before
+// touching any activation), which hides the launch gap between the dependent kernels of a step.
+template <typename... KArgs, typename... Args>
+static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Launches one tensor-core GEMM over T token rows of `img`; returns the number of K splits used.
 static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int splits, tc::Args A) {
   A.recs = W.recs;
@@ -702,7 +720,7 @@ static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int s
   A.splits = (W.kb + A.kb_split - 1) / A.kb_split;
   A.error = E->tc_err;
   const int units = A.tiles * A.tok_tiles * A.splits;
-  tc::k_tc_gemm<<<std::min(units, E->num_sms), tc::kThreads, tc::kSmemBytes, E->stream>>>(A);
+  launch_pdl(tc::k_tc_gemm, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::kSmemBytes, E->stream, A);
   return A.splits;
 }
 
@@ -758,39 +776,46 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     const DevLayer& D = E->L[l];
     float* kc = E->kcache + l * layer_stride;
     float* vc = E->vcache + l * layer_stride;
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, 0, dim, E->img_d);
+    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, 0, dim,
+               E->img_d);
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
                              rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
     if (prefill_p0 >= 0 || !fold)
-      k_rope_append<<<dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), 256, 0, s>>>(
-          E->t_qkv, sq, qkv_stride, dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
+      launch_pdl(k_rope_append, dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), dim3(256), 0, s, E->t_qkv, sq, qkv_stride,
+                 dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
     if (prefill_p0 >= 0) {
-      k_attn_prefill_tc<<<dim3(E->kv_heads, (n + 15) / 16), 128, 0, s>>>(E->t_q, dim, kc, vc, kvd, prefill_p0, n,
-                                                                         E->t_attn);
+      launch_pdl(k_attn_prefill_tc, dim3(E->kv_heads, (n + 15) / 16), dim3(128), 0, s, E->t_q, dim, kc, vc, kvd,
+                 prefill_p0, n, E->t_attn);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
       // without position splits the attention kernel writes the o-proj input image itself
-      k_attn_batch<<<dim3(n, E->kv_heads, attn_splits), 128, kAttnSmem, s>>>(
-          E->t_q, dim, kc, vc, slot_stride, kvd, pos, slot, E->t_attn, E->t_attn_part, fold ? E->t_qkv : nullptr,
-          sq, qkv_stride, E->rope_cos, E->rope_sin, attn_splits == 1 ? E->img_d : nullptr);
-      if (attn_splits > 1) k_attn_combine<<<n, 256, 0, s>>>(E->t_attn_part, E->kv_heads, attn_splits, dim, E->t_attn);
+      launch_pdl(k_attn_batch, dim3(n, E->kv_heads, attn_splits), dim3(128), kAttnSmem, s, E->t_q, dim, kc, vc,
+                 slot_stride, kvd, pos, slot, E->t_attn, E->t_attn_part, fold ? E->t_qkv : nullptr, sq, qkv_stride,
+                 E->rope_cos, E->rope_sin, attn_splits == 1 ? E->img_d : nullptr);
+      if (attn_splits > 1)
+        launch_pdl(k_attn_combine, dim3(n), dim3(256), 0, s, E->t_attn_part, (int)E->kv_heads, attn_splits, dim,
+                   E->t_attn);
     }
     if (prefill_p0 >= 0 || attn_splits > 1)
-      k_tc_stage<<<dim3(n, dim / 2048), 256, 0, s>>>(E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim, E->img_d);
+      launch_pdl(k_tc_stage, dim3(n, dim / 2048), dim3(256), 0, s, E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim,
+                 E->img_d);
     const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
-    k_tc_stage<<<n, 256, 0, s>>>(E->t_x, dim, E->t_part, so, part_stride, D.post_norm, 0, dim, E->img_d);
+    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, so, part_stride, D.post_norm, 0, dim,
+               E->img_d);
     tc_launch(E, Y.gu, E->img_d, n, 1, rows(E->t_gu, 2 * ffn, 2 * ffn, 0));
-    k_tc_stage<<<dim3(n, ffn / 2048), 256, 0, s>>>(E->t_gu, 2 * ffn, nullptr, 0, 0, nullptr, 1, ffn, E->img_f);
+    launch_pdl(k_tc_stage, dim3(n, ffn / 2048), dim3(256), 0, s, E->t_gu, 2 * ffn, nullptr, 0, 0, nullptr, 1, ffn,
+               E->img_f);
     d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), rows(E->t_part, dim, dim, part_stride));
   }
   if (nlog > 0) {
-    k_tc_stage<<<nlog, 256, 0, s>>>(E->t_x + (size_t)lrow0 * dim, dim, E->t_part + (size_t)lrow0 * dim, d_splits,
-                                     part_stride, E->final_norm, 0, dim, E->img_d);
+    launch_pdl(k_tc_stage, dim3(nlog), dim3(256), 0, s, E->t_x + (size_t)lrow0 * dim, dim,
+               E->t_part + (size_t)lrow0 * dim, d_splits, part_stride, E->final_norm, 0, dim, E->img_d);
     tc_launch(E, E->tc_lm, E->img_d, nlog, 1, rows(lg_out, (int)E->vocab, (int)E->vocab, 0));
     if (!logits_out) {
-      k_argmax_rows_batch<<<dim3(E->tc_am_parts, nlog), 256, 0, s>>>(E->logits, (int)E->vocab, E->vocab, E->t_am);
-      k_argmax_finish_batch<<<nlog, 256, 0, s>>>(E->t_am, E->tc_am_parts, E->am_result);
+      launch_pdl(k_argmax_rows_batch, dim3(E->tc_am_parts, nlog), dim3(256), 0, s, E->logits, (int)E->vocab,
+                 (size_t)E->vocab, E->t_am);
+      launch_pdl(k_argmax_finish_batch, dim3(nlog), dim3(256), 0, s, E->t_am, E->tc_am_parts, E->am_result);
     }
   }
   LE_CK(cudaGetLastError());

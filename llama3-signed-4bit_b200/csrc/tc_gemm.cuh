@@ -317,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  grid_dep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -328,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         prefetch_l2(A.recs + ((size_t)ahead.U.tile * A.kb_total + ahead.kb) * kRecBytes, kRecBytes);
         ahead.next(A, n_units);
       }
+      grid_dep_wait();  // the weight records are constant; the activation image is not
       int g = 0;
       for (; c.valid(n_units) && !s_abort; c.next(A, n_units), ++g) {
         const int s = g % kStages;
@@ -351,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       }
     }
   } else if (warp == 1) {
+    grid_dep_wait();
     if (lane == 0) {
       // ---------------- MMA issuer (one thread issues every MMA of the CTA) ----------------
       // Issuing from two threads that take alternate blocks was measured to corrupt an occasional
@@ -563,6 +566,7 @@ __global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G,
 __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx, const float* __restrict__ part,
                                                   int nsplit, size_t split_stride, const float* __restrict__ gamma,
                                                   int gateup, int K, uint8_t* __restrict__ img) {
+  grid_dep_begin();
   __shared__ float red[32];
   const int t = blockIdx.x;
   // runs of 8 elements per thread: j0 .. j1-1 (all K / 2048 runs when normalising, which needs
@@ -694,6 +698,7 @@ __global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ q
                                                      const int32_t* __restrict__ slot, const float* __restrict__ rope_cos,
                                                      const float* __restrict__ rope_sin, float* __restrict__ q_out,
                                                      float* __restrict__ kc, float* __restrict__ vc, size_t slot_stride) {
+  grid_dep_begin();
   const int t = blockIdx.x;
   const int p = pos[t];
   const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
