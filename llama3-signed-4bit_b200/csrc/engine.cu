@@ -740,6 +740,11 @@ static bool tc_upload_rows(Engine* E, const int32_t* tok, const int32_t* pos, co
   return true;
 }
 
+// Position-range splits of decode attention (each range >= 1024 positions); one formula for the
+// step and for its graph-cache key.  (Also limiting the splits by rows x kv heads measured the
+// same at 256 rows.)
+static int attn_splits_for(int max_pos) { return std::max(1, std::min(kAttnMaxSplits, (max_pos + 1) / 1024)); }
+
 // One forward step of n rows (rows already uploaded).  Logits and greedy ids are produced for
 // rows [lrow0, lrow0 + nlog) into logits rows 0..nlog-1 and am_result[0..nlog-1].
 // With prefill_p0 >= 0 the rows are consecutive positions prefill_p0 .. of slot 0 (a prefill
@@ -758,8 +763,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
   const int32_t* pos = E->t_idx + n;
   const int32_t* slot = E->t_idx + 2 * n;
   const int tok_tiles = (n + kTok - 1) / kTok;
-  // attention: split each (token, kv head) over position ranges of >= 1024 positions
-  const int attn_splits = std::max(1, std::min(kAttnMaxSplits, (max_pos + 1) / 1024));
+  const int attn_splits = attn_splits_for(max_pos);
   cudaStream_t s = E->stream;
   auto rows = [&](float* out, int ldo, int N, size_t split_stride) {
     Args A{};
@@ -825,7 +829,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
 
 // A decode step (rows already uploaded) through a cached CUDA graph of tc_step's launches.
 static bool tc_step_graph(Engine* E, int n, int nlog, int max_pos, bool fold) {
-  const int splits = std::max(1, std::min(kAttnMaxSplits, (max_pos + 1) / 1024));
+  const int splits = attn_splits_for(max_pos);
   for (const auto& g : E->tc_graphs)
     if (g.n == n && g.nlog == nlog && g.splits == splits && g.fold == fold) {
       LE_CK(cudaGraphLaunch(g.exec, E->stream));
