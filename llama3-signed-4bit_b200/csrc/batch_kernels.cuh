@@ -40,11 +40,11 @@ __global__ void k_embed_batch(QMat E, const int32_t* __restrict__ tok, float* __
 // as in k_rope_append, src/llama_engine.cpp:953-956), uses the token's k / v for position pos
 // in place of the cache row, and the CTA whose range holds pos appends them to the cache.  One CTA of 4 warps per (t, g): the CTA streams 32-position K / V tiles through shared
 // memory (coalesced cp.async, three tiles in a ring, rows padded to 68 floats so that 16-byte row
-// reads of 8 lanes hit distinct banks).  Each tile is read once for all four heads: for the
-// scores warp w takes dimensions 16w .. 16w+15 of every head (lane = position) and the four
-// warps' partial dot products meet in shared memory; warp h then runs the online softmax of head
-// h (running max and sum, rescaled per tile); for p . v warp w takes dimensions 16w .. 16w+15
-// of every head (lane = head x dimension pair).
+// reads of 8 lanes hit distinct banks), one barrier per tile.  Warp w owns positions 8w .. 8w+7
+// of every tile: lane (j, h) = 4j + h holds q of head h and computes the whole 64-wide score of
+// position 8w + j; each warp keeps its own online softmax per head (running max and sum,
+// rescaled per tile) and o for dimensions 2 lane, 2 lane + 1 of the four heads (p . v with the
+// probabilities broadcast by shuffles); the four warps' (max, sum, o) are merged at the end.
 //
 // With gridDim.z = S > 1 the positions of each (t, g) are split into S contiguous ranges, one
 // CTA each, and the CTA writes its unnormalised partial (running max m, sum l and o per head)
@@ -63,7 +63,7 @@ __device__ __forceinline__ float attn_sum_planes(const float* p, int nsplit, siz
   return tc::sum_planes(p, nsplit, stride);
 }
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 4)
     k_attn_batch(const float* __restrict__ q, int q_dim, float* __restrict__ kc, float* __restrict__ vc,
                  size_t slot_stride, int kv_dim, const int32_t* __restrict__ pos, const int32_t* __restrict__ slot,
                  float* __restrict__ out, float* __restrict__ part, const float* __restrict__ qkv, int nsplit,
@@ -74,11 +74,9 @@ __global__ void __launch_bounds__(128)
   extern __shared__ __align__(16) float attn_smem[];
   float (*sk)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem);
   float (*sv)[32][kAttnRow] = reinterpret_cast<float (*)[32][kAttnRow]>(attn_smem + 3 * 32 * kAttnRow);
-  __shared__ float sd[4][4][33];           // partial dots [warp][head][position]
-  __shared__ __align__(16) float sp[4][32];  // softmax numerators [head][position] of this tile
-  __shared__ float salpha[4], sl[4], sm[4];  // per head: rescale of this tile, final sum and max
+  __shared__ float wm[4][4], wl[4][4];         // per warp and head: running max and sum
   __shared__ __align__(16) float sqkv[6][64];  // with qkv: q of the 4 heads, k and v of this token
-  __shared__ float sbs[4][2];                  // with img: per warp, partial sums of the two blocks
+  __shared__ float sbs[4];                     // with img: per warp, the sum of its head's outputs
   const int t = blockIdx.x, g = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P_all = pos[t] + 1;
@@ -122,142 +120,142 @@ __global__ void __launch_bounds__(128)
     }
     cp_async_commit();
   };
-  // q slices: dims 16 warp .. 16 warp + 15 of the four heads
-  float qv[4][16];
+  // q of this lane's head, all 64 dimensions (lane = 4 x position-in-warp + head)
+  const int hq = lane & 3, pw = lane >> 2;
+  float qv[64];
   {
-    const float* qt = qkv != nullptr ? &sqkv[0][16 * warp] : q + (size_t)t * q_dim + (size_t)(4 * g) * LE_HEAD_DIM + 16 * warp;
+    const float* qt = qkv != nullptr ? &sqkv[hq][0] : q + (size_t)t * q_dim + (size_t)(4 * g + hq) * LE_HEAD_DIM;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const float4* qp = reinterpret_cast<const float4*>(qt + h * LE_HEAD_DIM);
-#pragma unroll
-      for (int d4 = 0; d4 < 4; ++d4) {
-        const float4 v = qp[d4];
-        qv[h][4 * d4] = v.x; qv[h][4 * d4 + 1] = v.y; qv[h][4 * d4 + 2] = v.z; qv[h][4 * d4 + 3] = v.w;
-      }
+    for (int d4 = 0; d4 < 16; ++d4) {
+      const float4 v = reinterpret_cast<const float4*>(qt)[d4];
+      qv[4 * d4] = v.x; qv[4 * d4 + 1] = v.y; qv[4 * d4 + 2] = v.z; qv[4 * d4 + 3] = v.w;
     }
   }
-  // softmax state of head `warp` (all lanes hold it); p . v accumulators of (head ph, dims 16 warp + 2 dp)
+  // this warp's online softmax of head hq (the same in the 8 lanes of the head) and its p . v for
+  // dimensions 2 lane, 2 lane + 1 of the four heads
   float m = -INFINITY, l = 0.0f;
-  const int ph = lane >> 3, dp = lane & 7;
-  float o0 = 0.0f, o1 = 0.0f;
+  float o[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
   if (tile0 < tile1) load_tile(tile0, 0);
   if (tile0 + 1 < tile1) load_tile(tile0 + 1, 1);
   for (int kt = tile0; kt < tile1; ++kt) {
     const int buf = (kt - tile0) % 3;
-    if (kt + 2 < tile1) {
-      load_tile(kt + 2, (kt - tile0 + 2) % 3);
-      cp_async_wait<2>();
-    } else if (kt + 1 < tile1) {
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
+    if (kt + 1 < tile1) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();  // tile kt has landed for every thread, and tile kt - 1's buffer is free
+    if (kt + 2 < tile1) load_tile(kt + 2, (kt - tile0 + 2) % 3);
     if (qkv != nullptr && p_tok >= kt * 32 && p_tok < kt * 32 + 32) {  // this step's own k / v
       const int r = p_tok - kt * 32;
       if (threadIdx.x < 64) sk[buf][r][threadIdx.x] = sqkv[4][threadIdx.x];
       else sv[buf][r][threadIdx.x - 64] = sqkv[5][threadIdx.x - 64];
       __syncthreads();
     }
-    // partial dots of position kt*32 + lane over this warp's 16 dimensions, for the four heads
-    {
-      const float4* kr = reinterpret_cast<const float4*>(&sk[buf][lane][16 * warp]);
-      float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    // score of position kt*32 + 8 warp + pw for head hq
+    const int r = 8 * warp + pw;
+    const float4* kr = reinterpret_cast<const float4*>(&sk[buf][r][0]);
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
-      for (int d4 = 0; d4 < 4; ++d4) {
-        const float4 k4 = kr[d4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          d[h] = fmaf(qv[h][4 * d4], k4.x, d[h]);
-          d[h] = fmaf(qv[h][4 * d4 + 1], k4.y, d[h]);
-          d[h] = fmaf(qv[h][4 * d4 + 2], k4.z, d[h]);
-          d[h] = fmaf(qv[h][4 * d4 + 3], k4.w, d[h]);
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 4; ++h) sd[warp][h][lane] = d[h];
+    for (int d4 = 0; d4 < 16; ++d4) {
+      const float4 k4 = kr[d4];
+      d0 = fmaf(qv[4 * d4], k4.x, d0);
+      d1 = fmaf(qv[4 * d4 + 1], k4.y, d1);
+      d2 = fmaf(qv[4 * d4 + 2], k4.z, d2);
+      d3 = fmaf(qv[4 * d4 + 3], k4.w, d3);
     }
-    __syncthreads();
-    // warp h: scores and online softmax of head h
-    {
-      const int h = warp;
-      const float dot = (sd[0][h][lane] + sd[1][h][lane]) + (sd[2][h][lane] + sd[3][h][lane]);
-      const float s = kt * 32 + lane < P ? dot * 0.125f : -INFINITY;
-      const float mn = fmaxf(m, warp_max(s));  // finite: the tile holds a position of the range
-      const float alpha = expf(m - mn);
-      const float pe = expf(s - mn);
-      l = l * alpha + warp_sum(pe);
-      m = mn;
-      sp[h][lane] = pe;
-      if (lane == 0) salpha[h] = alpha;
+    const float s = kt * 32 + r < P ? ((d0 + d1) + (d2 + d3)) * 0.125f : -INFINITY;
+    // the warp's 8 positions of head hq sit in lanes hq, hq + 4, ..., hq + 28
+    float tmax = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 4));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+    const float mn = fmaxf(m, tmax);
+    const float alpha = mn == -INFINITY ? 1.0f : expf(m - mn);  // no position of the head yet
+    const float pe = s == -INFINITY ? 0.0f : expf(s - mn);
+    float psum = pe + __shfl_xor_sync(0xffffffffu, pe, 4);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 8);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 16);
+    l = l * alpha + psum;
+    m = mn;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float ah = __shfl_sync(0xffffffffu, alpha, h);
+      o[h][0] *= ah;
+      o[h][1] *= ah;
     }
-    __syncthreads();
-    // p . v for (head ph, dims 16 warp + 2 dp, +1): positions past the range have p = 0
-    {
-      const float alpha = salpha[ph];
-      o0 *= alpha;
-      o1 *= alpha;
-      const float4* pw4 = reinterpret_cast<const float4*>(sp[ph]);
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 p4 = pw4[j4];
-        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+    for (int j = 0; j < 8; ++j) {
+      const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][8 * warp + j][2 * lane]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][4 * j4 + u][16 * warp + 2 * dp]);
-          o0 = fmaf(pj[u], v2.x, o0);
-          o1 = fmaf(pj[u], v2.y, o1);
-        }
+      for (int h = 0; h < 4; ++h) {
+        const float pj = __shfl_sync(0xffffffffu, pe, 4 * j + h);
+        o[h][0] = fmaf(pj, v2.x, o[h][0]);
+        o[h][1] = fmaf(pj, v2.y, o[h][1]);
       }
     }
-    __syncthreads();  // buffer buf and sd / sp are rewritten by the next iteration
   }
-  if (lane == 0) {
-    sm[warp] = m;
-    sl[warp] = l;
+  __syncthreads();  // every warp is done with the ring: its memory now holds the warps' o
+  float* wo = attn_smem;  // [warp][head][64]
+  if (lane < 4) {  // lane h (position 0) holds head h's max and sum
+    wm[warp][lane] = m;
+    wl[warp][lane] = l;
   }
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+    *reinterpret_cast<float2*>(&wo[(warp * 4 + h) * 64 + 2 * lane]) = make_float2(o[h][0], o[h][1]);
   if (qkv != nullptr && p_tok >= tile0 * 32 && p_tok < P) {  // append k / v at (slot, pos)
     const size_t crow = base + (size_t)p_tok * kv_dim;
     if (threadIdx.x < 64) kc[crow + threadIdx.x] = sqkv[4][threadIdx.x];
     else vc[crow + threadIdx.x - 64] = sqkv[5][threadIdx.x - 64];
   }
   __syncthreads();
+  // merge of the four warps: thread = (head ph = warp, dimensions 2 dp, 2 dp + 1)
+  const int ph = warp, dp = lane;
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][ph]);
+  float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float f = wm[w][ph] == -INFINITY ? 0.0f : expf(wm[w][ph] - M);  // warps without positions
+    const float2 ow = *reinterpret_cast<const float2*>(&wo[(w * 4 + ph) * 64 + 2 * dp]);
+    L = fmaf(wl[w][ph], f, L);
+    o0 = fmaf(ow.x, f, o0);
+    o1 = fmaf(ow.y, f, o1);
+  }
   if (gridDim.z > 1) {
     float* pp = part + ((size_t)(t * gridDim.y + g) * gridDim.z + blockIdx.z) * kAttnPart + ph * 66;
-    if (warp == 0 && dp == 0) { pp[0] = sm[ph]; pp[1] = sl[ph]; }
-    pp[2 + 16 * warp + 2 * dp] = o0;
-    pp[3 + 16 * warp + 2 * dp] = o1;
+    if (dp == 0) { pp[0] = M; pp[1] = L; }
+    pp[2 + 2 * dp] = o0;
+    pp[3 + 2 * dp] = o1;
     return;
   }
-  const float inv = 1.0f / sl[ph];
+  const float inv = 1.0f / L;
   const float a0 = o0 * inv, a1 = o1 * inv;
   if (img != nullptr) {
     // the o-proj GEMM input, written directly in the k_tc_stage image layout: bf16 hi / lo parts
     // of the element pair at its place in the 8-element run, and the 128-block sums
     const __nv_bfloat162 hh = __floats2bfloat162_rn(a0, a1);
     const __nv_bfloat162 ll = __floats2bfloat162_rn(a0 - __low2float(hh), a1 - __high2float(hh));
-    const int e = (4 * g + ph) * LE_HEAD_DIM + 16 * warp + 2 * dp;
+    const int e = (4 * g + ph) * LE_HEAD_DIM + 2 * dp;
     const int i0 = e & ~7, j = (e & 7) >> 1;
     const int tt = t / tc::kTok, tr = t % tc::kTok, kbt = q_dim >> 7;
     const int kb = i0 >> 7, kk = i0 & 127, atom = kk >> 6, c = (kk & 63) >> 3;
     uint8_t* im = img + ((size_t)tt * kbt + kb) * tc::kImgBytes;
-    const size_t o = (size_t)atom * 2 * tc::kAtom + tr * 128 + ((c ^ (tr & 7)) << 4) + 4 * j;
-    *reinterpret_cast<__nv_bfloat162*>(im + o) = hh;
-    *reinterpret_cast<__nv_bfloat162*>(im + tc::kAtom + o) = ll;
-    // lanes 0..15 hold heads 4g, 4g+1 (block 2g), lanes 16..31 heads 4g+2, 4g+3 (block 2g+1)
+    const size_t off = (size_t)atom * 2 * tc::kAtom + tr * 128 + ((c ^ (tr & 7)) << 4) + 4 * j;
+    *reinterpret_cast<__nv_bfloat162*>(im + off) = hh;
+    *reinterpret_cast<__nv_bfloat162*>(im + tc::kAtom + off) = ll;
+    // block 2g holds heads 4g, 4g+1 (warps 0, 1), block 2g+1 heads 4g+2, 4g+3 (warps 2, 3)
     float bs = a0 + a1;
 #pragma unroll
-    for (int o2 = 8; o2 > 0; o2 >>= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o2);
-    if ((lane & 15) == 0) sbs[warp][lane >> 4] = bs;
+    for (int o2 = 16; o2 > 0; o2 >>= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o2);
+    if (lane == 0) sbs[warp] = bs;
     __syncthreads();
     if (threadIdx.x < 2) {
       const int b = threadIdx.x;
-      const float tot = (sbs[0][b] + sbs[1][b]) + (sbs[2][b] + sbs[3][b]);
-      reinterpret_cast<float*>(img + ((size_t)tt * kbt + 2 * g + b) * tc::kImgBytes + tc::kOffXs)[tr] = tot;
+      reinterpret_cast<float*>(img + ((size_t)tt * kbt + 2 * g + b) * tc::kImgBytes + tc::kOffXs)[tr] =
+          sbs[2 * b] + sbs[2 * b + 1];
     }
     return;
   }
-  float* op = out + (size_t)t * q_dim + (size_t)(4 * g + ph) * LE_HEAD_DIM + 16 * warp + 2 * dp;
+  float* op = out + (size_t)t * q_dim + (size_t)(4 * g + ph) * LE_HEAD_DIM + 2 * dp;
   *reinterpret_cast<float2*>(op) = make_float2(a0, a1);
 }
 
