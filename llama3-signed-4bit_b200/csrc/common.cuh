@@ -20,6 +20,24 @@ struct QMat {
 // bf16 -> fp32 is a 16-bit shift (src/llama_engine.cpp:28-33).
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
 
+// Balanced base-256 digits of a fixed-point integer |X| < 2^29: the bytes of the result, read as
+// s8, are d0..d3 with X = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3 and every d in [-128, 127].  (Adding 128
+// to every byte position and then flipping each byte's top bit is the same as taking the digit
+// d = ((X + 128) & 255) - 128 and carrying (X - d) >> 8 to the next position.)
+__device__ __forceinline__ uint32_t balanced_digits(int X) {
+  return ((uint32_t)X + 0x80808080u) ^ 0x80808080u;
+}
+// Byte transpose of four digit words: plane p of the result holds byte p of d0, d1, d2, d3 (in
+// that byte order).
+__device__ __forceinline__ void digit_planes(uint32_t d0, uint32_t d1, uint32_t d2, uint32_t d3, uint32_t (&pl)[4]) {
+  const uint32_t t0 = __byte_perm(d0, d1, 0x5140), t1 = __byte_perm(d0, d1, 0x7362);
+  const uint32_t t2 = __byte_perm(d2, d3, 0x5140), t3 = __byte_perm(d2, d3, 0x7362);
+  pl[0] = __byte_perm(t0, t2, 0x5410);
+  pl[1] = __byte_perm(t0, t2, 0x7632);
+  pl[2] = __byte_perm(t1, t3, 0x5410);
+  pl[3] = __byte_perm(t1, t3, 0x7632);
+}
+
 // Programmatic dependent launch (kernels of one batched step, launched with the programmatic
 // stream-serialisation attribute): the kernel lets the next one in the stream be scheduled as
 // soon as all of its CTAs are running, then waits until the previous kernel has completed and

@@ -83,18 +83,14 @@ __device__ __forceinline__ void stage_digits(const float* xs, int MX, int K, Dig
     const float es = img.escl[m * nb + b];
     const int e = es > 0.0f ? 127 - (int)(__float_as_uint(es) >> 23) : 0;
     const float up = __uint_as_float((uint32_t)(e + 127) << 23);  // 2^e
-    uint32_t plane[4] = {0u, 0u, 0u, 0u};
+    uint32_t dg[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float xv = xs[(size_t)m * K + b * 128 + 32 * t + 8 * i + 2 * j + h];
-      int X = es > 0.0f ? __float2int_rn(xv * up) : 0;
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int d = ((X + 128) & 255) - 128;
-        X = (X - d) >> 8;
-        plane[p] |= (uint32_t)(d & 255) << (8 * j);
-      }
+      dg[j] = balanced_digits(es > 0.0f ? __float2int_rn(xv * up) : 0);
     }
+    uint32_t plane[4];
+    digit_planes(dg[0], dg[1], dg[2], dg[3], plane);
     const int jt = m >> 1;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
