@@ -87,6 +87,28 @@ def phase_bytes(shape, pos: int) -> dict:
     }
 
 
+# ---------------------------------------------------------------------------------------------
+# multi-GPU plumbing: one process per GPU, independent sequences (no collective on the data path)
+# ---------------------------------------------------------------------------------------------
+def max_over_ranks(values, world: int, device="cuda"):
+    """Element-wise max of a list of timings over the ranks: every multi-GPU number is timed as
+    the slowest rank's.  Every rank must call it at the same point."""
+    vals = [float(v) for v in values]
+    if world <= 1:
+        return vals
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def rank_seed(base: int, rank: int) -> int:
+    """Seed of a rank's synthetic sequences: each rank decodes its own (weak scaling)."""
+    return base + rank
+
+
 def token_bytes(shape, pos: int) -> int:
     """Weights + norms + KV read (pos+1 rows incl. the new one) + KV write, per token."""
     kv_row = shape.layers * shape.kv_dim * 4 * 2
@@ -217,7 +239,7 @@ def run_ours(args, rank, world, local_rank):
     eng = pkg.LlamaEngine(str(model), bindings, device=local_rank, max_batch=1, max_seq_len=0)
     lib = bindings.lib
     stream = torch.cuda.ExternalStream(lib.llama_engine_get_stream(eng.handle))
-    prompt = np.random.default_rng(1000 + rank).integers(0, shape.vocab, PROMPT_LEN).astype(np.int32)
+    prompt = np.random.default_rng(rank_seed(1000, rank)).integers(0, shape.vocab, PROMPT_LEN).astype(np.int32)
     eng.prefill([int(t) for t in prompt[:-1]], 0, False)
     first, start = int(prompt[-1]), PROMPT_LEN - 1
 
@@ -242,10 +264,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     clocks = clk.summary() if rank == 0 else None
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks([ms], world)[0]
     value = world * args.steps / (ms / 1e3)
 
     # e2e through the reference ABI: forward_token + sample(0) per step, from the host
@@ -271,10 +290,8 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
     e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms, wall * 1e3], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms, wall = float(t[0].item()), float(t[1].item()) / 1e3
+    e2e_ms, wall_ms = max_over_ranks([e2e_ms, wall * 1e3], world)
+    wall = wall_ms / 1e3
     e2e_value = world * args.steps / max(e2e_ms / 1e3, wall)
 
     # roofline of the dominant kernel
@@ -480,7 +497,7 @@ def run_box(args, model, shape, local_rank, world):
     lib = bindings.lib
     stream = torch.cuda.ExternalStream(lib.llama_engine_get_stream(eng.handle))
     rank = dist.get_rank() if world > 1 else 0
-    rng = np.random.default_rng(4000 + rank)
+    rng = np.random.default_rng(rank_seed(4000, rank))
     slots = list(range(B))
     per = 1024 // B
 
@@ -509,11 +526,7 @@ def run_box(args, model, shape, local_rank, world):
             t = eng.argmax_batch(B)
         e1.record(stream)
         torch.cuda.synchronize()
-        times = [e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3]
-        if world > 1:
-            tt = torch.tensor(times, device="cuda")
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            times = [float(x) for x in tt.tolist()]
+        times = max_over_ranks([e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3], world)
         return times, t
 
     ids = rng.integers(0, shape.vocab, (B, MAXS)).astype(np.int32)
