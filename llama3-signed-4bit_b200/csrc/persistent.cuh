@@ -547,6 +547,8 @@ __device__ __forceinline__ void trace_mark(const PArgs& A, int& n, int tok, uint
 // ---------------------------------------------------------------------------------------------
 constexpr int kAttnP = 4;                           // positions per warp per chunk
 constexpr int kAttnChunk = kAttnP * kPConsumerWarps;
+// the second chunk is staged in the image region as [row][K 64 | V 64] floats
+static_assert(kAttnChunk * 128 * 4 <= kImageBytes, "second attention chunk must fit the image region");
 
 __device__ __forceinline__ float warp_allsum(float v) {
 #pragma unroll
