@@ -1,13 +1,21 @@
 // Byte-level BPE tokenizer behind llama_tokenizer_* (src/llama_engine.h:59-62).
 //
 // Host code, off the GPU path.  Behaviour follows the reference's LLaMATokenizer
-// (src/llama_engine.cpp:526-739): bytes map to printable code points with the GPT-2 byte table;
-// text is split on single spaces (every space becomes its own token); each non-space run is
-// merged pair-by-pair by lowest merge rank (one merge per round, leftmost pair among equal
-// ranks); pieces missing from the vocabulary are dropped.  Decoding maps code points back to
-// bytes.  The tokenizer.json reader here is a small JSON parser of its own; it reads
-// model.vocab and model.merges, with merges given either as "a b" strings or as ["a", "b"] pairs.
+// (src/llama_engine.cpp:526-739) exactly, including how it reads tokenizer.json:
+// * the vocabulary is the run of "piece": id entries between the first `"vocab": {` and the
+//   following `"merges": [` of the file; in a piece only the escapes \" and \\ are undone
+//   (every other backslash sequence stays as written, :594-603);
+// * merges are the quoted strings from there to the file's last `]`, taken verbatim (no escape
+//   is undone), split at their first space; strings without a space are skipped and consume no
+//   rank, and a repeated pair keeps its last rank (:623-647);
+// * bytes map to printable code points with the GPT-2 byte table; text is split on single
+//   spaces (every space becomes its own token); each non-space run is merged pair by pair by
+//   lowest merge rank (one merge per round, leftmost pair among equal ranks); pieces missing from
+//   the vocabulary are dropped; decoding maps code points back to bytes.
+// The scanning code here is this library's own; it keeps those rules because a drop-in must
+// produce the same ids from the same tokenizer.json.
 #include <algorithm>
+#include <cctype>
 #include <cstdint>
 #include <cstring>
 #include <fstream>
@@ -49,120 +57,18 @@ size_t utf8_len(unsigned char c) {
   return 1;
 }
 
-// Minimal JSON reader: enough to walk tokenizer.json and pull out strings and integers.
-class Json {
- public:
-  explicit Json(const std::string& s) : s_(s) {}
-  bool ok() const { return ok_; }
-
-  void ws() {
-    while (p_ < s_.size() && (s_[p_] == ' ' || s_[p_] == '\n' || s_[p_] == '\r' || s_[p_] == '\t')) ++p_;
+// End of the quoted string whose opening quote is at q1: the next quote before `limit` that is
+// preceded by an even number of backslashes; `limit` when there is none.
+size_t quote_end(const std::string& s, size_t q1, size_t limit) {
+  size_t q2 = q1 + 1;
+  for (; q2 < limit; ++q2) {
+    if (s[q2] != '"') continue;
+    size_t bs = 0;
+    for (size_t k = q2; k > q1 && s[k - 1] == '\\'; --k) ++bs;
+    if (bs % 2 == 0) break;
   }
-  bool eat(char c) {
-    ws();
-    if (p_ < s_.size() && s_[p_] == c) { ++p_; return true; }
-    return false;
-  }
-  char peek() {
-    ws();
-    return p_ < s_.size() ? s_[p_] : '\0';
-  }
-  bool str(std::string& out) {
-    out.clear();
-    if (!eat('"')) return fail();
-    while (p_ < s_.size()) {
-      char c = s_[p_++];
-      if (c == '"') return true;
-      if (c != '\\') { out += c; continue; }
-      if (p_ >= s_.size()) return fail();
-      char e = s_[p_++];
-      switch (e) {
-        case 'n': out += '\n'; break;
-        case 't': out += '\t'; break;
-        case 'r': out += '\r'; break;
-        case 'b': out += '\b'; break;
-        case 'f': out += '\f'; break;
-        case 'u': {
-          uint32_t cp = 0;
-          if (!hex4(cp)) return fail();
-          if (cp >= 0xD800 && cp < 0xDC00 && p_ + 6 <= s_.size() && s_[p_] == '\\' && s_[p_ + 1] == 'u') {
-            p_ += 2;
-            uint32_t lo = 0;
-            if (!hex4(lo)) return fail();
-            cp = 0x10000 + ((cp - 0xD800) << 10) + (lo - 0xDC00);
-          }
-          append_utf8(out, cp);
-          break;
-        }
-        default: out += e; break;  // \" \\ \/
-      }
-    }
-    return fail();
-  }
-  bool integer(int64_t& v) {
-    ws();
-    size_t q = p_;
-    bool neg = false;
-    if (q < s_.size() && s_[q] == '-') { neg = true; ++q; }
-    if (q >= s_.size() || s_[q] < '0' || s_[q] > '9') return fail();
-    v = 0;
-    while (q < s_.size() && s_[q] >= '0' && s_[q] <= '9') v = v * 10 + (s_[q++] - '0');
-    // skip fraction / exponent if any
-    while (q < s_.size() && (s_[q] == '.' || s_[q] == 'e' || s_[q] == 'E' || s_[q] == '+' || s_[q] == '-' ||
-                             (s_[q] >= '0' && s_[q] <= '9')))
-      ++q;
-    p_ = q;
-    if (neg) v = -v;
-    return true;
-  }
-  // Skips any JSON value.
-  bool skip() {
-    char c = peek();
-    if (c == '"') { std::string t; return str(t); }
-    if (c == '{') {
-      eat('{');
-      if (eat('}')) return true;
-      do {
-        std::string k;
-        if (!str(k) || !eat(':') || !skip()) return fail();
-      } while (eat(','));
-      return eat('}') || fail();
-    }
-    if (c == '[') {
-      eat('[');
-      if (eat(']')) return true;
-      do {
-        if (!skip()) return fail();
-      } while (eat(','));
-      return eat(']') || fail();
-    }
-    if (c == '-' || (c >= '0' && c <= '9')) { int64_t v; return integer(v); }
-    for (const char* lit : {"true", "false", "null"}) {
-      size_t n = std::strlen(lit);
-      if (s_.compare(p_, n, lit) == 0) { p_ += n; return true; }
-    }
-    return fail();
-  }
-
- private:
-  bool hex4(uint32_t& cp) {
-    if (p_ + 4 > s_.size()) return false;
-    cp = 0;
-    for (int i = 0; i < 4; ++i) {
-      char h = s_[p_++];
-      cp <<= 4;
-      if (h >= '0' && h <= '9') cp |= h - '0';
-      else if (h >= 'a' && h <= 'f') cp |= h - 'a' + 10;
-      else if (h >= 'A' && h <= 'F') cp |= h - 'A' + 10;
-      else return false;
-    }
-    return true;
-  }
-  bool fail() { ok_ = false; return false; }
-  const std::string& s_;
-  size_t p_ = 0;
-  bool ok_ = true;
-};
+  return q2;
+}
 
 struct PairHash {
   size_t operator()(const std::pair<std::string, std::string>& p) const {
@@ -179,19 +85,12 @@ class Tokenizer {
     std::stringstream ss;
     ss << f.rdbuf();
     const std::string text = ss.str();
-    Json j(text);
-    if (!j.eat('{')) return false;
-    if (j.eat('}')) return false;
-    do {
-      std::string key;
-      if (!j.str(key) || !j.eat(':')) return false;
-      if (key == "model") {
-        if (!read_model(j)) return false;
-      } else if (!j.skip()) {
-        return false;
-      }
-    } while (j.eat(','));
-    return j.ok() && !vocab_.empty();
+    const size_t npos = std::string::npos;
+    const size_t vb = text.find("\"vocab\": {");
+    const size_t mb = text.find("\"merges\": [", vb);
+    if (vb != npos && mb != npos) read_vocab(text, vb + 10, mb);
+    if (mb != npos) read_merges(text, mb + 11, text.rfind(']'));
+    return true;  // like the reference: a file without these sections gives an empty tokenizer
   }
 
   std::vector<int32_t> encode(const std::string& text) const {
@@ -253,50 +152,50 @@ class Tokenizer {
     }
   }
 
-  bool read_model(Json& j) {
-    if (!j.eat('{')) return false;
-    if (j.eat('}')) return true;
-    do {
-      std::string key;
-      if (!j.str(key) || !j.eat(':')) return false;
-      if (key == "vocab") {
-        if (!j.eat('{')) return false;
-        if (!j.eat('}')) {
-          do {
-            std::string piece;
-            int64_t id;
-            if (!j.str(piece) || !j.eat(':') || !j.integer(id)) return false;
-            vocab_[piece] = (int32_t)id;
-            id_to_piece_[(int32_t)id] = piece;
-          } while (j.eat(','));
-          if (!j.eat('}')) return false;
+  // "piece": id entries in [cur, end)
+  void read_vocab(const std::string& t, size_t cur, size_t end) {
+    while (cur < end) {
+      const size_t q1 = t.find('"', cur);
+      if (q1 == std::string::npos || q1 >= end) return;
+      const size_t q2 = quote_end(t, q1, end);
+      if (q2 >= end) return;
+      std::string piece;
+      for (size_t i = q1 + 1; i < q2; ++i) {
+        if (t[i] == '\\' && i + 1 < q2 && (t[i + 1] == '"' || t[i + 1] == '\\')) {
+          piece += t[++i];
+          continue;
         }
-      } else if (key == "merges") {
-        if (!j.eat('[')) return false;
-        int32_t rank = 0;
-        if (!j.eat(']')) {
-          do {
-            std::string a, b;
-            if (j.peek() == '[') {
-              j.eat('[');
-              if (!j.str(a) || !j.eat(',') || !j.str(b) || !j.eat(']')) return false;
-            } else {
-              std::string m;
-              if (!j.str(m)) return false;
-              size_t sp = m.find(' ');
-              if (sp == std::string::npos) continue;  // not a pair: ignored, rank not consumed
-              a = m.substr(0, sp);
-              b = m.substr(sp + 1);
-            }
-            ranks_[std::make_pair(a, b)] = rank++;  // a repeated pair keeps its last rank
-          } while (j.eat(','));
-          if (!j.eat(']')) return false;
-        }
-      } else if (!j.skip()) {
-        return false;
+        piece += t[i];
       }
-    } while (j.eat(','));
-    return j.eat('}');
+      const size_t colon = t.find(':', q2);
+      if (colon == std::string::npos || colon >= end) return;
+      size_t d0 = colon + 1;
+      while (d0 < end && !std::isdigit(static_cast<unsigned char>(t[d0]))) ++d0;
+      size_t d1 = d0;
+      int32_t id = 0;
+      for (; d1 < end && std::isdigit(static_cast<unsigned char>(t[d1])); ++d1) id = id * 10 + (t[d1] - '0');
+      if (d1 > d0) {
+        vocab_[piece] = id;
+        id_to_piece_[id] = piece;
+      }
+      cur = d1;
+    }
+  }
+
+  // quoted "a b" strings in [cur, end), verbatim
+  void read_merges(const std::string& t, size_t cur, size_t end) {
+    if (end == std::string::npos) return;
+    int32_t rank = 0;
+    while (cur < end) {
+      const size_t q1 = t.find('"', cur);
+      if (q1 == std::string::npos || q1 >= end) return;
+      const size_t q2 = quote_end(t, q1, end);
+      if (q2 >= end) return;
+      const std::string m = t.substr(q1 + 1, q2 - q1 - 1);
+      const size_t sp = m.find(' ');
+      if (sp != std::string::npos) ranks_[std::make_pair(m.substr(0, sp), m.substr(sp + 1))] = rank++;
+      cur = q2 + 1;
+    }
   }
 
   std::vector<std::string> merge(const std::string& s) const {
@@ -307,7 +206,7 @@ class Tokenizer {
       i += n;
     }
     while (w.size() > 1) {
-      int32_t best = INT32_MAX;
+      int32_t best = 1000000000;  // ranks at or above 1e9 never merge (src/llama_engine.cpp:668)
       size_t at = SIZE_MAX;
       for (size_t i = 0; i + 1 < w.size(); ++i) {
         auto it = ranks_.find({w[i], w[i + 1]});
