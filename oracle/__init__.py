@@ -8,6 +8,7 @@ to check or time the reference algorithm; the product library never touches it.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -20,9 +21,19 @@ _P = ctypes.c_void_p
 _F = ctypes.POINTER(ctypes.c_float)
 
 
+def _default_ref_dir() -> str | None:
+    """The reference tree: $LLAMA_REF_DIR, else the checker-building machine's copy if present."""
+    env = os.environ.get("LLAMA_REF_DIR")
+    if env:
+        return env
+    cand = Path("/root/reference")
+    return str(cand) if (cand / "src" / "llama_engine.cpp").exists() else None
+
+
 def build(ref_dir: str | None = None) -> None:
-    """Runs oracle/Makefile (restatement always; reference builds when its source is present)."""
+    """Runs oracle/Makefile (restatement always; the reference builds when its source is given)."""
     cmd = ["make", "-s", "-C", str(ORACLE_DIR)]
+    ref_dir = ref_dir or _default_ref_dir()
     if ref_dir:
         cmd.append(f"REF_DIR={ref_dir}")
     res = subprocess.run(cmd, capture_output=True, text=True)
