@@ -109,6 +109,12 @@ def rank_seed(base: int, rank: int) -> int:
     return base + rank
 
 
+def bytes_per_tok_ref(shape, start: int) -> float:
+    """Mean algorithmic bytes per token of a GEN_LEN-token launch from `start` (the launch that
+    profiles/traffic_per_launch.txt scales its DRAM capture to)."""
+    return sum(token_bytes(shape, p) for p in range(start, start + GEN_LEN)) / GEN_LEN
+
+
 def token_bytes(shape, pos: int) -> int:
     """Weights + norms + KV read (pos+1 rows incl. the new one) + KV write, per token."""
     kv_row = shape.layers * shape.kv_dim * 4 * 2
@@ -134,11 +140,19 @@ class ClockSampler:
                                           "-lms", "50"], stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-        time.sleep(0.15)
+        # wait (up to 5 s) until the sampler has written its first row, so that a short timed
+        # region is still covered
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 5.0:
+            self.out.flush()
+            if Path(self.out.name).stat().st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
         if self.proc:
+            time.sleep(0.12)  # at least one more sample after the timed region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -171,42 +185,6 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------------
 # reference / oracle on the host (CPU baseline)
 # ---------------------------------------------------------------------------------------------
-def _cpu_decode_worker(args):
-    model_path, n_tokens, n_warm, use_ref = args
-    sys.path.insert(0, str(ROOT))
-    import oracle
-    if use_ref:
-        lib = oracle.load_ref_engine()
-        h = lib.llama_engine_create(str(model_path).encode())
-        fwd = lambda t, p: lib.llama_engine_forward_token(h, t, p, 1)  # noqa: E731
-        smp = lambda: lib.llama_engine_sample(h, ctypes.c_float(0.0), ctypes.c_float(0.9))  # noqa: E731
-    else:
-        lib = oracle.load_oracle()
-        h = lib.orc_create(str(model_path).encode())
-        fwd = lambda t, p: lib.orc_forward_token(h, t, p, 1)  # noqa: E731
-        smp = lambda: lib.orc_sample_engine(h, ctypes.c_float(0.0), ctypes.c_float(0.9))  # noqa: E731
-    tok = 128000
-    for p in range(n_warm):
-        fwd(tok, p)
-        tok = smp()
-    t0 = time.perf_counter()
-    for p in range(n_warm, n_warm + n_tokens):
-        fwd(tok, p)
-        tok = smp()
-    return time.perf_counter() - t0
-
-
-def cpu_decode_rate(model_path, n_proc, n_tokens, n_warm):
-    import oracle
-    oracle.build()
-    use_ref = oracle.have_reference()
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(n_proc) as pool:
-        times = pool.map(_cpu_decode_worker, [(str(model_path), n_tokens, n_warm, use_ref)] * n_proc)
-    rate = n_proc * n_tokens / max(times)
-    return rate, ("reference" if use_ref else "port")
-
-
 def host_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -251,19 +229,23 @@ def run_ours(args, rank, world, local_rank):
             eng.generate_greedy(first, start, c)
             done += c
 
-    device_steps(args.warmup)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(range(world) if world > 1 else [local_rank]) as clk:
+    # clocks: rank 0 samples every GPU of the job (nvidia-smi indices) from the warm-up through
+    # the timed region (the sampler starts before the warm-up, so a short region is covered)
+    import contextlib
+    clk = ClockSampler(range(world) if world > 1 else [local_rank]) if rank == 0 else None
+    with (clk if clk is not None else contextlib.nullcontext()):
+        device_steps(args.warmup)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         ev0.record(stream)
         device_steps(args.steps)
         ev1.record(stream)
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
-    clocks = clk.summary() if rank == 0 else None
+    clocks = clk.summary() if clk is not None else None
     ms = max_over_ranks([ms], world)[0]
     value = world * args.steps / (ms / 1e3)
 
@@ -294,10 +276,13 @@ def run_ours(args, rank, world, local_rank):
     wall = wall_ms / 1e3
     e2e_value = world * args.steps / max(e2e_ms / 1e3, wall)
 
-    # roofline of the dominant kernel
+    # roofline of the dominant kernel, over the positions actually timed: device_steps runs
+    # generations of up to GEN_LEN tokens, each from position `start`
     peak, peak_kind = hbm_peak()
-    avg_pos = start + (GEN_LEN - 1) / 2.0
-    bytes_tok = sum(token_bytes(shape, p) for p in range(start, start + GEN_LEN)) / GEN_LEN
+    chunks = [min(GEN_LEN, args.steps - d) for d in range(0, args.steps, GEN_LEN)]
+    timed_bytes = sum(token_bytes(shape, start + i) for c in chunks for i in range(c))
+    bytes_tok = timed_bytes / args.steps
+    avg_pos = start + sum(c * (c - 1) / 2.0 for c in chunks) / args.steps
     persistent = eng.decode_path == "persistent"
     pb = phase_bytes(shape, int(avg_pos))
     launches = {"qkv": shape.layers, "attn": shape.layers, "oproj": shape.layers, "gateup": shape.layers,
@@ -311,14 +296,19 @@ def run_ours(args, rank, world, local_rank):
         phase_ms[ph] = float(out.value) if rc == 0 else float("nan")
     share = {ph: phase_ms[ph] * launches[ph] for ph in launches}
     if persistent:
-        # one launch = one 128-token greedy generation (positions 31..158) of the timed region
-        launch_ms = ms / (args.steps / GEN_LEN)
-        launch_bytes = bytes_tok * GEN_LEN
-        achieved = launch_bytes / (launch_ms / 1e3) / 1e9
+        # one launch = one greedy generation of up to GEN_LEN tokens from position 31; achieved =
+        # the timed launches' algorithmic bytes over their summed duration
+        launch_ms = ms / len(chunks)
+        launch_bytes = timed_bytes / len(chunks)
+        achieved = timed_bytes / (ms / 1e3) / 1e9
+        traffic = read_traffic("k_decode_persistent")
         roofline = {"bound": "hbm", "kernel": "k_decode_persistent", "achieved": round(achieved, 1), "peak": peak,
-                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": read_traffic("k_decode_persistent"),
+                    "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "traffic": int(traffic * launch_bytes / (GEN_LEN * bytes_per_tok_ref(shape, start)))
+                    if traffic else None,
                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": int(launch_bytes),
-                    "launch_ms": round(launch_ms, 5), "tokens_per_launch": GEN_LEN,
+                    "launch_ms": round(launch_ms, 5), "tokens_per_launch": round(args.steps / len(chunks), 2),
+                    "timed_positions": f"{start}..{start + max(chunks) - 1}",
                     "kernel_chain_phase_ms": {k: round(v, 5) for k, v in phase_ms.items()}}
     else:
         dom = max(share, key=share.get)
@@ -342,6 +332,7 @@ def run_ours(args, rank, world, local_rank):
     box = None
     if args.box_steps > 0:  # every rank: its own 256 sequences
         box = run_box(args, model, shape, local_rank, world)
+    tp2 = run_tp2(args, model, prompt, local_rank, rank, world) if (world == 2 and args.tp2) else None
     trace = None
     if persistent and rank == 0 and args.trace:
         tr = load_package().trace
@@ -352,10 +343,12 @@ def run_ours(args, rank, world, local_rank):
         launches_timed = (args.steps + GEN_LEN - 1) // GEN_LEN if persistent else kernels_per_token * args.steps
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            rate, kind = cpu_decode_rate(model, 1, args.cpu_tokens, 1)
-            cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": 1, "kind": kind,
-                   "sample": f"{args.cpu_tokens} greedy decode tokens (forward_token + sample) of the same model "
-                             f"after 1 warm-up token, one process, 1 thread"}
+            with mp.get_context("spawn").Pool(1) as pool:
+                secs, use_ref = pool.map(_ref_decode_worker, [(str(model), prompt, 1, args.cpu_tokens, True)])[0]
+            cpu = {"value": round(args.cpu_tokens / secs, 4), "unit": "tok/s", "cores": 1,
+                   "kind": "reference" if use_ref else "port",
+                   "sample": f"one process, 1 thread: prefill of the 31-id prompt (untimed), 1 warm-up + "
+                             f"{args.cpu_tokens} timed greedy decode tokens (forward_token + sample) from position 32"}
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
@@ -363,7 +356,9 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": ("decode-b1: LLaMA-3.2-1B shape" if args.layers == 16 else
                                     f"decode-b1 profiling model: LLaMA-3.2-1B widths, {args.layers} layers")
                                    + ", LLM4S128 block-128 4-bit, seeded random-init N(0,0.02) weights, batch 1 per "
-                                   "GPU, greedy, 128-token generation at positions 31..158 repeated",
+                                   f"GPU, greedy; 32-id prompt, then {args.steps} timed greedy tokens as generations "
+                                   f"of up to {GEN_LEN} tokens from position {start} "
+                                   f"(positions {start}..{start + max(chunks) - 1})",
                        "global_batch": world, "seq_len": start + GEN_LEN, "parallelism": f"dp{world} (replicas)",
                        "l2": "no flush: 657 MB of weights streamed per step > 126 MB L2"},
             "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu,
@@ -373,6 +368,7 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": launches_timed, "decode_path": eng.decode_path, "clocks": clocks,
             **({"batch64": batched} if batched else {}),
             **({"box256": box} if box else {}),
+            **({"tp2": tp2} if tp2 else {}),
             **({"gemv_sweep": gemv} if gemv else {}),
             **({"phase_trace": trace} if trace else {}),
         }
@@ -571,6 +567,48 @@ def run_box(args, model, shape, local_rank, world):
     return out
 
 
+def run_tp2(args, model, prompt, local_rank, rank, world):
+    """Batch-1 latency on two GPUs with the 2-way tensor-parallel engine: one sequence, its layers
+    split over the two ranks with two NCCL all-reduces per layer.  Same greedy generations from
+    position 31 as the headline line; device time of each rank, max over the two."""
+    import torch
+    import torch.distributed as dist
+
+    pkg = load_package()
+    b = pkg.LlamaEngineBindings()
+    obj = [pkg.tp_unique_id(b) if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    eng = pkg.LlamaEngine(str(model), b, device=local_rank, tp_rank=rank, tp_world=world, tp_unique_id=obj[0])
+    stream = torch.cuda.ExternalStream(b.lib.llama_engine_get_stream(eng.handle))
+    eng.prefill([int(t) for t in prompt[:-1]], 0, False)
+    first, start = int(prompt[-1]), PROMPT_LEN - 1
+    steps = min(args.steps, 512)
+
+    def gen(n):
+        done = 0
+        while done < n:
+            c = min(GEN_LEN, n - done)
+            eng.generate_greedy(first, start, c)
+            done += c
+
+    gen(min(args.warmup, GEN_LEN))
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    gen(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks([e0.elapsed_time(e1)], world)[0]
+    eng.close()
+    return {"value": round(steps / (ms / 1e3), 2), "unit": "tok/s", "n_gpus": 2, "steps": steps,
+            "ms_per_token": round(ms / steps, 5),
+            "workload": "decode-b1 latency, one sequence split over 2 GPUs (tensor parallel: q/kv heads, "
+                        "W_o / W_down column halves, gate/up and lm_head row halves; 2 NCCL all-reduces per "
+                        "layer), per-phase kernels in one CUDA graph per token",
+            "api": "llama_engine_create_tp + llama_engine_generate_greedy"}
+
+
 def run_gemv_sweep(local_rank, reps=200):
     """Isolated block-128 GEMV (llama_b128_gemv) at the model's five K x N shapes, M = 1 and 4:
     nibbles uniform 0..15, step ~U(1e-3, 2e-2) and min = -8 step U(0.8, 1.2) as bf16, x ~N(0, 1).
@@ -651,26 +689,88 @@ def read_traffic(kernel_phase: str):
     return None
 
 
+def _write_model_subprocess() -> Path:
+    """The config-0 model file, written (once, cached) by a child process, so that the reference
+    arm's own process maps no library of this repository (the writer is one)."""
+    out = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--write-model"], capture_output=True,
+                         text=True, check=True)
+    return Path(out.stdout.strip().splitlines()[-1])
+
+
+def _ref_decode_worker(args):
+    """One reference process: prefill the 31-id prompt (untimed), `warm` greedy steps, then
+    `steps` timed greedy steps (forward_token + sample), as in src/main.py:339-370."""
+    model_path, prompt, warm, steps, with_prefill = args
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    use_ref = oracle.have_reference()
+    lib = oracle.load_ref_engine() if use_ref else oracle.load_oracle()
+    if use_ref:
+        h = lib.llama_engine_create(str(model_path).encode())
+        fwd = lambda t, p: lib.llama_engine_forward_token(h, t, p, 1)  # noqa: E731
+        smp = lambda: lib.llama_engine_sample(h, ctypes.c_float(0.0), ctypes.c_float(0.9))  # noqa: E731
+        pre = lambda ids: lib.llama_engine_prefill(h, (ctypes.c_int32 * len(ids))(*ids), len(ids), 0, 0)  # noqa: E731
+    else:
+        h = lib.orc_create(str(model_path).encode())
+        fwd = lambda t, p: lib.orc_forward_token(h, t, p, 1)  # noqa: E731
+        smp = lambda: lib.orc_sample_engine(h, ctypes.c_float(0.0), ctypes.c_float(0.9))  # noqa: E731
+        pre = lambda ids: lib.orc_prefill(h, (ctypes.c_int32 * len(ids))(*ids), len(ids), 0, 0)  # noqa: E731
+    pos = 0
+    if with_prefill:
+        pre([int(t) for t in prompt[:-1]])
+        pos = len(prompt) - 1
+    tok = int(prompt[-1])
+    for _ in range(warm):
+        fwd(tok, pos)
+        tok = smp()
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fwd(tok, pos)
+        tok = smp()
+        pos += 1
+    return time.perf_counter() - t0, use_ref
+
+
 def run_reference(args, rank):
+    """The reference engine itself (oracle/_ref, compiled from its own source; the C port of it
+    only when that build is absent, and then labelled "port") on the host cores, on our arm's
+    workload: one sequence, batch 1, the 32-id config-0 prompt prefilled, then greedy decode
+    tokens from position 31.  The reference runs one sequence on one thread on Linux
+    (src/llama_engine.cpp:79-80), so one process is all the threads it can use for this
+    workload.  The all-cores aggregate (one sequence per process) is reported beside it."""
     if rank != 0:
         return None
-    pkg = load_package()
-    shape = pkg.model_file.LLAMA_3_2_1B
-    model = pkg.model_file.cached_model(cache_dir(), shape, seed=0, sigma=0.02)
-    n_proc = max(1, min(host_cores(), 32))
+    import numpy as np
+
+    model = _write_model_subprocess()
+    prompt = np.random.default_rng(rank_seed(1000, 0)).integers(0, 128256, PROMPT_LEN).astype(np.int32)
     steps = max(1, min(args.steps, args.ref_max_steps))
     warm = max(1, min(args.warmup, 2))
-    rate, kind = cpu_decode_rate(model, n_proc, steps, warm)
-    sample = (f"{n_proc} concurrent processes (one sequence each, 1 thread each; the reference is serial on "
-              f"Linux), {warm} warm-up + {steps} timed greedy decode tokens per process")
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(1) as pool:
+        secs, use_ref = pool.map(_ref_decode_worker, [(str(model), prompt, warm, steps, True)])[0]
+    kind = "reference" if use_ref else "port"
+    rate = steps / secs
+    n_proc = max(1, min(host_cores(), 32))
+    agg_steps = max(1, min(steps, 6))
+    with ctx.Pool(n_proc) as pool:
+        times = pool.map(_ref_decode_worker, [(str(model), prompt, 1, agg_steps, False)] * n_proc)
+    agg = n_proc * agg_steps / max(t for t, _ in times)
+    sample = (f"one process, 1 thread: prefill of the 31-id prompt (untimed), {warm} warm-up + {steps} timed "
+              f"greedy decode tokens (forward_token + sample) at positions {PROMPT_LEN - 1 + warm}.."
+              f"{PROMPT_LEN - 1 + warm + steps - 1}")
     return {"impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s", "n_gpus": 0,
-            "steps": steps, "warmup": warm, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "decode-b1: LLaMA-3.2-1B shape, LLM4S128 block-128 4-bit, seeded random-init, "
-                                   "greedy, one sequence per process"},
-            "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": n_proc, "kind": kind,
-                             "sample": sample},
-            "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "steps": steps, "warmup": warm, "ms_per_step": round(1e3 * secs / steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "decode-b1: LLaMA-3.2-1B shape, LLM4S128 block-128 4-bit, seeded random-init "
+                                   "N(0,0.02) weights, batch 1, greedy; 32-id prompt, decode from position 31",
+                       "global_batch": 1, "seq_len": PROMPT_LEN + warm + steps, "parallelism": "none (host CPU)"},
+            "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": 1, "kind": kind, "sample": sample},
+            "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "all_cores_aggregate": {"value": round(agg, 4), "unit": "tok/s", "cores": n_proc, "kind": kind,
+                                    "sample": f"{n_proc} concurrent processes, one sequence each from position 0, "
+                                              f"1 warm-up + {agg_steps} timed greedy tokens each"}}
 
 
 def main():
@@ -693,7 +793,14 @@ def main():
     ap.add_argument("--trace-raw", default=None, help="with --trace: save the raw trace array (.npy) here")
     ap.add_argument("--layers", type=int, default=16,
                     help="layers of the synthetic model (16 = LLaMA-3.2-1B; fewer only for profiling runs)")
+    ap.add_argument("--no-tp2", dest="tp2", action="store_false",
+                    help="skip the 2-way tensor-parallel batch-1 measurement of a 2-GPU run")
+    ap.add_argument("--write-model", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.write_model:  # child of the reference arm: write the config-0 model, print its path
+        pkg = load_package()
+        print(pkg.model_file.cached_model(cache_dir(), pkg.model_file.LLAMA_3_2_1B, seed=0, sigma=0.02))
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", 0))
