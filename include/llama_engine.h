@@ -171,7 +171,8 @@ int llama_engine_score_tokens(llama_engine_t engine, const int32_t* tokens, size
 /* Which implementation runs the slot-0 token steps: 1 = the persistent token-step kernel (one
  * cooperative launch per forward_token, or per whole generate_greedy call; used for dim 2048
  * and ffn_dim in {2048, 4096, 8192}), 0 = the per-phase kernel chain in a CUDA graph (any other
- * supported geometry, or LLAMA_B200_PERSISTENT=0 at create time).  -1 for a NULL handle. */
+ * supported geometry, or LLAMA_B200_PERSISTENT=0 at create time), 2 = the 2-way tensor-parallel
+ * engine (llama_engine_create_tp).  -1 for a NULL handle. */
 int llama_engine_decode_path(llama_engine_t engine);
 
 /* Which implementation runs prefill (2 or more tokens) and llama_engine_forward_batch: 1 = the
@@ -198,6 +199,55 @@ void* llama_engine_get_stream(llama_engine_t engine);
  * "oproj", "gateup", "down", "lmhead", "step" (one whole token, graph launch).  Returns 0 or -1.
  * Activations are whatever the last step left; the numbers are timings only. */
 int llama_engine_profile_phase(llama_engine_t engine, const char* phase, int iters, float* avg_ms);
+
+/* 2-way tensor-parallel batch-1 variant (no counterpart in the reference, which runs on one
+ * CPU): one process per GPU, each creating its engine with the same NCCL unique id.  Rank 0
+ * makes the id with llama_engine_tp_unique_id (writes 128 bytes; returns 0, or -1 when NCCL
+ * cannot be loaded) and the caller passes it to the other rank.  Each rank holds half of every
+ * layer (q heads and kv heads by halves, W_o and W_down by column halves, W_gate / W_up and the
+ * lm_head by row halves); per layer the o-proj and down partial sums are all-reduced (NCCL over
+ * NVLink) and the greedy id is the better of the two ranks' candidates.  Both ranks must make
+ * the same calls in the same order: forward_token, prefill (token by token), sample with
+ * temperature <= 0.01, get_logits (all 128,256 logits, gathered on both ranks),
+ * generate_greedy.  Batched calls are not available on this engine.  NULL on failure. */
+int llama_engine_tp_unique_id(void* out_id, int len);
+llama_engine_t llama_engine_create_tp(const char* model_path, int device, int rank, int world, const void* unique_id,
+                                      int max_seq_len);
+
+/* Opt-in llama3 RoPE frequency scaling.  By default the engine uses the reference's table,
+ * theta_i = 500000^(-2i/64) without scaling (src/llama_engine.cpp:908-917), which is what parity
+ * with the reference requires.  With factor > 0 the table is rebuilt with the "llama3" rescaling
+ * of the reference's models/config.json:26-32 (factor 32, low_freq_factor 1, high_freq_factor 4,
+ * original_max_position 8192 there), which its Hugging Face path applies (chat.py:42): wavelengths
+ * longer than original/low_freq_factor are stretched by factor, shorter than
+ * original/high_freq_factor are kept, and the band between is blended.  factor <= 0 restores the
+ * reference's table.  Waits for the engine's queued work first.  Returns 0, or -1 on bad
+ * parameters or a device error. */
+int llama_engine_set_rope_scaling(llama_engine_t engine, float factor, float low_freq_factor,
+                                  float high_freq_factor, int original_max_position);
+
+/* The RoPE table the engine would use for those parameters (host only): cos_out and sin_out
+ * receive [n_pos][32] floats, n_pos <= 8192.  Returns 0, or -1 on bad arguments. */
+int llama_engine_rope_table(float factor, float low_freq_factor, float high_freq_factor, int original_max_position,
+                            int n_pos, float* cos_out, float* sin_out);
+
+/* Diagnostics, host only (no device is touched): builds the persistent kernel's work schedule
+ * for a model geometry and a grid of `grid` CTAs, and checks it the way the kernel reads it
+ * (every 16-row tile of every phase handled by exactly one CTA with that tile's records of the
+ * right matrices, records consumed in stream order, segments in phase order, every attention
+ * head once per layer, shared-memory capacity limits).  Returns 0 when the schedule is valid,
+ * -1 otherwise with a message in err (err_len bytes, may be NULL). */
+int llama_engine_check_schedule(int layers, int dim, int ffn_dim, int vocab_size, int num_heads, int num_kv_heads,
+                                int grid, char* err, int err_len);
+
+/* Test hook for the bounded device waits: sets the time bound of every wait of the persistent
+ * kernel and of the tensor-core GEMM to wait_ns (0 restores the default of 2 s), and with
+ * expire_code != 0 makes the next launches wait on a device word that nothing writes, so that
+ * the wait runs out: the persistent kernel's CTA 0 at the start of a launch, the GEMM's MMA
+ * issuer before its first block.  The launch then drains and the next waiting call fails with
+ * the timeout reported; expire_code = 0 turns that off again and clears the recorded error so
+ * the engine can be used again.  Returns 0, or -1 for a NULL handle. */
+int llama_engine_debug_waits(llama_engine_t engine, unsigned long long wait_ns, int expire_code);
 
 /* Greedy argmax of n device-resident fp32 logits that allocates no memory: writes the first
  * index among the maxima (values <= -1e30 and NaN never win; 0 when none qualifies, the

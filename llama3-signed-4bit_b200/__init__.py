@@ -14,4 +14,5 @@ from .engine import (  # noqa: F401
     LlamaEngineBindings,
     TokenizerWrapper,
     ensure_library_built,
+    tp_unique_id,
 )

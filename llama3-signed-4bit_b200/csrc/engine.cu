@@ -5,6 +5,7 @@
 // arena, builds the RoPE table on the host with the reference's own libm calls (:908-917) so
 // the table is bit-identical, allocates device KV caches, and captures the per-token kernel
 // sequence into CUDA graphs.
+#include <dlfcn.h>
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -16,8 +17,10 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "batch_kernels.cuh"
@@ -26,6 +29,7 @@
 #include "persistent.cuh"
 #include "tc_gemm.cuh"
 #include "llama_engine.h"
+#include <nccl.h>
 
 #define LE_API extern "C" __attribute__((visibility("default")))
 
@@ -227,6 +231,8 @@ struct Engine {
   int tc_am_parts = 0;
   uint32_t* tc_err = nullptr;  // device error word of the tensor-core GEMM
   bool tc_dirty = true;        // a batched step ran since tc_err was last read
+  unsigned long long tc_wait_ns = kWaitNs;  // bound on the GEMM's waits (test hook)
+  int tc_expire = 0;                        // test hook: the GEMM's issuer waits on nothing
   // decode steps of the batched path replayed as CUDA graphs, one per (rows, logits rows,
   // attention splits); the rows' ids, positions and slots are read from t_idx
   struct TcGraph { int n, nlog, splits; bool fold; cudaGraphExec_t exec; };
@@ -239,6 +245,21 @@ struct Engine {
 
   cudaGraphExec_t g_fwd[2] = {nullptr, nullptr};  // [compute_logits]
   cudaGraphExec_t g_gen = nullptr;                // forward + greedy + advance
+
+  // 2-way tensor-parallel batch-1 variant (tp_world == 2): this rank's share of every layer
+  int tp_world = 1, tp_rank = 0;
+  ncclComm_t tp_comm = nullptr;
+  uint8_t* tp_arena = nullptr;      // column halves of W_o and W_down
+  std::vector<DevLayer> tpl;        // row slices (q, k, v, gate, up) and column halves (o, down)
+  QMat tp_lm{};                     // this rank's vocabulary rows of the lm_head
+  float* tp_kc = nullptr;           // [layers][max_seq][kv_dim / 2]
+  float* tp_vc = nullptr;
+  float* tp_qkv = nullptr;          // [(dim + 2 kv_dim) / 2]
+  float* tp_attn = nullptr;         // [dim / 2]
+  float* tp_act = nullptr;          // [ffn / 2]
+  ArgmaxPart* tp_part = nullptr;    // [lm_grid]
+  int32_t* tp_cand = nullptr;       // [world][2]: (value bits, global index) of each rank's greedy candidate
+  cudaGraphExec_t tp_g[3] = {nullptr, nullptr, nullptr};  // no logits | logits (gathered) | greedy + advance
 
   std::string err;
 };
@@ -376,56 +397,37 @@ static size_t persistent_smem() {
   return (size_t)kRingSlots * kRecBytes + kImageBytes + kMiscFloats * 4 + kRingSlots * 8 + kSchedBytes;
 }
 
-static bool init_persistent(Engine* E) {
-  if (!persistent_supported(E)) return true;
-  const int L = (int)E->layers, G = E->num_sms;
-  const size_t smem = persistent_smem();
-  LE_CK(cudaFuncSetAttribute(k_decode_persistent<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  LE_CK(cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  int per_sm = 0;
-  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent<false>, kPThreads, smem));
-  int per_sm_trace = 0;
-  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_trace, k_decode_persistent<true>, kPThreads, smem));
-  per_sm = std::min(per_sm, per_sm_trace);
-  if (per_sm < 1) {  // keep the kernel-chain path, and say why
-    cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, k_decode_persistent<false>);
-    E->err = "persistent kernel declined: 0 resident CTAs per SM (regs " + std::to_string(fa.numRegs) +
-             ", static smem " + std::to_string(fa.sharedSizeBytes) + ", dynamic smem " + std::to_string(smem) +
-             ", max threads " + std::to_string(fa.maxThreadsPerBlock) + ")";
-    return true;
-  }
-  // record arena: per layer [q|k|v tiles][o tiles][gate tiles][up tiles][down tiles x 4], lm_head
-  const size_t rec_qkv = (E->dim + 2 * E->kv_dim) / 16, rec_o = E->dim / 16, rec_g = E->ffn / 16;
-  const size_t rec_d = (E->dim / 16) * (E->ffn / 2048), rec_lm = E->vocab / 16;
-  const size_t per_layer = rec_qkv + rec_o + 2 * rec_g + rec_d;
-  const size_t nrec_total = per_layer * L + rec_lm;
-  E->rec_bytes = nrec_total * kRecBytes;
-  LE_CK(cudaMalloc(&E->rec_arena, E->rec_bytes));
-  auto layer_base = [&](int l) { return (size_t)l * per_layer; };
-  auto repack = [&](const QMat& W, size_t rec0) -> bool {
-    k_repack<<<E->num_sms * 8, 256, 0, E->stream>>>(W, E->rec_arena + rec0 * kRecBytes);
-    LE_CK(cudaGetLastError());
-    return true;
-  };
-  for (int l = 0; l < L; ++l) {
-    const DevLayer& D = E->L[l];
-    size_t b = layer_base(l);
-    if (!repack(D.q, b)) return false;
-    if (!repack(D.k, b + E->dim / 16)) return false;
-    if (!repack(D.v, b + (E->dim + E->kv_dim) / 16)) return false;
-    b += rec_qkv;
-    if (!repack(D.o, b)) return false;
-    b += rec_o;
-    if (!repack(D.g, b)) return false;
-    if (!repack(D.u, b + rec_g)) return false;
-    b += 2 * rec_g;
-    if (!repack(D.d, b)) return false;
-  }
-  const size_t lm_base = per_layer * L;
-  if (!repack(E->lm_head, lm_base)) return false;
+// ---------------------------------------------------------------------------------------------
+// Static schedule of the persistent kernel (host only, no device calls).
+// ---------------------------------------------------------------------------------------------
+struct PGeom { int layers, dim, ffn, vocab, heads, kv_heads; };
 
-  // ---- static schedule ----
+struct PSchedule {
+  // record arena: per layer [q|k|v tiles][o tiles][gate tiles][up tiles][down tiles x ffn/2048],
+  // then the lm_head tiles
+  size_t rec_qkv = 0, rec_o = 0, rec_g = 0, rec_d = 0, rec_lm = 0, per_layer = 0, lm_base = 0, nrec_total = 0;
+  size_t layer_base(int l) const { return (size_t)l * per_layer; }
+  std::vector<PCtaSched> sched;
+  std::vector<PSeg> segs;
+  std::vector<PItem> items;
+  std::vector<uint32_t> recs;
+  int n_lm_ctas = 0;
+};
+
+// Every phase hands out whole items (16-row tiles with their records) round-robin over the CTAs,
+// continuing where the previous phase stopped; attention heads are spread over the grid.  Inside
+// a CTA a segment's records are cut into work units of 16 / split blocks (split chosen per
+// segment by choose_split).
+static bool build_schedule(const PGeom& g, int G, PSchedule& P, std::string& err) {
+  const int L = g.layers, kv_dim = g.kv_heads * LE_HEAD_DIM;
+  P.rec_qkv = (size_t)(g.dim + 2 * kv_dim) / 16;
+  P.rec_o = (size_t)g.dim / 16;
+  P.rec_g = (size_t)g.ffn / 16;
+  P.rec_d = (size_t)(g.dim / 16) * (g.ffn / 2048);
+  P.rec_lm = (size_t)g.vocab / 16;
+  P.per_layer = P.rec_qkv + P.rec_o + 2 * P.rec_g + P.rec_d;
+  P.lm_base = P.per_layer * L;
+  P.nrec_total = P.lm_base + P.rec_lm;
   struct CtaLists { std::vector<PSeg> segs; std::vector<PItem> items; std::vector<uint32_t> recs; };
   // Work units per record for a segment of n_rec records: the split (block ranges of 16/split
   // blocks) that minimises the busiest warp's (units x (blocks per unit + 2)), the 2 standing
@@ -440,9 +442,8 @@ static bool init_persistent(Engine* E) {
     }
     return best;
   };
-  bool split_ok = true;
+  bool fits = true;
   std::vector<CtaLists> C(G);
-  std::vector<int> warp_rr(G, 0);
   int rot = 0;
   auto add_phase = [&](uint16_t kind, int layer, int n_items, int nrec_per_item,
                        const std::function<size_t(int, int)>& rec_of, const std::function<int(int)>& cta_of) {
@@ -467,30 +468,30 @@ static bool init_persistent(Engine* E) {
       sg.item_end = (uint16_t)C[c].items.size();
       const int n_rec = (int)per[c].size() * nrec_per_item;
       sg.split = (uint8_t)choose_split(n_rec);
-      if (n_rec * sg.split > kMaxUnits) split_ok = false;
+      if (n_rec * sg.split > kMaxUnits) fits = false;
       C[c].segs.push_back(sg);
     }
   };
-  const int n_qkv = (int)rec_qkv, n_o = (int)rec_o, n_gu = (int)rec_g, n_down = (int)(E->dim / 16);
-  const int kq_down = (int)(E->ffn / 2048), n_lm = (int)rec_lm;
+  const int n_qkv = (int)P.rec_qkv, n_o = (int)P.rec_o, n_gu = (int)P.rec_g, n_down = g.dim / 16;
+  const int kq_down = g.ffn / 2048, n_lm = (int)P.rec_lm;
   for (int l = 0; l < L; ++l) {
-    const size_t b = layer_base(l);
+    const size_t b = P.layer_base(l);
     int r0 = rot;
     add_phase(PK_QKV, l, n_qkv, 1, [&](int i, int) { return b + i; }, [&](int i) { return (r0 + i) % G; });
     rot = (rot + n_qkv) % G;
-    add_phase(PK_ATTN, l, (int)E->heads, 0, [&](int, int) { return (size_t)0; },
-              [&](int h) { return (int)(((long long)h * G) / E->heads + G / (2 * (int)E->heads)) % G; });
+    add_phase(PK_ATTN, l, g.heads, 0, [&](int, int) { return (size_t)0; },
+              [&](int h) { return (int)(((long long)h * G) / g.heads + G / (2 * g.heads)) % G; });
     r0 = rot;
-    add_phase(PK_O, l, n_o, 1, [&](int i, int) { return b + rec_qkv + i; }, [&](int i) { return (r0 + i) % G; });
+    add_phase(PK_O, l, n_o, 1, [&](int i, int) { return b + P.rec_qkv + i; }, [&](int i) { return (r0 + i) % G; });
     rot = (rot + n_o) % G;
     r0 = rot;
     add_phase(PK_GATEUP, l, n_gu, 2,
-              [&](int i, int r) { return b + rec_qkv + rec_o + (r == 0 ? 0 : rec_g) + i; },
+              [&](int i, int r) { return b + P.rec_qkv + P.rec_o + (r == 0 ? 0 : P.rec_g) + i; },
               [&](int i) { return (r0 + i) % G; });
     rot = (rot + n_gu) % G;
     r0 = rot;
     add_phase(PK_DOWN, l, n_down, kq_down,
-              [&](int i, int r) { return b + rec_qkv + rec_o + 2 * rec_g + (size_t)i * kq_down + r; },
+              [&](int i, int r) { return b + P.rec_qkv + P.rec_o + 2 * P.rec_g + (size_t)i * kq_down + r; },
               [&](int i) { return (r0 + i) % G; });
     rot = (rot + n_down) % G;
   }
@@ -498,37 +499,174 @@ static bool init_persistent(Engine* E) {
   for (int c = 0; c < G; ++c) nrec_nolm[c] = (uint32_t)C[c].recs.size();
   {
     const int r0 = rot;
-    add_phase(PK_LMHEAD, L, n_lm, 1, [&](int i, int) { return lm_base + i; }, [&](int i) { return (r0 + i) % G; });
+    add_phase(PK_LMHEAD, L, n_lm, 1, [&](int i, int) { return P.lm_base + i; }, [&](int i) { return (r0 + i) % G; });
   }
-  int n_lm_ctas = 0;
+  P.n_lm_ctas = 0;
   for (int c = 0; c < G; ++c)
     for (const auto& sg : C[c].segs)
-      if (sg.kind == PK_LMHEAD) ++n_lm_ctas;
+      if (sg.kind == PK_LMHEAD) ++P.n_lm_ctas;
+  for (int c = 0; c < G; ++c)
+    if (C[c].recs.size() > (size_t)kMaxRecs || C[c].items.size() > (size_t)kMaxItems ||
+        C[c].segs.size() > (size_t)kMaxSegs)
+      fits = false;
+  if (!fits) { err = "a CTA's schedule exceeds its shared-memory capacity"; return false; }
+  P.sched.assign(G, PCtaSched{});
   for (int c = 0; c < G; ++c) {
-    if (!split_ok || C[c].recs.size() > (size_t)kMaxRecs || C[c].items.size() > (size_t)kMaxItems ||
-        C[c].segs.size() > (size_t)kMaxSegs) {
-      E->err = "persistent kernel declined: a CTA's schedule exceeds its shared-memory capacity";
-      cudaFree(E->rec_arena);
-      E->rec_arena = nullptr;
-      return true;  // keep the kernel-chain path
+    PCtaSched& cs = P.sched[c];
+    cs.seg_off = (uint32_t)P.segs.size();
+    cs.nseg = (uint32_t)C[c].segs.size();
+    cs.item_off = (uint32_t)P.items.size();
+    cs.nitem = (uint32_t)C[c].items.size();
+    cs.rec_off = (uint32_t)P.recs.size();
+    cs.nrec = (uint32_t)C[c].recs.size();
+    cs.nrec_nolm = nrec_nolm[c];
+    P.segs.insert(P.segs.end(), C[c].segs.begin(), C[c].segs.end());
+    P.items.insert(P.items.end(), C[c].items.begin(), C[c].items.end());
+    P.recs.insert(P.recs.end(), C[c].recs.begin(), C[c].recs.end());
+  }
+  return true;
+}
+
+// Host check of a schedule against the arena layout, reading every entry the way the kernel
+// does: every (phase, layer, tile) is one item of exactly one CTA, and its records are that
+// tile's records of the right matrices (gate then up; the down row's 2048-column groups in
+// order); items and records are consumed in stream order; segments run in phase order; every
+// attention head runs once per layer; units fit the shared-memory partials.
+static bool check_schedule(const PGeom& g, int G, const PSchedule& P, std::string& err) {
+  const int L = g.layers, KQd = g.ffn / 2048;
+  struct RecInfo { int kind, layer, tile, sub; };  // sub: gate 0 / up 1, or the down kq
+  auto rec_info = [&](size_t r) -> RecInfo {
+    if (r >= P.nrec_total) return {-1, -1, -1, -1};
+    if (r >= P.lm_base) return {PK_LMHEAD, L, (int)(r - P.lm_base), 0};
+    const int l = (int)(r / P.per_layer);
+    size_t o = r % P.per_layer;
+    if (o < P.rec_qkv) return {PK_QKV, l, (int)o, 0};
+    o -= P.rec_qkv;
+    if (o < P.rec_o) return {PK_O, l, (int)o, 0};
+    o -= P.rec_o;
+    if (o < 2 * P.rec_g) return {PK_GATEUP, l, (int)(o % P.rec_g), (int)(o / P.rec_g)};
+    o -= 2 * P.rec_g;
+    return {PK_DOWN, l, (int)(o / KQd), (int)(o % KQd)};
+  };
+  auto ntiles_of = [&](int kind) -> int {
+    switch (kind) {
+      case PK_QKV: return (int)P.rec_qkv;
+      case PK_ATTN: return g.heads;
+      case PK_O: return (int)P.rec_o;
+      case PK_GATEUP: return (int)P.rec_g;
+      case PK_DOWN: return g.dim / 16;
+      default: return (int)P.rec_lm;
     }
-  }
-  std::vector<PCtaSched> sched(G);
-  std::vector<PSeg> segs;
-  std::vector<PItem> items;
-  std::vector<uint32_t> recs;
+  };
+  auto nrec_of = [&](int kind) { return kind == PK_ATTN ? 0 : kind == PK_GATEUP ? 2 : kind == PK_DOWN ? KQd : 1; };
+  std::map<std::pair<int, int>, std::vector<int>> seen;  // (kind, layer) -> items per tile
+  auto fail = [&](int c, const std::string& m) { err = "schedule check, CTA " + std::to_string(c) + ": " + m; return false; };
   for (int c = 0; c < G; ++c) {
-    sched[c].seg_off = (uint32_t)segs.size();
-    sched[c].nseg = (uint32_t)C[c].segs.size();
-    sched[c].item_off = (uint32_t)items.size();
-    sched[c].nitem = (uint32_t)C[c].items.size();
-    sched[c].rec_off = (uint32_t)recs.size();
-    sched[c].nrec = (uint32_t)C[c].recs.size();
-    sched[c].nrec_nolm = nrec_nolm[c];
-    segs.insert(segs.end(), C[c].segs.begin(), C[c].segs.end());
-    items.insert(items.end(), C[c].items.begin(), C[c].items.end());
-    recs.insert(recs.end(), C[c].recs.begin(), C[c].recs.end());
+    const PCtaSched& cs = P.sched[c];
+    int next_item = 0, next_rec = 0, prev_order = -1;
+    for (uint32_t si = 0; si < cs.nseg; ++si) {
+      const PSeg& sg = P.segs[cs.seg_off + si];
+      const int order = sg.kind == PK_LMHEAD ? 1 << 30 : sg.layer * 8 + sg.kind;
+      if (order <= prev_order) return fail(c, "segments out of phase order");
+      prev_order = order;
+      if (sg.item_begin != next_item || sg.item_end <= sg.item_begin || sg.item_end > cs.nitem)
+        return fail(c, "segment items not contiguous");
+      if (sg.kind != PK_ATTN && sg.split != 2 && sg.split != 4 && sg.split != 8 && sg.split != 16)
+        return fail(c, "bad split");
+      int seg_recs = 0;
+      auto& cov = seen[{sg.kind, sg.layer}];
+      if (cov.empty()) cov.assign(ntiles_of(sg.kind), 0);
+      for (int it = sg.item_begin; it < sg.item_end; ++it) {
+        const PItem& item = P.items[cs.item_off + it];
+        if (item.kind != sg.kind || item.layer != sg.layer) return fail(c, "item of another phase");
+        if (item.tile >= cov.size()) return fail(c, "tile out of range");
+        cov[item.tile]++;
+        if (item.nrec != nrec_of(sg.kind)) return fail(c, "wrong record count");
+        if (sg.kind == PK_ATTN) continue;
+        if (item.rec != next_rec) return fail(c, "records not in stream order");
+        for (int k = 0; k < item.nrec; ++k) {
+          const RecInfo ri = rec_info(P.recs[cs.rec_off + item.rec + k]);
+          if (ri.kind != sg.kind || ri.layer != (sg.kind == PK_LMHEAD ? L : sg.layer) || ri.tile != item.tile ||
+              ri.sub != (sg.kind == PK_GATEUP || sg.kind == PK_DOWN ? k : 0))
+            return fail(c, "record does not belong to its item");
+        }
+        next_rec += item.nrec;
+        seg_recs += item.nrec;
+      }
+      if (sg.kind != PK_ATTN && seg_recs * sg.split > kMaxUnits) return fail(c, "too many units in a segment");
+      if (sg.kind != PK_LMHEAD && (uint32_t)next_rec > cs.nrec_nolm) return fail(c, "records before the lm_head");
+      next_item = sg.item_end;
+    }
+    if ((uint32_t)next_item != cs.nitem || (uint32_t)next_rec != cs.nrec) return fail(c, "item/record totals");
   }
+  for (int l = 0; l < L; ++l)
+    for (int kind : {PK_QKV, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN}) {
+      auto it = seen.find({kind, l});
+      if (it == seen.end()) { err = "schedule check: a phase has no work"; return false; }
+      for (int v : it->second)
+        if (v != 1) { err = "schedule check: a tile or head is not handled exactly once"; return false; }
+    }
+  auto it = seen.find({PK_LMHEAD, L});
+  if (it == seen.end()) { err = "schedule check: no lm_head work"; return false; }
+  for (int v : it->second)
+    if (v != 1) { err = "schedule check: an lm_head tile is not handled exactly once"; return false; }
+  return true;
+}
+
+static bool init_persistent(Engine* E) {
+  if (!persistent_supported(E)) return true;
+  const int L = (int)E->layers, G = E->num_sms;
+  const size_t smem = persistent_smem();
+  LE_CK(cudaFuncSetAttribute(k_decode_persistent<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  LE_CK(cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent<false>, kPThreads, smem));
+  int per_sm_trace = 0;
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_trace, k_decode_persistent<true>, kPThreads, smem));
+  per_sm = std::min(per_sm, per_sm_trace);
+  if (per_sm < 1) {  // keep the kernel-chain path, and say why
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, k_decode_persistent<false>);
+    E->err = "persistent kernel declined: 0 resident CTAs per SM (regs " + std::to_string(fa.numRegs) +
+             ", static smem " + std::to_string(fa.sharedSizeBytes) + ", dynamic smem " + std::to_string(smem) +
+             ", max threads " + std::to_string(fa.maxThreadsPerBlock) + ")";
+    return true;
+  }
+  PGeom geo{L, (int)E->dim, (int)E->ffn, (int)E->vocab, (int)E->heads, (int)E->kv_heads};
+  PSchedule P;
+  std::string serr;
+  if (!build_schedule(geo, G, P, serr) || !check_schedule(geo, G, P, serr)) {
+    E->err = "persistent kernel declined: " + serr;
+    return true;  // keep the kernel-chain path
+  }
+  E->rec_bytes = P.nrec_total * kRecBytes;
+  LE_CK(cudaMalloc(&E->rec_arena, E->rec_bytes));
+  auto repack = [&](const QMat& W, size_t rec0) -> bool {
+    k_repack<<<E->num_sms * 8, 256, 0, E->stream>>>(W, E->rec_arena + rec0 * kRecBytes);
+    LE_CK(cudaGetLastError());
+    return true;
+  };
+  for (int l = 0; l < L; ++l) {
+    const DevLayer& D = E->L[l];
+    size_t b = P.layer_base(l);
+    if (!repack(D.q, b)) return false;
+    if (!repack(D.k, b + E->dim / 16)) return false;
+    if (!repack(D.v, b + (E->dim + E->kv_dim) / 16)) return false;
+    b += P.rec_qkv;
+    if (!repack(D.o, b)) return false;
+    b += P.rec_o;
+    if (!repack(D.g, b)) return false;
+    if (!repack(D.u, b + P.rec_g)) return false;
+    b += 2 * P.rec_g;
+    if (!repack(D.d, b)) return false;
+  }
+  if (!repack(E->lm_head, P.lm_base)) return false;
+  const std::vector<PCtaSched>& sched = P.sched;
+  const std::vector<PSeg>& segs = P.segs;
+  const std::vector<PItem>& items = P.items;
+  const std::vector<uint32_t>& recs = P.recs;
+  const int n_lm_ctas = P.n_lm_ctas;
+  const size_t lm_base = P.lm_base;
   auto upload = [&](void** dst, const void* src, size_t bytes) -> bool {
     LE_CK(cudaMalloc(dst, std::max<size_t>(bytes, 16)));
     if (bytes) LE_CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
@@ -564,10 +702,12 @@ static bool init_persistent(Engine* E) {
   A.ctrl = E->d_ctrl; A.prm = E->d_params;
   A.token_log = E->token_log; A.am_result = E->am_result;
   A.lm_rec_base = (unsigned long long)lm_base * kRecBytes;
+  A.wait_ns = kWaitNs;
   A.layers = L; A.dim = (int)E->dim; A.ffn = (int)E->ffn; A.vocab = (int)E->vocab;
   A.heads = (int)E->heads; A.kv_heads = (int)E->kv_heads; A.max_seq = E->max_seq;
   A.n_lm_ctas = n_lm_ctas;
   A.n_tokens = 1; A.do_logits = 1;
+  A.expire_where = 0;
   E->p_grid = G;
   LE_CK(cudaStreamSynchronize(E->stream));
   E->persist = true;
@@ -719,6 +859,8 @@ static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int s
   A.kb_split = (W.kb + splits - 1) / splits;
   A.splits = (W.kb + A.kb_split - 1) / A.kb_split;
   A.error = E->tc_err;
+  A.wait_ns = E->tc_wait_ns;
+  A.expire = E->tc_expire;
   const int units = A.tiles * A.tok_tiles * A.splits;
   launch_pdl(tc::k_tc_gemm, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::kSmemBytes, E->stream, A);
   return A.splits;
@@ -909,6 +1051,50 @@ static bool persistent_ok(Engine* E) {
   return check_status(E);
 }
 
+// RoPE tables [n_pos][32] (cos, sin).  The default is the reference's table: theta_i =
+// powf(500000, -2i/64), cos/sin(pos * theta_i) in float with the same libm calls
+// (src/llama_engine.cpp:908-917), so the table is bit-identical.  With factor > 0 the
+// frequencies are first rescaled the "llama3" way (the rope_scaling of the reference's
+// models/config.json:26-32, applied by its Hugging Face path chat.py:42 but not by the C++
+// engine): with wavelength w_i = 2 pi / theta_i, low = original / low_freq_factor and
+// high = original / high_freq_factor, theta_i is kept when w_i < high, divided by factor when
+// w_i > low, and in between blended as (1 - s) theta_i / factor + s theta_i with
+// s = (original / w_i - low_freq_factor) / (high_freq_factor - low_freq_factor).
+struct RopeScaling {
+  float factor = 0.0f;  // <= 0: the reference's unscaled table
+  float low_freq_factor = 1.0f, high_freq_factor = 4.0f;
+  int original_max_position = 8192;
+};
+
+static void build_rope_table(const RopeScaling& rs, int n_pos, std::vector<float>& cs, std::vector<float>& sn) {
+  const size_t hd2 = LE_HEAD_DIM / 2;
+  float theta[LE_HEAD_DIM / 2];
+  for (size_t i = 0; i < hd2; ++i) {
+    theta[i] = std::pow(500000.0f, -2.0f * static_cast<float>(i) / static_cast<float>(LE_HEAD_DIM));
+    if (rs.factor > 0.0f) {
+      const double pi = 3.14159265358979323846, t = theta[i];
+      const double w = 2.0 * pi / t, orig = rs.original_max_position;
+      const double low = orig / rs.low_freq_factor, high = orig / rs.high_freq_factor;
+      double v = t;
+      if (w > low) {
+        v = t / rs.factor;
+      } else if (w >= high) {
+        const double sm = (orig / w - rs.low_freq_factor) / (rs.high_freq_factor - rs.low_freq_factor);
+        v = (1.0 - sm) * t / rs.factor + sm * t;
+      }
+      theta[i] = static_cast<float>(v);
+    }
+  }
+  cs.assign((size_t)n_pos * hd2, 0.0f);
+  sn.assign((size_t)n_pos * hd2, 0.0f);
+  for (size_t pos = 0; pos < (size_t)n_pos; ++pos) {
+    for (size_t i = 0; i < hd2; ++i) {
+      cs[pos * hd2 + i] = std::cos(static_cast<float>(pos) * theta[i]);
+      sn[pos * hd2 + i] = std::sin(static_cast<float>(pos) * theta[i]);
+    }
+  }
+}
+
 static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   LE_CK(cudaSetDevice(E->device));
   LE_CK(cudaDeviceGetAttribute(&E->num_sms, cudaDevAttrMultiProcessorCount, E->device));
@@ -964,15 +1150,8 @@ static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
 
   // ---- RoPE table on the host, same float calls as src/llama_engine.cpp:911-917 ----
   {
-    const size_t hd2 = LE_HEAD_DIM / 2;
-    std::vector<float> cs((size_t)LE_MAX_SEQ_LEN * hd2), sn((size_t)LE_MAX_SEQ_LEN * hd2);
-    for (size_t pos = 0; pos < LE_MAX_SEQ_LEN; ++pos) {
-      for (size_t i = 0; i < hd2; ++i) {
-        float theta = std::pow(500000.0f, -2.0f * static_cast<float>(i) / static_cast<float>(LE_HEAD_DIM));
-        cs[pos * hd2 + i] = std::cos(static_cast<float>(pos) * theta);
-        sn[pos * hd2 + i] = std::sin(static_cast<float>(pos) * theta);
-      }
-    }
+    std::vector<float> cs, sn;
+    build_rope_table(RopeScaling{}, LE_MAX_SEQ_LEN, cs, sn);
     LE_CK(cudaMalloc(&E->rope_cos, cs.size() * 4));
     LE_CK(cudaMalloc(&E->rope_sin, sn.size() * 4));
     LE_CK(cudaMemcpy(E->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
@@ -1015,15 +1194,18 @@ static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   if (!capture(E, row_buffers(E, 0, 0, true, 0), &E->g_fwd[1])) return false;
   if (!capture(E, row_buffers(E, 0, 0, true, 1), &E->g_gen)) return false;
   LE_CK(cudaStreamSynchronize(E->stream));
+  if (E->tp_world > 1) return true;  // the tensor-parallel engine runs its own graph (init_tp)
   if (!init_persistent(E)) return false;
   if (!init_tc(E)) return false;
   return true;
 }
 
+static void destroy_tp(Engine* E);
 static void destroy(Engine* E) {
   if (!E) return;
   DeviceGuard dg(E->device);
   if (E->stream) cudaStreamSynchronize(E->stream);
+  destroy_tp(E);
   for (auto& g : E->g_fwd) if (g) cudaGraphExecDestroy(g);
   for (auto& g : E->tc_graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
   if (E->g_gen) cudaGraphExecDestroy(E->g_gen);
@@ -1047,7 +1229,9 @@ static void destroy(Engine* E) {
   delete E;
 }
 
-static Engine* create(const char* path, int device, int max_batch, int max_seq) {
+static bool init_tp(Engine* E, const ncclUniqueId& id);
+static Engine* create(const char* path, int device, int max_batch, int max_seq, int tp_rank = 0, int tp_world = 1,
+                      const ncclUniqueId* tp_id = nullptr) {
   if (!path) { set_create_error("model path is NULL"); return nullptr; }
   if (max_batch < 1 || max_batch > 4096) { set_create_error("max_batch out of range"); return nullptr; }
   if (max_seq == 0) max_seq = LE_MAX_SEQ_LEN;
@@ -1068,10 +1252,13 @@ static Engine* create(const char* path, int device, int max_batch, int max_seq) 
   E->device = device;
   E->max_batch = max_batch;
   E->max_seq = max_seq;
+  E->tp_rank = tp_rank;
+  E->tp_world = tp_world;
   bool good;
   {
     DeviceGuard dg(device);
     good = init_device(E, static_cast<const uint8_t*>(map), P);
+    if (good && tp_world > 1) good = init_tp(E, *tp_id);
   }
   munmap(map, size);
   if (!good) {
@@ -1080,6 +1267,232 @@ static Engine* create(const char* path, int device, int max_batch, int max_seq) 
     return nullptr;
   }
   return E;
+}
+
+// =============================================================================================
+// 2-way tensor-parallel batch-1 variant.  Each of the two ranks (one process and one GPU each)
+// holds half of every layer: q heads [16r, 16r+16) and kv heads [4r, 4r+4) (rows of Wq, Wk, Wv),
+// the matching 1024 columns of W_o, ffn rows [4096r, 4096r+4096) of W_gate / W_up and those
+// columns of W_down, and vocabulary rows [64128r, 64128r+64128) of the lm_head.  Per layer the
+// o-proj and down partial sums are added across the ranks with one NCCL all-reduce each (rank 0
+// adds the residual, rank 1 contributes its partial from zero), and the greedy id is the better
+// of the two ranks' candidates (all-gather of (value, index); the lower index wins ties).  The
+// step runs the per-phase kernels and is captured into a CUDA graph with the NCCL calls.
+// NCCL is loaded at run time, so the engine library has no link-time NCCL dependency.
+// =============================================================================================
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+static const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    // an NCCL already loaded into the process (e.g. by PyTorch) is found first by its soname
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.comm_destroy &&
+             api.error_string;
+  });
+  return api;
+}
+
+#define LE_NCCL(expr)                                                        \
+  do {                                                                       \
+    ncclResult_t r_ = (expr);                                                \
+    if (r_ != ncclSuccess) {                                                 \
+      E->err = std::string(#expr) + ": " + nccl().error_string(r_);          \
+      return false;                                                          \
+    }                                                                        \
+  } while (0)
+
+// This rank's greedy candidate with its global index, as (value bits, index).
+__global__ void k_tp_candidate(const ArgmaxPart* __restrict__ part, int nparts, int offset, int32_t* __restrict__ out) {
+  __shared__ float s_bv[32];
+  __shared__ int s_bi[32];
+  float bv = -1e30f;
+  int bi = kNoIndex;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) argmax_merge(bv, bi, part[i].val, part[i].idx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_merge(bv, bi, ov, oi);
+  }
+  if ((threadIdx.x & 31) == 0) { s_bv[threadIdx.x >> 5] = bv; s_bi[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) argmax_merge(bv, bi, s_bv[w], s_bi[w]);
+    out[0] = __float_as_int(bv);
+    out[1] = bi == kNoIndex ? kNoIndex : bi + offset;
+  }
+}
+
+// The greedy id over all ranks' candidates (the reference's rule: first index among the
+// maxima, 0 when none exceeds -1e30); with `advance` the step parameters move on as in
+// k_argmax_finish.
+__global__ void k_tp_pick(const int32_t* __restrict__ cand, int world, int32_t* __restrict__ result,
+                          StepParams* __restrict__ prm, int32_t* __restrict__ token_log, int advance) {
+  if (threadIdx.x != 0) return;
+  float bv = -1e30f;
+  int bi = kNoIndex;
+  for (int r = 0; r < world; ++r) argmax_merge(bv, bi, __int_as_float(cand[2 * r]), cand[2 * r + 1]);
+  const int id = bi == kNoIndex ? 0 : bi;
+  *result = id;
+  if (advance) {
+    token_log[prm->step] = id;
+    prm->step += 1;
+    prm->token = id;
+    prm->pos += 1;
+  }
+}
+
+// Captures one tensor-parallel token step (mode 0: no logits, 1: logits gathered on both ranks,
+// 2: greedy + advance without gathering the logits).
+static bool capture_tp(Engine* E, int mode, cudaGraphExec_t* out) {
+  const NcclApi& nc = nccl();
+  const int dim = (int)E->dim, ffn = (int)E->ffn, kvh = (int)E->kv_dim / 2;
+  const int nq = (int)E->heads / 2, nkv = (int)E->kv_heads / 2;
+  const size_t layer_stride = (size_t)E->max_seq * kvh;
+  cudaStream_t s = E->stream;
+  cudaGraph_t g = nullptr;
+  LE_CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  k_embed<<<1, kThreads, 0, s>>>(E->lm_head, E->d_params, nullptr, E->x);
+  for (uint32_t l = 0; l < E->layers; ++l) {
+    const DevLayer& T = E->tpl[l];
+    const int qkv_rows = T.q.N + T.k.N + T.v.N;
+    k_qkv<2><<<(qkv_rows / 2 + kWarps - 1) / kWarps, kThreads, gemv_smem(dim), s>>>(E->x, T.in_norm, T.q, T.k, T.v,
+                                                                                   E->tp_qkv);
+    const size_t att_smem = (size_t)(64 * 3 + 32 + 256 + E->max_seq) * 4;
+    k_attention<<<nq, kThreads, att_smem, s>>>(E->tp_qkv, E->tp_kc + l * layer_stride, E->tp_vc + l * layer_stride,
+                                               E->rope_cos, E->rope_sin, E->d_params, nq, nkv, E->tp_attn);
+    if (E->tp_rank != 0) cudaMemsetAsync(E->x, 0, (size_t)dim * 4, s);
+    k_proj_residual<1, 2><<<(dim + kWarps - 1) / kWarps, kThreads, gemv_smem(dim), s>>>(E->tp_attn, T.o, E->x);
+    nc.all_reduce(E->x, E->x, (size_t)dim, ncclFloat, ncclSum, E->tp_comm, s);
+    k_gateup<2><<<(T.g.N / 2 + kWarps - 1) / kWarps, kThreads, gemv_smem(dim), s>>>(E->x, T.post_norm, T.g, T.u,
+                                                                                   E->tp_act);
+    if (E->tp_rank != 0) cudaMemsetAsync(E->x, 0, (size_t)dim * 4, s);
+    k_proj_residual<1, 8><<<(dim + kWarps - 1) / kWarps, kThreads, gemv_smem(ffn), s>>>(E->tp_act, T.d, E->x);
+    nc.all_reduce(E->x, E->x, (size_t)dim, ncclFloat, ncclSum, E->tp_comm, s);
+  }
+  if (mode != 0) {
+    const int half = E->tp_lm.N;
+    float* mine = E->logits + (size_t)E->tp_rank * half;
+    k_lmhead<2><<<E->lm_grid, kThreads, gemv_smem(dim), s>>>(E->x, E->final_norm, E->tp_lm, mine, E->tp_part);
+    k_tp_candidate<<<1, 1024, 0, s>>>(E->tp_part, E->lm_grid, E->tp_rank * half, E->tp_cand + 2 * E->tp_rank);
+    nc.all_gather(E->tp_cand + 2 * E->tp_rank, E->tp_cand, 2, ncclInt32, E->tp_comm, s);
+    if (mode == 1) nc.all_gather(mine, E->logits, (size_t)half, ncclFloat, E->tp_comm, s);
+    k_tp_pick<<<1, 32, 0, s>>>(E->tp_cand, E->tp_world, E->am_result, E->d_params, E->token_log, mode == 2 ? 1 : 0);
+  }
+  cudaError_t ce = cudaStreamEndCapture(s, &g);
+  if (ce != cudaSuccess) { E->err = std::string("tp capture: ") + cudaGetErrorString(ce); return false; }
+  ce = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) { E->err = std::string("tp instantiate: ") + cudaGetErrorString(ce); return false; }
+  return true;
+}
+
+static bool init_tp(Engine* E, const ncclUniqueId& id) {
+  const NcclApi& nc = nccl();
+  if (!nc.ok) { E->err = "tensor parallel: NCCL (libnccl.so.2) could not be loaded"; return false; }
+  const int r = E->tp_rank, W = E->tp_world;
+  if (W != 2 || E->heads % 4 || E->kv_heads % 2 || E->dim % 256 || E->ffn % 256 || E->vocab % 32 ||
+      (E->heads / 2) % (E->kv_heads / 2)) {
+    E->err = "tensor parallel: needs 2 ranks and a geometry that halves on 128-blocks";
+    return false;
+  }
+  const int dim = (int)E->dim, ffn = (int)E->ffn, kv = (int)E->kv_dim;
+  // row slices are views of the uploaded matrices
+  auto rows = [](const QMat& M, int n0, int n) {
+    QMat q = M;
+    q.nib = M.nib + (size_t)n0 * (M.K / 2);
+    q.step = M.step + (size_t)n0 * (M.K / 128);
+    q.mn = M.mn + (size_t)n0 * (M.K / 128);
+    q.N = n;
+    return q;
+  };
+  // column halves are copied into a contiguous matrix (2-D copies of the nibble and scale rows)
+  const size_t o_half = (size_t)dim * (dim / 2), d_half = (size_t)dim * (ffn / 2);  // weights per half
+  auto mat_bytes = [](size_t w) { return align_up(w / 2, 256) + 2 * align_up(w / 128 * 2, 256); };
+  const size_t tp_bytes = E->layers * (mat_bytes(o_half) + mat_bytes(d_half));
+  LE_CK(cudaMalloc(&E->tp_arena, tp_bytes));
+  size_t off = 0;
+  auto cols = [&](const QMat& M, int k0, int k) -> QMat {
+    QMat q;
+    q.N = M.N;
+    q.K = k;
+    uint8_t* nib = E->tp_arena + off;
+    off += align_up((size_t)M.N * k / 2, 256);
+    uint16_t* st = reinterpret_cast<uint16_t*>(E->tp_arena + off);
+    off += align_up((size_t)M.N * (k / 128) * 2, 256);
+    uint16_t* mn = reinterpret_cast<uint16_t*>(E->tp_arena + off);
+    off += align_up((size_t)M.N * (k / 128) * 2, 256);
+    cudaMemcpy2DAsync(nib, k / 2, M.nib + k0 / 2, M.K / 2, k / 2, M.N, cudaMemcpyDeviceToDevice, E->stream);
+    cudaMemcpy2DAsync(st, (k / 128) * 2, M.step + k0 / 128, (M.K / 128) * 2, (k / 128) * 2, M.N,
+                      cudaMemcpyDeviceToDevice, E->stream);
+    cudaMemcpy2DAsync(mn, (k / 128) * 2, M.mn + k0 / 128, (M.K / 128) * 2, (k / 128) * 2, M.N,
+                      cudaMemcpyDeviceToDevice, E->stream);
+    q.nib = nib;
+    q.step = st;
+    q.mn = mn;
+    return q;
+  };
+  E->tpl.resize(E->layers);
+  for (uint32_t l = 0; l < E->layers; ++l) {
+    const DevLayer& D = E->L[l];
+    DevLayer& T = E->tpl[l];
+    T.in_norm = D.in_norm;
+    T.post_norm = D.post_norm;
+    T.q = rows(D.q, r * dim / 2, dim / 2);
+    T.k = rows(D.k, r * kv / 2, kv / 2);
+    T.v = rows(D.v, r * kv / 2, kv / 2);
+    T.o = cols(D.o, r * dim / 2, dim / 2);
+    T.g = rows(D.g, r * ffn / 2, ffn / 2);
+    T.u = rows(D.u, r * ffn / 2, ffn / 2);
+    T.d = cols(D.d, r * ffn / 2, ffn / 2);
+  }
+  LE_CK(cudaGetLastError());
+  E->tp_lm = rows(E->lm_head, r * (int)E->vocab / 2, (int)E->vocab / 2);
+  const size_t kv_elems = (size_t)E->layers * E->max_seq * (kv / 2);
+  LE_CK(cudaMalloc(&E->tp_kc, kv_elems * 4));
+  LE_CK(cudaMalloc(&E->tp_vc, kv_elems * 4));
+  LE_CK(cudaMemsetAsync(E->tp_kc, 0, kv_elems * 4, E->stream));
+  LE_CK(cudaMemsetAsync(E->tp_vc, 0, kv_elems * 4, E->stream));
+  LE_CK(cudaMalloc(&E->tp_qkv, (size_t)(dim + 2 * kv) / 2 * 4));
+  LE_CK(cudaMalloc(&E->tp_attn, (size_t)dim / 2 * 4));
+  LE_CK(cudaMalloc(&E->tp_act, (size_t)ffn / 2 * 4));
+  LE_CK(cudaMalloc(&E->tp_part, (size_t)E->lm_grid * sizeof(ArgmaxPart)));
+  LE_CK(cudaMalloc(&E->tp_cand, (size_t)W * 2 * 4));
+  LE_CK(cudaStreamSynchronize(E->stream));
+  LE_NCCL(nc.comm_init_rank(&E->tp_comm, W, id, r));
+  for (int m = 0; m < 3; ++m)
+    if (!capture_tp(E, m, &E->tp_g[m])) return false;
+  return true;
+}
+
+static void destroy_tp(Engine* E) {
+  for (auto& g : E->tp_g)
+    if (g) { cudaGraphExecDestroy(g); g = nullptr; }  // graphs holding NCCL calls go first
+  if (E->tp_comm) { nccl().comm_destroy(E->tp_comm); E->tp_comm = nullptr; }
+  void* p[] = {E->tp_arena, E->tp_kc, E->tp_vc, E->tp_qkv, E->tp_attn, E->tp_act, E->tp_part, E->tp_cand};
+  for (void* q : p) if (q) cudaFree(q);
+  E->tp_arena = nullptr;
+  E->tp_kc = E->tp_vc = E->tp_qkv = E->tp_attn = E->tp_act = nullptr;
+  E->tp_part = nullptr;
+  E->tp_cand = nullptr;
 }
 
 static bool queue_params(Engine* E, int32_t token, int32_t pos) {
@@ -1098,7 +1511,9 @@ static bool forward_token(Engine* E, int32_t token, size_t pos, bool logits) {
   if (pos >= (size_t)E->max_seq) return true;  // silent no-op, src/llama_engine.cpp:936
   if (token < 0 || token >= (int32_t)E->vocab) token = 0;  // :937
   if (!queue_params(E, token, (int32_t)pos)) return false;
-  if (E->persist) {
+  if (E->tp_world > 1) {
+    LE_CK(cudaGraphLaunch(E->tp_g[logits ? 1 : 0], E->stream));
+  } else if (E->persist) {
     if (!launch_persistent(E, 1, logits)) return false;
   } else {
     LE_CK(cudaGraphLaunch(E->g_fwd[logits ? 1 : 0], E->stream));
@@ -1304,7 +1719,10 @@ LE_API int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_tok
   if (first_token < 0 || first_token >= (int32_t)E->vocab) first_token = 0;
   if (!queue_params(E, first_token, (int32_t)start_pos)) return -1;
   E->last_pos = (int32_t)(start_pos + n_steps - 1);
-  if (E->persist) {
+  if (E->tp_world > 1) {
+    for (int32_t i = 0; i < n_steps; ++i)
+      if (cudaGraphLaunch(E->tp_g[2], E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
+  } else if (E->persist) {
     if (!launch_persistent(E, n_steps, true)) return -1;
   } else {
     for (int32_t i = 0; i < n_steps; ++i)
@@ -1335,6 +1753,15 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
   for (int i = 0; i < n; ++i) {
     if (slots[i] < 0 || slots[i] >= E->max_batch) { E->err = "forward_batch: slot out of range"; return -1; }
     if (positions[i] < 0 || positions[i] >= E->max_seq) { E->err = "forward_batch: position out of range"; return -1; }
+  }
+  {  // two rows for the same (slot, position) would both append its k / v: rejected
+    std::vector<std::pair<int32_t, int32_t>> sp(n);
+    for (int i = 0; i < n; ++i) sp[i] = {slots[i], positions[i]};
+    std::sort(sp.begin(), sp.end());
+    if (std::adjacent_find(sp.begin(), sp.end()) != sp.end()) {
+      E->err = "forward_batch: two rows for the same (slot, position)";
+      return -1;
+    }
   }
   DeviceGuard dg(E->device);
   if (E->tc) {
@@ -1392,9 +1819,106 @@ LE_API int llama_engine_trace(llama_engine_t engine, int enable, unsigned long l
   return (int)std::min<size_t>((size_t)E->p_grid * kTraceCap, (size_t)std::max(0, max_entries));
 }
 
+LE_API int llama_engine_rope_table(float factor, float low_freq_factor, float high_freq_factor,
+                                   int original_max_position, int n_pos, float* cos_out, float* sin_out) {
+  if (!cos_out || !sin_out || n_pos < 1 || n_pos > LE_MAX_SEQ_LEN) return -1;
+  if (factor > 0.0f && !(high_freq_factor > low_freq_factor && low_freq_factor > 0.0f && original_max_position > 0))
+    return -1;
+  RopeScaling rs{factor, low_freq_factor, high_freq_factor, original_max_position};
+  std::vector<float> cs, sn;
+  build_rope_table(rs, n_pos, cs, sn);
+  std::memcpy(cos_out, cs.data(), cs.size() * 4);
+  std::memcpy(sin_out, sn.data(), sn.size() * 4);
+  return 0;
+}
+
+LE_API int llama_engine_set_rope_scaling(llama_engine_t engine, float factor, float low_freq_factor,
+                                         float high_freq_factor, int original_max_position) {
+  if (!engine) return -1;
+  Engine* E = H(engine);
+  if (factor > 0.0f && !(high_freq_factor > low_freq_factor && low_freq_factor > 0.0f && original_max_position > 0)) {
+    E->err = "set_rope_scaling: bad parameters";
+    return -1;
+  }
+  DeviceGuard dg(E->device);
+  RopeScaling rs{factor, low_freq_factor, high_freq_factor, original_max_position};
+  std::vector<float> cs, sn;
+  build_rope_table(rs, LE_MAX_SEQ_LEN, cs, sn);
+  // queued steps read the table: replace it only after they are done
+  cudaError_t ce = cudaStreamSynchronize(E->stream);
+  if (ce == cudaSuccess) ce = cudaMemcpy(E->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMemcpy(E->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
+  return 0;
+}
+
+LE_API int llama_engine_check_schedule(int layers, int dim, int ffn_dim, int vocab_size, int num_heads,
+                                       int num_kv_heads, int grid, char* err, int err_len) {
+  std::string msg;
+  bool ok = layers > 0 && dim == 2048 && ffn_dim % 2048 == 0 && ffn_dim > 0 && ffn_dim <= 8192 && vocab_size > 0 &&
+            vocab_size % 16 == 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0 &&
+            dim / num_heads == LE_HEAD_DIM && grid > 0 && grid <= 1024;
+  if (!ok) msg = "unsupported geometry or grid";
+  if (ok) {
+    PGeom geo{layers, dim, ffn_dim, vocab_size, num_heads, num_kv_heads};
+    PSchedule P;
+    ok = build_schedule(geo, grid, P, msg) && check_schedule(geo, grid, P, msg);
+  }
+  if (err && err_len > 0) {
+    std::strncpy(err, msg.c_str(), (size_t)err_len - 1);
+    err[err_len - 1] = '\0';
+  }
+  return ok ? 0 : -1;
+}
+
+LE_API int llama_engine_debug_waits(llama_engine_t engine, unsigned long long wait_ns, int expire_code) {
+  if (!engine) return -1;
+  Engine* E = H(engine);
+  DeviceGuard dg(E->device);
+  if (cudaStreamSynchronize(E->stream) != cudaSuccess) return -1;
+  const unsigned long long ns = wait_ns ? wait_ns : kWaitNs;
+  E->pargs.wait_ns = ns;
+  E->pargs.expire_where = expire_code;
+  E->tc_wait_ns = ns;
+  E->tc_expire = expire_code != 0 ? 1 : 0;
+  // captured batched steps hold the old GEMM arguments
+  for (auto& g : E->tc_graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  E->tc_graphs.clear();
+  if (expire_code == 0) {  // clear a recorded timeout so the engine can run again
+    if (E->persist && cudaMemsetAsync(&E->d_ctrl->error, 0, 2 * sizeof(uint32_t), E->stream) != cudaSuccess) return -1;
+    if (E->tc && cudaMemsetAsync(E->tc_err, 0, sizeof(uint32_t), E->stream) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(E->stream) != cudaSuccess) return -1;
+    E->h_err[0] = E->h_err[1] = E->h_err[2] = 0;
+    E->tc_dirty = true;
+  }
+  return 0;
+}
+
 LE_API int llama_engine_decode_path(llama_engine_t engine) {
   if (!engine) return -1;
-  return H(engine)->persist ? 1 : 0;
+  return H(engine)->tp_world > 1 ? 2 : H(engine)->persist ? 1 : 0;
+}
+
+LE_API int llama_engine_tp_unique_id(void* out_id, int len) {
+  if (!out_id || len < (int)sizeof(ncclUniqueId)) return -1;
+  const NcclApi& nc = nccl();
+  if (!nc.ok) return -1;
+  ncclUniqueId id;
+  if (nc.get_unique_id(&id) != ncclSuccess) return -1;
+  std::memcpy(out_id, &id, sizeof(id));
+  return 0;
+}
+
+LE_API llama_engine_t llama_engine_create_tp(const char* model_path, int device, int rank, int world,
+                                             const void* unique_id, int max_seq_len) {
+  if (!unique_id || world != 2 || rank < 0 || rank >= world) {
+    set_create_error("create_tp: needs world = 2, 0 <= rank < world and the rank-0 unique id");
+    return nullptr;
+  }
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  return create(model_path, device, 1, max_seq_len, rank, world, &id);
 }
 
 LE_API int llama_engine_batch_path(llama_engine_t engine) {
@@ -1673,6 +2197,7 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     A.out = y;
     A.ldo = N;
     A.error = err;
+    A.wait_ns = kWaitNs;
     // diagnostics: $LLAMA_B128_GEMM_TRACE names a file that receives CTA 0's pipeline events
     const char* trace_path = getenv("LLAMA_B128_GEMM_TRACE");
     unsigned long long* trace = nullptr;

@@ -21,8 +21,9 @@
 // exactly one writer per phase, and the dependency chain guarantees that no element is
 // overwritten before every reader of its previous value has read it.
 //
-// All waits are bounded in time; on timeout a global error word is set, every later wait returns
-// at once and the launch drains, so the host sees an error, never a hang.
+// All waits are bounded in time (PArgs::wait_ns); on timeout a global error word is set, every
+// later wait returns at once, the CTA issues no further copies and waits for the ones in flight,
+// and the launch drains, so the host sees an error, never a hang.
 //
 // Record format (built at load time from the LLM4S128 matrices): 16 rows x 16 blocks
 // (2048 columns) of one matrix, 17408 bytes:
@@ -45,7 +46,7 @@ constexpr int kMiscFloats = 2304;          // attention scratch (q, k, v, reduct
                                            // or the row partials of a segment's work units
 constexpr int kMaxUnits = kMiscFloats / 16;  // work units per segment
 constexpr int kImageBytes = 32768 + 1024;  // digit fragments for K <= 8192, or attention scores
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every wait
+constexpr unsigned long long kWaitNs = 2000000000ull;  // default bound on every wait (2 s)
 constexpr unsigned kPollNs = 20;  // pause between polls of tagged activations
 constexpr int kTraceCap = 1024;
 
@@ -90,7 +91,8 @@ struct PCtrl {
   uint32_t error;      // nonzero after a wait timed out
   uint32_t err_where;  // code of the first wait that timed out
   uint32_t lm_ctr;     // CTAs done with the lm_head (monotonic, generate-mode token feedback)
-  uint32_t pad[2];
+  uint32_t never;      // never written: the target of the test-only expiring wait
+  uint32_t pad;
   unsigned long long key[3];  // packed greedy candidates, by lm step modulo 3
 };
 
@@ -115,9 +117,11 @@ struct PArgs {
   int32_t* token_log;
   int32_t* am_result;
   unsigned long long lm_rec_base;  // record offset of lm_head tile 0 (embedding lookup)
+  unsigned long long wait_ns;      // bound on every wait
   int layers, dim, ffn, vocab, heads, kv_heads, max_seq;
   int n_lm_ctas;
   int n_tokens, do_logits;
+  int expire_where;  // test only: nonzero makes CTA 0 wait on PCtrl::never with this code
   unsigned long long* trace;  // optional: per CTA kTraceCap (time, tag) pairs, first token only
 };
 
@@ -217,7 +221,7 @@ __device__ bool wait_counter(const PArgs& A, const uint32_t* p, uint32_t target,
   while (true) {
     if (failed(A)) return false;
     if (reached(ld_acquire(p), target)) return true;
-    if (gtimer() - t0 > kWaitNs) { fail(A, where); return false; }
+    if (gtimer() - t0 > A.wait_ns) { fail(A, where); return false; }
     __nanosleep(40);
   }
 }
@@ -228,20 +232,31 @@ __device__ bool wait_mbar(const PArgs& A, uint32_t bar, uint32_t parity, uint32_
   while (true) {
     if (mbar_try(bar, parity)) return true;
     if (failed(A)) return false;
-    if (gtimer() - t0 > kWaitNs) { fail(A, where); return false; }
+    if (gtimer() - t0 > A.wait_ns) { fail(A, where); return false; }
+  }
+}
+
+// Drain wait for a copy this CTA issued: bounded, but not cut short by another wait's failure,
+// so that no copy is still in flight into shared memory when the CTA exits.
+__device__ void wait_mbar_drain(const PArgs& A, uint32_t bar, uint32_t parity, uint32_t where) {
+  if (mbar_try(bar, parity)) return;
+  const unsigned long long t0 = gtimer();
+  while (!mbar_try(bar, parity)) {
+    if (gtimer() - t0 > A.wait_ns) { fail(A, where); return; }
   }
 }
 
 // Waits until ring slot `slot` has been issued record q (bounded).
-__device__ __forceinline__ void wait_slot(const PArgs& A, volatile int* slot_rec, uint32_t slot, uint32_t q,
+__device__ __forceinline__ bool wait_slot(const PArgs& A, volatile int* slot_rec, uint32_t slot, uint32_t q,
                                           uint32_t where) {
-  if (slot_rec[slot] == (int)q) return;
+  if (slot_rec[slot] == (int)q) return true;
   const unsigned long long t0 = gtimer();
   while (slot_rec[slot] != (int)q) {
-    if (failed(A)) return;
-    if (gtimer() - t0 > kWaitNs) { fail(A, where); return; }
+    if (failed(A)) return false;
+    if (gtimer() - t0 > A.wait_ns) { fail(A, where); return false; }
     __nanosleep(20);
   }
+  return true;
 }
 
 // Loads N2 pairs of tagged words starting at p until every tag equals `tag` (bounded).
@@ -263,7 +278,7 @@ __device__ __forceinline__ void ld_tagged(const PArgs& A, const unsigned long lo
 #pragma unroll
       for (int i = 0; i < 2 * N2; ++i) ok &= tag_of(w[i]) == tag;
       if (ok || failed(A)) break;
-      if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+      if (gtimer() - t0 > A.wait_ns) { fail(A, where); break; }
       __nanosleep(kPollNs);
     }
   }
@@ -293,7 +308,7 @@ __device__ __forceinline__ void ld_tagged2x(const PArgs& A, const unsigned long 
     while (true) {
       load();
       if (all_ok() || failed(A)) break;
-      if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+      if (gtimer() - t0 > A.wait_ns) { fail(A, where); break; }
       __nanosleep(kPollNs);
     }
   }
@@ -311,7 +326,7 @@ __device__ __forceinline__ float ld_tagged1(const PArgs& A, const unsigned long 
     while (true) {
       w = ld_tag(p);
       if (tag_of(w) == tag || failed(A)) break;
-      if (gtimer() - t0 > kWaitNs) { fail(A, where); break; }
+      if (gtimer() - t0 > A.wait_ns) { fail(A, where); break; }
       __nanosleep(kPollNs);
     }
   }
@@ -740,6 +755,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   // its slot holds q: only then does the slot's mbarrier parity refer unambiguously to q (a
   // consumer that ran two uses ahead would otherwise see an older phase of the same parity).
   __shared__ volatile int s_slot_rec[kRingSlots];
+  __shared__ volatile int s_fail;  // a ring wait of this CTA gave up: no more copies are issued
 
   const PCtaSched cs = A.sched[blockIdx.x];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -762,6 +778,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   for (uint32_t i = tid; i < cs.nitem; i += kPThreads) s_items[i] = A.items[cs.item_off + i];
   for (uint32_t i = tid; i < cs.nseg; i += kPThreads) s_segs[i] = A.segs[cs.seg_off + i];
   if (tid == 0) {
+    s_fail = 0;
     for (int s = 0; s < kRingSlots; ++s) {
       mbar_init(full0 + 8 * s, 1);
       s_slot_rec[s] = -1;
@@ -772,6 +789,9 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   __syncthreads();
   if (tid == 0)
     for (uint32_t q = 0; q < total && q < (uint32_t)kRingSlots; ++q) issue(q);
+  // test only: a wait that no one will satisfy runs out (the error path of every wait)
+  if (A.expire_where != 0 && blockIdx.x == 0 && tid == 0)
+    wait_counter(A, &A.ctrl->never, 1u, (uint32_t)A.expire_where);
 
   const int cw = warp;
   Stage S;
@@ -794,7 +814,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
       if (tid == 0) {
         wait_counter(A, &A.ctrl->lm_ctr, (lm_seq + (uint32_t)tok) * (uint32_t)A.n_lm_ctas, 3);
         const unsigned long long k = atomicAdd(&A.ctrl->key[(lm_seq + tok - 1) % 3], 0ull);
-        s_token = k == 0ull ? 0 : (int)(~(uint32_t)(k & 0xFFFFFFFFull));
+        const int t = k == 0ull ? 0 : (int)(~(uint32_t)(k & 0xFFFFFFFFull));
+        s_token = (unsigned)t < (unsigned)A.vocab ? t : 0;  // (a failed step leaves no valid key)
       }
       consumer_sync();
       token = s_token;
@@ -885,8 +906,14 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
         const uint32_t q = q0 + (uint32_t)rl;
         const uint32_t slot = q % kRingSlots;
         const long long w0 = kTrace ? clock64() : 0;
-        wait_slot(A, s_slot_rec, slot, q, 650 + sg.kind);
-        wait_mbar(A, full0 + 8 * slot, (q / kRingSlots) & 1, 600 + sg.kind);
+        // after a failed wait (error set) the unit still runs, on whatever the slot holds, and this
+        // CTA issues no further copies
+        const bool landed = wait_slot(A, s_slot_rec, slot, q, 650 + sg.kind) &&
+                            wait_mbar(A, full0 + 8 * slot, (q / kRingSlots) & 1, 600 + sg.kind);
+        if (!landed) {
+          s_fail = 1;
+          __threadfence_block();  // seen by the record's last releaser, after its counter add
+        }
         if (kTrace) wait_cycles += (unsigned long long)(clock64() - w0);
         if (fine) trace_mark<kTrace>(A, ntr, tok, tag | 0x70000u);
         float p0, p1;
@@ -903,7 +930,9 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
             last = atomicAdd(&s_slot_cnt[slot], 1) == SP - 1;
             if (last) atomicExch(&s_slot_cnt[slot], 0);  // atomic: ordered with the next record's adds
           }
-          if (last && q + kRingSlots < total) issue(q + kRingSlots);
+          // only while every wait of this CTA has succeeded: then record q has landed and been
+          // read, so the slot holds at most one copy in flight
+          if (last && q + kRingSlots < total && !s_fail) issue(q + kRingSlots);
         }
         if (fine) trace_mark<kTrace>(A, ntr, tok, tag | 0x90000u);
       }
@@ -975,9 +1004,10 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   __syncthreads();
   if (tid == 0) {
     // every issued copy has been consumed, unless a wait gave up: make sure none is in flight
-    for (uint32_t sl = 0; sl < (uint32_t)kRingSlots && sl < total; ++sl) {
-      const uint32_t qlast = ((total - 1 - sl) / kRingSlots) * kRingSlots + sl;
-      wait_mbar(A, full0 + 8 * sl, (qlast / kRingSlots) & 1, 2);
+    // (the last copy issued into each slot has landed; earlier ones were waited for before it)
+    for (int sl = 0; sl < kRingSlots; ++sl) {
+      const int qlast = s_slot_rec[sl];
+      if (qlast >= 0) wait_mbar_drain(A, full0 + 8 * sl, ((uint32_t)qlast / kRingSlots) & 1, 2);
     }
     __threadfence();
     const uint32_t prev = atomicAdd(&A.ctrl->done_ctas, 1u);

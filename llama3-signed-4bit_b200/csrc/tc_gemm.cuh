@@ -86,6 +86,8 @@ struct Args {
   size_t split_stride;
   uint32_t* error;       // set to a nonzero code on a wait timeout
   unsigned long long* trace;  // optional: CTA 0's pipeline events, [kTraceEvents][kTraceBlocks]
+  unsigned long long wait_ns;  // bound on every wait
+  int expire;            // test only: nonzero makes the MMA issuer wait on a barrier nothing completes
 };
 
 // Pipeline trace (diagnostics): globaltimer stamps of CTA 0 for its first kTraceBlocks blocks.
@@ -221,10 +223,24 @@ __device__ __forceinline__ bool wait_bar(const Args& A, volatile uint32_t* abort
   while (true) {
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (gtimer() - t0 > kWaitNs) {
+    if (gtimer() - t0 > A.wait_ns) {
       *abort_flag = 1u;
       atomicCAS(A.error, 0u, where);
       return false;
+    }
+  }
+}
+// Drain wait for this CTA's own copies or MMAs: bounded, but not cut short by another role's
+// failure, so that nothing is still in flight into shared or tensor memory when the CTA exits.
+__device__ __forceinline__ void wait_bar_drain(const Args& A, volatile uint32_t* abort_flag, uint32_t bar,
+                                               uint32_t parity, uint32_t where) {
+  if (mbar_try(bar, parity)) return;
+  const unsigned long long t0 = gtimer();
+  while (!mbar_try(bar, parity)) {
+    if (gtimer() - t0 > A.wait_ns) {
+      *abort_flag = 1u;
+      atomicCAS(A.error, 0u, where);
+      return;
     }
   }
 }
@@ -349,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       const int issued = g;
       for (int s = 0; s < kStages && s < issued; ++s) {
         const int last = issued - 1 - ((issued - 1 - s) % kStages);  // last fill of stage s
-        wait_bar(A, &s_abort, bar_full(S, s), (last / kStages) & 1, 2);
+        wait_bar_drain(A, &s_abort, bar_full(S, s), (last / kStages) & 1, 2);
       }
     }
   } else if (warp == 1) {
@@ -365,6 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       const int nblk = cta_blocks(A, n_units);
       const uint32_t desc_hi = (uint32_t)(sw128_desc(0) >> 32);
       const uint32_t desc_lo0 = (uint32_t)sw128_desc(S.base);
+      // test only: phase 0 of the final barrier completes only after the last commit below, so
+      // this wait runs out and the launch takes its error path
+      if (A.expire) wait_bar(A, &s_abort, bar_final(S), 0, 13);
       for (int g = 0; g < nblk; ++g) {
         const int s = g % kStages, n = g / kStages;
         const int ba = g % kBufsA, na = g / kBufsA, bd = g % kBufsD, nd = g / kBufsD;
@@ -392,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       }
       // all issued MMAs complete before the tensor memory is released
       tc_commit(bar_final(S));
-      wait_bar(A, &s_abort, bar_final(S), 0, 6);
+      wait_bar_drain(A, &s_abort, bar_final(S), 0, 6);
     }
   } else if (warp == 2) {
     // no role

@@ -97,9 +97,31 @@ class LlamaEngineBindings:
         lib.llama_b128_gemm.restype = ctypes.c_int
         lib.llama_b128_argmax_noalloc.argtypes = [_P, ctypes.c_int, _P, _P]
         lib.llama_b128_argmax_noalloc.restype = ctypes.c_int
+        lib.llama_engine_set_rope_scaling.argtypes = [_P, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int]
+        lib.llama_engine_set_rope_scaling.restype = ctypes.c_int
+        lib.llama_engine_rope_table.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                                ctypes.c_int, _FP, _FP]
+        lib.llama_engine_rope_table.restype = ctypes.c_int
+        lib.llama_engine_tp_unique_id.argtypes = [_P, ctypes.c_int]
+        lib.llama_engine_tp_unique_id.restype = ctypes.c_int
+        lib.llama_engine_create_tp.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
+                                               ctypes.c_int]
+        lib.llama_engine_create_tp.restype = _P
+        lib.llama_engine_check_schedule.argtypes = [ctypes.c_int] * 7 + [ctypes.c_char_p, ctypes.c_int]
+        lib.llama_engine_check_schedule.restype = ctypes.c_int
+        lib.llama_engine_debug_waits.argtypes = [_P, ctypes.c_ulonglong, ctypes.c_int]
+        lib.llama_engine_debug_waits.restype = ctypes.c_int
 
     def last_error(self, handle=None) -> str:
         return self.lib.llama_engine_last_error(handle).decode(errors="replace")
+
+
+def tp_unique_id(bindings: LlamaEngineBindings) -> bytes:
+    """The NCCL unique id that rank 0 of a tensor-parallel pair makes and shares."""
+    buf = ctypes.create_string_buffer(128)
+    if bindings.lib.llama_engine_tp_unique_id(buf, 128) != 0:
+        raise RuntimeError("NCCL unique id: NCCL could not be loaded")
+    return buf.raw
 
 
 class TokenizerWrapper:
@@ -146,10 +168,15 @@ class LlamaEngine:
     """
 
     def __init__(self, model_path: str, bindings: LlamaEngineBindings, device: int | None = None,
-                 max_batch: int = 1, max_seq_len: int = 0):
+                 max_batch: int = 1, max_seq_len: int = 0, tp_rank: int | None = None, tp_world: int = 1,
+                 tp_unique_id: bytes | None = None):
         self.bindings = bindings
         lib = bindings.lib
-        if device is None and max_batch == 1 and max_seq_len == 0:
+        if tp_rank is not None:  # 2-way tensor-parallel engine (llama_engine_create_tp)
+            uid = ctypes.create_string_buffer(tp_unique_id, 128)
+            self.handle = lib.llama_engine_create_tp(model_path.encode("utf-8"), device or 0, tp_rank, tp_world,
+                                                     uid, max_seq_len)
+        elif device is None and max_batch == 1 and max_seq_len == 0:
             self.handle = lib.llama_engine_create(model_path.encode("utf-8"))
         else:
             self.handle = lib.llama_engine_create_ex(model_path.encode("utf-8"), device or 0, max_batch,
@@ -242,9 +269,17 @@ class LlamaEngine:
                     "score_tokens")
         return lp[:n - 1], gr[:n - 1].astype(bool)
 
+    def set_rope_scaling(self, factor: float = 32.0, low_freq_factor: float = 1.0, high_freq_factor: float = 4.0,
+                         original_max_position: int = 8192) -> None:
+        """Opt-in llama3 RoPE scaling (factor <= 0 restores the reference's unscaled table)."""
+        self._check(self.bindings.lib.llama_engine_set_rope_scaling(self.handle, factor, low_freq_factor,
+                                                                     high_freq_factor, original_max_position),
+                    "set_rope_scaling")
+
     @property
     def decode_path(self) -> str:
-        return {1: "persistent", 0: "kernel-chain"}.get(self.bindings.lib.llama_engine_decode_path(self.handle), "?")
+        return {1: "persistent", 0: "kernel-chain", 2: "tensor-parallel"}.get(
+            self.bindings.lib.llama_engine_decode_path(self.handle), "?")
 
     @property
     def batch_path(self) -> str:

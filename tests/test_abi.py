@@ -91,3 +91,24 @@ def test_geometry_checks(bindings, pkg, tmp_path):
     p = pkg.model_file.write_model(tmp_path / "hd128.bin", shape, seed=1)  # head_dim 128
     assert not bindings.lib.llama_engine_create(str(p).encode())
     assert b"head_dim" in bindings.lib.llama_engine_last_error(None)
+
+
+@pytest.mark.parametrize("geometry", [
+    (16, 2048, 8192, 128256, 32, 8),   # LLaMA-3.2-1B
+    (2, 2048, 2048, 4096, 32, 8),      # the small test model
+    (2, 2048, 4096, 4096, 32, 8),
+])
+@pytest.mark.parametrize("grid", [148, 160])
+def test_persistent_schedule_is_complete(bindings, geometry, grid):
+    """The persistent kernel's schedule, read the way the kernel reads it: every tile of every
+    phase on exactly one CTA with its own records, records in stream order, heads once a layer."""
+    err = ctypes.create_string_buffer(256)
+    rc = bindings.lib.llama_engine_check_schedule(*geometry, grid, err, 256)
+    assert rc == 0, err.value.decode()
+
+
+def test_persistent_schedule_rejects_bad_geometry(bindings):
+    err = ctypes.create_string_buffer(256)
+    assert bindings.lib.llama_engine_check_schedule(16, 4096, 8192, 128256, 32, 8, 148, err, 256) == -1
+    assert err.value
+    assert bindings.lib.llama_engine_check_schedule(16, 2048, 8192, 128256, 32, 8, 0, None, 0) == -1

@@ -401,3 +401,33 @@ def test_temperature_sampling_full_vocab(pkg, bindings, full_model):
             assert sid == _reference_walk(probs, top_p, libc.rand()), (temp, top_p, seed)
     finally:
         eng.close()
+
+
+def test_llama3_rope_scaling_changes_only_the_table(pkg, bindings, small_model, oracle_lib):
+    """The opt-in llama3 RoPE scaling replaces the table and nothing else: at position 0 (cos 1,
+    sin 0 in both tables) the logits are bit-identical; later positions differ; restoring the
+    reference's table gives the oracle's logits again."""
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    o = oracle_lib.orc_create(str(small_model).encode())
+    try:
+        vocab = eng.vocab_size
+        ids = [17, 99, 5, 4000, 23]
+        eng.forward_token(ids[0], 0, True)
+        l0 = eng.get_logits()
+        eng.set_rope_scaling(32.0, 1.0, 4.0, 8192)
+        eng.forward_token(ids[0], 0, True)
+        assert np.array_equal(eng.get_logits(), l0)
+        for p, t in enumerate(ids[1:], start=1):
+            eng.forward_token(t, p, True)
+        scaled = eng.get_logits()
+        eng.set_rope_scaling(0.0, 1.0, 4.0, 8192)
+        for p, t in enumerate(ids):
+            eng.forward_token(t, p, True)
+            oracle_lib.orc_forward_token(o, t, p, 1)
+        ref = _oracle_logits(oracle_lib, o, vocab)
+        assert rel_max_err(eng.get_logits(), ref) <= LOGIT_RTOL
+        assert rel_max_err(scaled, ref) > 1e-4  # the scaled table does change the result
+        assert eng.bindings.lib.llama_engine_set_rope_scaling(eng.handle, 32.0, 4.0, 1.0, 8192) == -1
+    finally:
+        oracle_lib.orc_free(o)
+        eng.close()
