@@ -6,7 +6,8 @@ fixtures that the reference engine itself produced (tests/golden/make_golden.py)
 * config 2 — 64 sequences (512-id prompts) fed through forward_batch, then 32 batched greedy
   decode steps of all 64 rows; each step's ids come from the reference run (teacher forcing, so a
   near-tie cannot derail the comparison), and every row's greedy id, top-16 logits and 128 sampled
-  logits are checked against it.
+  logits are checked against it.  A greedy id may differ only where the reference's own top-2
+  margin is below 1e-4 and the engine chose the reference's runner-up (reported as a tie).
 
 Tolerance: max |l - l_ref| <= 1e-3 * max |l_ref| per row ("1e-3 relative").
 """
@@ -20,6 +21,7 @@ from conftest import GOLDEN
 pytestmark = pytest.mark.gpu
 
 LOGIT_RTOL = 1e-3
+TIE_MARGIN = 1e-4  # a reference top-2 margin below this counts as a tie for the greedy id
 
 
 @pytest.fixture(scope="module")
@@ -73,6 +75,7 @@ def test_config2_batched_decode_vs_reference(pkg, bindings, full_model):
                               [s for p in ps for s in slots], False)
         toks = [int(prompts[s, P - 1]) for s in slots]
         worst = 0.0
+        ties = []
         for step in range(steps):
             pos = P - 1 + step
             eng.forward_batch(toks, [pos] * B, slots, True)
@@ -84,9 +87,14 @@ def test_config2_batched_decode_vs_reference(pkg, bindings, full_model):
                 e2 = float(np.abs(lg[g["top_ids"][s, step]] - g["top_vals"][s, step]).max()) / scale
                 worst = max(worst, e1, e2)
                 assert e1 <= LOGIT_RTOL and e2 <= LOGIT_RTOL, f"step {step} seq {s}: {e1:.3e} {e2:.3e}"
-                assert am[s] == int(ref_tok[s, step]), \
-                    f"step {step} seq {s}: greedy id (top-2 margin {float(g['margins'][s, step]):.3g})"
+                if am[s] != int(ref_tok[s, step]):
+                    # a tie within the rounding of a different summation order: the reference's own
+                    # top-2 margin is below 1e-4 and the engine picked its runner-up
+                    margin = float(g["margins"][s, step])
+                    assert margin < TIE_MARGIN and am[s] == int(g["top_ids"][s, step, 1]), \
+                        f"step {step} seq {s}: greedy id {am[s]} vs {int(ref_tok[s, step])} (top-2 margin {margin:.3g})"
+                    ties.append((step, s, margin))
             toks = [int(t) for t in ref_tok[:, step]]
-        print(f"config 2: worst rel err over {B} x {steps} rows {worst:.3e}")
+        print(f"config 2: worst rel err over {B} x {steps} rows {worst:.3e}; near-ties taken the other way: {ties}")
     finally:
         eng.close()
