@@ -180,13 +180,14 @@ __global__ void __launch_bounds__(128, 4)
       o[h][0] *= ah;
       o[h][1] *= ah;
     }
-    // rows at or past P hold a substitute row (see load_tile): skip them rather than weighting
-    // them by 0, so a non-finite value left in the cache cannot reach the sum (warp-uniform)
-    const int jn = min(8, P - (kt * 32 + 8 * warp));
+    // rows at or past P hold a substitute row (see load_tile): their values are replaced by
+    // zero rather than weighted by zero, so a non-finite value left in the cache cannot reach
+    // the sum (a select, no branch in the unrolled loop)
+    const int jn = P - (kt * 32 + 8 * warp);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      if (j >= jn) break;
-      const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][8 * warp + j][2 * lane]);
+      float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][8 * warp + j][2 * lane]);
+      if (j >= jn) v2 = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const float pj = __shfl_sync(0xffffffffu, pe, 4 * j + h);

@@ -28,6 +28,7 @@
 #include "mma_gemv.cuh"
 #include "persistent.cuh"
 #include "tc_gemm.cuh"
+#include "attn_tc.cuh"
 #include "llama_engine.h"
 #include <nccl.h>
 
@@ -810,6 +811,7 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMemsetAsync(E->tc_err, 0, 16, E->stream));
   LE_CK(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
   LE_CK(cudaFuncSetAttribute(k_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+  LE_CK(cudaFuncSetAttribute(k_attn_prefill_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
   int per_sm = 0;
   LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm, tc::kThreads, kSmemBytes));
   if (per_sm < 1) {
@@ -931,8 +933,9 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
       launch_pdl(k_rope_append, dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), dim3(256), 0, s, E->t_qkv, sq, qkv_stride,
                  dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
     if (prefill_p0 >= 0) {
-      launch_pdl(k_attn_prefill_tc, dim3(E->kv_heads, (n + 15) / 16), dim3(128), 0, s, E->t_q, dim, kc, vc, kvd,
-                 prefill_p0, n, E->t_attn);
+      launch_pdl(k_attn_prefill_tc5, dim3(E->kv_heads, (n + attn::kQ - 1) / attn::kQ), dim3(128),
+                 (size_t)attn::kSmemBytes, s, E->t_q, dim, kc, vc, kvd, prefill_p0, n, E->t_attn, E->tc_err,
+                 E->tc_wait_ns);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
       // without position splits the attention kernel writes the o-proj input image itself

@@ -695,24 +695,32 @@ __device__ void attention_head(const PArgs& A, int l, int h, int pos, uint32_t s
     m = mn;
   }
   if (fine) trace_mark<kTrace>(A, ntr, tok, ftag | 0xB0000u);
-  if (lane == 0) {
-    wm[w] = m;
-    wl[w] = lsum;
-  }
-  reinterpret_cast<float2*>(wacc + w * 64)[lane] = acc;
+  // merge of the 16 warps: every warp rescales its own (sum, output row) to the common maximum
+  // in registers, then 64 threads add the 16 rescaled rows as a tree
+  if (lane == 0) wm[w] = m;
+  consumer_sync();
+  float M = wm[0];
+#pragma unroll
+  for (int v = 1; v < kPConsumerWarps; ++v) M = fmaxf(M, wm[v]);
+  const float f = m == -INFINITY ? 0.0f : expf(m - M);  // a warp without positions adds nothing
+  reinterpret_cast<float2*>(wacc + w * 64)[lane] = make_float2(acc.x * f, acc.y * f);
+  if (lane == 0) wl[w] = lsum * f;
   consumer_sync();
   if (tid < 64) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int v = 0; v < kPConsumerWarps; ++v) M = fmaxf(M, wm[v]);
-    float L = 0.0f, o = 0.0f;
+    float o[kPConsumerWarps], L[kPConsumerWarps];
 #pragma unroll
     for (int v = 0; v < kPConsumerWarps; ++v) {
-      const float f = wm[v] == -INFINITY ? 0.0f : expf(wm[v] - M);
-      L = fmaf(wl[v], f, L);
-      o = fmaf(wacc[v * 64 + tid], f, o);
+      o[v] = wacc[v * 64 + tid];
+      L[v] = wl[v];
     }
-    st_tag(A.attn + h * LE_HEAD_DIM + tid, o / L, phase_tag(s, A.layers, l, TG_ATTN));
+#pragma unroll
+    for (int st = kPConsumerWarps / 2; st > 0; st >>= 1)
+#pragma unroll
+      for (int v = 0; v < st; ++v) {
+        o[v] += o[v + st];
+        L[v] += L[v + st];
+      }
+    st_tag(A.attn + h * LE_HEAD_DIM + tid, o[0] / L[0], phase_tag(s, A.layers, l, TG_ATTN));
   }
   if (fine) trace_mark<kTrace>(A, ntr, tok, ftag | 0xC0000u);
   consumer_sync();
