@@ -113,10 +113,12 @@ __global__ void __launch_bounds__(128, 4)
     for (int i = 0; i < 4; ++i) {
       const int c = threadIdx.x + 128 * i;  // 16-byte chunk 0..511 of the tile
       const int r = c >> 4, d4 = c & 15;
-      // rows past the range are masked out; read its last row in their place
+      // rows past the range are masked out of the scores; their K is the range's last row, and
+      // their V is zero, so that no value left in the cache beyond the range reaches p . v
       const size_t row = (size_t)min(kt * 32 + r, P - 1) * kv_dim + 4 * d4;
       cp_async16(smem_u32(&sk[buf][r][4 * d4]), Kb + row);
-      cp_async16(smem_u32(&sv[buf][r][4 * d4]), Vb + row);
+      if (kt * 32 + r < P) cp_async16(smem_u32(&sv[buf][r][4 * d4]), Vb + row);
+      else *reinterpret_cast<float4*>(&sv[buf][r][4 * d4]) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     cp_async_commit();
   };
@@ -180,14 +182,9 @@ __global__ void __launch_bounds__(128, 4)
       o[h][0] *= ah;
       o[h][1] *= ah;
     }
-    // rows at or past P hold a substitute row (see load_tile): their values are replaced by
-    // zero rather than weighted by zero, so a non-finite value left in the cache cannot reach
-    // the sum (a select, no branch in the unrolled loop)
-    const int jn = P - (kt * 32 + 8 * warp);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][8 * warp + j][2 * lane]);
-      if (j >= jn) v2 = make_float2(0.0f, 0.0f);
+      const float2 v2 = *reinterpret_cast<const float2*>(&sv[buf][8 * warp + j][2 * lane]);
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const float pj = __shfl_sync(0xffffffffu, pe, 4 * j + h);
@@ -290,16 +287,9 @@ __global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ 
   }
 }
 
-// Causal attention of a prefill chunk: T consecutive tokens of one sequence, positions p0 ..
-// p0+T-1, all already in the cache of `kc` / `vc` (src/llama_engine.cpp:958-1021 per token:
-// s = (q . k) * 0.125, softmax over 0..pos, o = sum p v), on the tensor cores (mma.sync m16n8k16,
-// bf16 inputs, fp32 accumulation).  Grid (kv heads, 16-token query tiles), 4 warps;
-// warp w computes q head 4g + w for the tile's 16 tokens (16 MMA rows).  Per 32-position K / V
-// tile: S = Q K^T (4 key groups x 4 dim steps) and O += P V (2 key steps x 8 dim groups), each as
-// three MMAs on bf16 hi / lo parts (hi.hi + hi.lo + lo.hi: x = hi + lo with hi = bf16(x),
-// lo = bf16(x - hi)), so every product carries ~2^-16 relative error at most; online softmax on
-// the S fragments in registers (FlashAttention-2 form).  K / V tiles are converted to bf16 hi / lo
-// in shared memory as they are loaded (V transposed, so both B operands are read as bf16 pairs).
+// bf16 hi / lo parts of fp32 values for the tensor cores: x = hi + lo with hi = bf16(x) and
+// lo = bf16(x - hi), so a product of two such sums, taken as hi.hi + hi.lo + lo.hi, carries
+// ~2^-16 relative error at most.
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -309,187 +299,6 @@ __device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint3
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   hi = *reinterpret_cast<const uint32_t*>(&h);
   lo = pack_bf16(a - __low2float(h), b - __high2float(h));
-}
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-constexpr int kPfK = 72;   // bf16 per K row in shared memory (64 + 8 pad: conflict-free pair loads)
-constexpr int kPfV = 40;   // bf16 per transposed V row (32 keys + 8 pad)
-
-__global__ void __launch_bounds__(128)
-    k_attn_prefill_tc(const float* __restrict__ q, int q_dim, const float* __restrict__ kc,
-                      const float* __restrict__ vc, int kv_dim, int p0, int T, float* __restrict__ out) {
-  grid_dep_begin();
-  // [hi, lo][32 keys][kPfK] and [hi, lo][64 dims][kPfV]
-  __shared__ __align__(16) __nv_bfloat16 sk[2][32][kPfK];
-  __shared__ __align__(16) __nv_bfloat16 svt[2][64][kPfV];
-  const int g = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = 4 * g + warp;
-  // the last query tiles see the most keys: blockIdx.y = 0 (dispatched first) takes the last one
-  const int tok0 = (gridDim.y - 1 - blockIdx.y) * 16;
-  const int r0 = lane >> 2, cq = lane & 3;          // fragment row (and row + 8), column pair
-  const int qa = p0 + min(tok0 + r0, T - 1);        // query positions of this thread's two rows
-  const int qb = p0 + min(tok0 + r0 + 8, T - 1);
-  const int p_last = p0 + min(tok0 + 15, T - 1);
-  const int ntiles = p_last / 32 + 1;
-  const float* Kb = kc + (size_t)g * LE_HEAD_DIM;
-  const float* Vb = vc + (size_t)g * LE_HEAD_DIM;
-
-  // Q fragments (A operand, 16 x 64 = 4 k-steps), hi and lo, scaled by 0.125 after the MMA
-  uint32_t qh[4][4], ql[4][4];
-  {
-    const float* qra = q + (size_t)min(tok0 + r0, T - 1) * q_dim + (size_t)h * LE_HEAD_DIM;
-    const float* qrb = q + (size_t)min(tok0 + r0 + 8, T - 1) * q_dim + (size_t)h * LE_HEAD_DIM;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const int c0 = 16 * ks + 2 * cq;
-      const float2 a0 = *reinterpret_cast<const float2*>(qra + c0);
-      const float2 a1 = *reinterpret_cast<const float2*>(qrb + c0);
-      const float2 a2 = *reinterpret_cast<const float2*>(qra + c0 + 8);
-      const float2 a3 = *reinterpret_cast<const float2*>(qrb + c0 + 8);
-      split_bf16(a0.x, a0.y, qh[ks][0], ql[ks][0]);
-      split_bf16(a1.x, a1.y, qh[ks][1], ql[ks][1]);
-      split_bf16(a2.x, a2.y, qh[ks][2], ql[ks][2]);
-      split_bf16(a3.x, a3.y, qh[ks][3], ql[ks][3]);
-    }
-  }
-  float o[8][4];
-#pragma unroll
-  for (int n = 0; n < 8; ++n)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[n][i] = 0.0f;
-  float ma = -INFINITY, mb = -INFINITY, la = 0.0f, lb = 0.0f;
-
-  for (int kt = 0; kt < ntiles; ++kt) {
-    __syncthreads();  // the previous tile's shared data is no longer read
-    // load + convert: 32 keys x 64 dims of K and V, 128 threads x 4 float4 each
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int c = threadIdx.x + 128 * i;  // float4 chunk 0..511
-      const int key = c >> 4, d = 4 * (c & 15);
-      const size_t row = (size_t)min(kt * 32 + key, p_last) * kv_dim + d;  // rows past p_last are masked
-      const float4 k4 = *reinterpret_cast<const float4*>(Kb + row);
-      const float4 v4 = *reinterpret_cast<const float4*>(Vb + row);
-      uint32_t h0, l0, h1, l1;
-      split_bf16(k4.x, k4.y, h0, l0);
-      split_bf16(k4.z, k4.w, h1, l1);
-      *reinterpret_cast<uint2*>(&sk[0][key][d]) = make_uint2(h0, h1);
-      *reinterpret_cast<uint2*>(&sk[1][key][d]) = make_uint2(l0, l1);
-      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat16 vh = __float2bfloat16_rn(vv[e]);
-        svt[0][d + e][key] = vh;
-        svt[1][d + e][key] = __float2bfloat16_rn(vv[e] - __bfloat162float(vh));
-      }
-    }
-    __syncthreads();
-    // S = Q K^T: 4 key groups of 8 (n) x 4 dim steps of 16 (k)
-    float sc[4][4];
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sc[n][i] = 0.0f;
-      const int key = 8 * n + r0;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int d = 16 * ks + 2 * cq;
-        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&sk[0][key][d]);
-        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&sk[0][key][d + 8]);
-        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&sk[1][key][d]);
-        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&sk[1][key][d + 8]);
-        mma_bf16(sc[n], qh[ks], bh0, bh1);
-        mma_bf16(sc[n], qh[ks], bl0, bl1);
-        mma_bf16(sc[n], ql[ks], bh0, bh1);
-      }
-    }
-    // scale, causal mask, online softmax (rows r0 -> a, r0 + 8 -> b; a quad shares a row)
-    float mta = -INFINITY, mtb = -INFINITY;
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      const int key = kt * 32 + 8 * n + 2 * cq;
-      sc[n][0] = key <= qa ? sc[n][0] * 0.125f : -INFINITY;
-      sc[n][1] = key + 1 <= qa ? sc[n][1] * 0.125f : -INFINITY;
-      sc[n][2] = key <= qb ? sc[n][2] * 0.125f : -INFINITY;
-      sc[n][3] = key + 1 <= qb ? sc[n][3] * 0.125f : -INFINITY;
-      mta = fmaxf(mta, fmaxf(sc[n][0], sc[n][1]));
-      mtb = fmaxf(mtb, fmaxf(sc[n][2], sc[n][3]));
-    }
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-      mta = fmaxf(mta, __shfl_xor_sync(0xffffffffu, mta, off));
-      mtb = fmaxf(mtb, __shfl_xor_sync(0xffffffffu, mtb, off));
-    }
-    // tile 0 holds key 0 <= every query position, so the running max is finite from there on
-    const float mna = fmaxf(ma, mta), mnb = fmaxf(mb, mtb);
-    const float alpha_a = expf(ma - mna), alpha_b = expf(mb - mnb);
-    float sa = 0.0f, sb = 0.0f;
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      sc[n][0] = expf(sc[n][0] - mna);
-      sc[n][1] = expf(sc[n][1] - mna);
-      sc[n][2] = expf(sc[n][2] - mnb);
-      sc[n][3] = expf(sc[n][3] - mnb);
-      sa += sc[n][0] + sc[n][1];
-      sb += sc[n][2] + sc[n][3];
-    }
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-      sa += __shfl_xor_sync(0xffffffffu, sa, off);
-      sb += __shfl_xor_sync(0xffffffffu, sb, off);
-    }
-    la = la * alpha_a + sa;
-    lb = lb * alpha_b + sb;
-    ma = mna;
-    mb = mnb;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      o[n][0] *= alpha_a;
-      o[n][1] *= alpha_a;
-      o[n][2] *= alpha_b;
-      o[n][3] *= alpha_b;
-    }
-    // O += P V: P as A fragments (2 key steps of 16: S groups 2j, 2j+1), V^T rows as B
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      uint32_t ph[4], pl[4];
-      split_bf16(sc[2 * j][0], sc[2 * j][1], ph[0], pl[0]);
-      split_bf16(sc[2 * j][2], sc[2 * j][3], ph[1], pl[1]);
-      split_bf16(sc[2 * j + 1][0], sc[2 * j + 1][1], ph[2], pl[2]);
-      split_bf16(sc[2 * j + 1][2], sc[2 * j + 1][3], ph[3], pl[3]);
-      const int key = 16 * j + 2 * cq;
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const int d = 8 * n + r0;
-        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&svt[0][d][key]);
-        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&svt[0][d][key + 8]);
-        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&svt[1][d][key]);
-        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&svt[1][d][key + 8]);
-        mma_bf16(o[n], ph, bh0, bh1);
-        mma_bf16(o[n], ph, bl0, bl1);
-        mma_bf16(o[n], pl, bh0, bh1);
-      }
-    }
-  }
-  // out rows: token tok0 + r0 (c0, c1) and tok0 + r0 + 8 (c2, c3)
-  const float inva = 1.0f / la, invb = 1.0f / lb;
-  const int ta = tok0 + r0, tb = tok0 + r0 + 8;
-#pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const int d = 8 * n + 2 * cq;
-    if (ta < T)
-      *reinterpret_cast<float2*>(out + (size_t)ta * q_dim + (size_t)h * LE_HEAD_DIM + d) =
-          make_float2(o[n][0] * inva, o[n][1] * inva);
-    if (tb < T)
-      *reinterpret_cast<float2*>(out + (size_t)tb * q_dim + (size_t)h * LE_HEAD_DIM + d) =
-          make_float2(o[n][2] * invb, o[n][3] * invb);
-  }
 }
 
 // Greedy candidates of logits row blockIdx.y (ld floats apart) into part[row * gridDim.x + x].
