@@ -224,6 +224,8 @@ struct Engine {
   float* t_gu = nullptr;     // [tc_T][2 ffn] gate / up rows, 64-row groups interleaved
   float* t_part = nullptr;   // [kTcMaxSplits][tc_T][dim] split-K partial sums
   float* t_attn_part = nullptr;  // [tc_T][kv_heads][kAttnMaxSplits][kAttnPart] attention partials
+  uint8_t* kv_img = nullptr;     // [kv_heads][kv_img_tiles] prefill K / V tile images (attn::kTileBytes)
+  int kv_img_tiles = 0;          // tiles per kv head: ceil(max_seq / 64)
   int32_t* t_idx = nullptr;  // [3][tc_T] token | position | slot of the step's rows
   int32_t* h_idx = nullptr;  // pinned staging of t_idx
   cudaEvent_t idx_ev = nullptr;
@@ -802,6 +804,8 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMalloc(&E->t_gu, (size_t)T * 2 * ffn * 4));
   LE_CK(cudaMalloc(&E->t_part, (size_t)kTcMaxSplits * T * dim * 4));
   LE_CK(cudaMalloc(&E->t_attn_part, (size_t)T * E->kv_heads * kAttnMaxSplits * kAttnPart * 4));
+  E->kv_img_tiles = (E->max_seq + attn::kKeys - 1) / attn::kKeys;
+  LE_CK(cudaMalloc(&E->kv_img, (size_t)E->kv_heads * E->kv_img_tiles * attn::kTileBytes));
   LE_CK(cudaMalloc(&E->t_idx, (size_t)3 * T * 4));
   LE_CK(cudaMallocHost(&E->h_idx, (size_t)3 * T * 4));
   LE_CK(cudaEventCreateWithFlags(&E->idx_ev, cudaEventDisableTiming));
@@ -933,9 +937,12 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
       launch_pdl(k_rope_append, dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), dim3(256), 0, s, E->t_qkv, sq, qkv_stride,
                  dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
     if (prefill_p0 >= 0) {
+      const int p_last = prefill_p0 + n - 1;
+      launch_pdl(k_kv_tiles, dim3(E->kv_heads, p_last / attn::kKeys + 1), dim3(128), 0, s, kc, vc, kvd, p_last,
+                 E->kv_img, E->kv_img_tiles);
       launch_pdl(k_attn_prefill_tc5, dim3(E->kv_heads, (n + attn::kQ - 1) / attn::kQ), dim3(128),
-                 (size_t)attn::kSmemBytes, s, E->t_q, dim, kc, vc, kvd, prefill_p0, n, E->t_attn, E->tc_err,
-                 E->tc_wait_ns);
+                 (size_t)attn::kSmemBytes, s, E->t_q, dim, E->kv_img, E->kv_img_tiles, prefill_p0, n, E->t_attn,
+                 E->tc_err, E->tc_wait_ns);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
       // without position splits the attention kernel writes the o-proj input image itself
@@ -1217,7 +1224,7 @@ static void destroy(Engine* E) {
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
   void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_qkv, E->t_gu, E->t_part,
-                  E->t_idx, E->t_am, E->tc_err, E->t_attn_part, E->sc_logits, E->sc_target, E->sc_lp,
+                  E->t_idx, E->t_am, E->tc_err, E->t_attn_part, E->kv_img, E->sc_logits, E->sc_target, E->sc_lp,
                   E->sc_greedy};
   for (void* p : tdev) if (p) cudaFree(p);
   if (E->h_idx) cudaFreeHost(E->h_idx);
