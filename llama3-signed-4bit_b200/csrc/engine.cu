@@ -2114,11 +2114,14 @@ static int launch_gemv_mma(int mx, const QMat& W, const float* x, float* y, cuda
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(k_gemv_mma_sk<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return -1;
-    k_gemv_mma_sk<NT><<<ntiles, 32 * kw, smem, s>>>(x, mx, W, y);
+    // programmatic launch lets the next GEMV's CTAs start as these retire (~0.4 us per launch
+    // at most shapes); with one vector at K = 8192 the early dependents measured slower
+    if (NT == 1 && W.K >= 8192) k_gemv_mma_sk<NT><<<ntiles, 32 * kw, smem, s>>>(x, mx, W, y);
+    else launch_pdl(k_gemv_mma_sk<NT>, dim3(ntiles), dim3(32 * kw), smem, s, x, mx, W, y);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
   }
   const int grid = std::min<int>((ntiles + 7) / 8, num_sms * 4);
-  k_gemv_mma<NT><<<grid, 256, smem, s>>>(x, mx, W, y);
+  launch_pdl(k_gemv_mma<NT>, dim3(grid), dim3(256), smem, s, x, mx, W, y);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

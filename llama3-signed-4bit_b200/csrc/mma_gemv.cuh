@@ -210,7 +210,9 @@ __global__ void __launch_bounds__(256) k_gemv_mma(const float* __restrict__ x, i
   img.bfrag = reinterpret_cast<uint2*>(smem4);
   img.bsum = reinterpret_cast<float*>(img.bfrag + (size_t)nb * 4 * NT * 32);
   img.escl = img.bsum + MX * nb;
+  grid_dep_wait();  // x (and y) may belong to the previous kernel of the stream
   stage_digits(x, MX, W.K, img);
+  grid_dep_launch();  // the next kernel's CTAs may take SM room as this grid's CTAs retire
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int ntiles = (W.N + 15) / 16;
   const int warps = blockDim.x >> 5;
@@ -249,6 +251,7 @@ __global__ void __launch_bounds__(512) k_gemv_mma_sk(const float* __restrict__ x
   img.bfrag = reinterpret_cast<uint2*>(smem4);
   img.bsum = reinterpret_cast<float*>(img.bfrag + (size_t)nb * 4 * NT * 32);
   img.escl = img.bsum + MX * nb;
+  grid_dep_wait();  // x (and y) may belong to the previous kernel of the stream
   stage_digits(x, MX, W.K, img);
   const int KW = blockDim.x >> 5, w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -261,6 +264,7 @@ __global__ void __launch_bounds__(512) k_gemv_mma_sk(const float* __restrict__ x
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc.y[j][0] = acc.y[j][1] = 0.0f;
   mma_tile<NT, NT == 1>(W, row0, img, MX, acc, b0, b1);
+  grid_dep_launch();  // only the reduction and the store remain
   if ((t & 1) == 0) {
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
