@@ -89,19 +89,26 @@ def analyse(tr: np.ndarray) -> dict:
             per_seg[(kind, layer, c)][ev] = time_ns  # event 5 holds SM cycles spent waiting on ring data
     agg = defaultdict(lambda: defaultdict(list))
     ends = defaultdict(lambda: defaultdict(int))
+    layer_work = defaultdict(lambda: defaultdict(list))  # kind -> layer -> work of each CTA
     for (kind, layer, c), ev in per_seg.items():
         if all(e in ev for e in (1, 2, 3, 4)):
             k = KINDS.get(kind, str(kind))
             agg[k]["wait_us"].append((ev[2] - ev[1]) / 1e3)
             agg[k]["stage_us"].append((ev[3] - ev[2]) / 1e3)
             agg[k]["work_us"].append((ev[4] - ev[3]) / 1e3)
+            layer_work[k][layer].append((ev[4] - ev[3]) / 1e3)
             if 5 in ev:
                 agg[k]["ring_wait_kcyc"].append(ev[5] / 1e3)
             ends[k][layer] = max(ends[k][layer], ev[4])
     out = {}
     for k, d in agg.items():
         out[k] = {m: round(float(np.mean(v)), 3) for m, v in d.items()}
+        # slowest single (CTA, layer) sample, and the slowest CTA of each layer averaged over the
+        # layers (the one that holds up the next phase): max-over-CTAs / mean-over-CTAs per layer
         out[k]["max_work_us"] = round(float(np.max(d["work_us"])), 3)
+        lw = layer_work[k].values()
+        out[k]["layer_max_work_us"] = round(float(np.mean([max(v) for v in lw])), 3)
+        out[k]["layer_max_over_mean"] = round(float(np.mean([max(v) / max(np.mean(v), 1e-9) for v in lw])), 3)
         out[k]["n"] = len(d["work_us"])
     if t0 is not None:
         out["critical_path_end_us"] = {k: {int(l): round((t - t0) / 1e3, 2) for l, t in sorted(v.items())}
