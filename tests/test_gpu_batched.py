@@ -205,6 +205,33 @@ def test_batched_decode_40_rows(pkg, bindings, small_model, oracle_lib):
         eng.close()
 
 
+def test_prefill_chunk_edges(pkg, bindings, small_model, oracle_lib):
+    """One sequence prefilled as consecutive chunks whose starts and lengths sit on and off the
+    prefill attention's 32-query and 64-key tile edges (single-query chunks, a chunk that ends a
+    key tile exactly, chunks starting mid-tile); after every chunk the last position's logits and
+    greedy id against the oracle fed the same chunks.  One-token chunks go through forward_token
+    (the batch-1 path), so the two paths also read each other's KV rows."""
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    o = oracle_lib.orc_create(str(small_model).encode())
+    try:
+        vocab = eng.vocab_size
+        lens = [1, 31, 32, 2, 33, 63, 65, 1, 128]  # starts 0, 1, 32, 64, 66, 99, 162, 227, 228
+        ids = np.random.default_rng(61).integers(0, vocab, sum(lens)).astype(np.int32)
+        start = 0
+        for n in lens:
+            chunk = ids[start:start + n]
+            eng.prefill([int(t) for t in chunk], start, True)
+            oracle_lib.orc_prefill(o, fptr(chunk), n, start, 1)
+            ref = _oracle_logits(oracle_lib, o, vocab)
+            err = rel_max_err(eng.get_logits(), ref)
+            assert err <= LOGIT_RTOL, (start, n, err)
+            assert int(np.argmax(eng.get_logits())) == int(np.argmax(ref)), (start, n)
+            start += n
+    finally:
+        oracle_lib.orc_free(o)
+        eng.close()
+
+
 def test_long_prefill_and_split_attention(pkg, bindings, small_model, oracle_lib):
     """1040 prompt tokens in two chunks (query-tiled causal attention, the second chunk over 33
     key tiles), then two batched decode rows at positions 1040 and 1041: their attention is split
