@@ -167,24 +167,19 @@ __device__ __forceinline__ void mma_tile(const QMat& W, int row0, const DigitIma
       }
     }
     if (!kScalesAhead) scales(b, sc);
-    // epilogue of block b: lanes t and t^1 hold digit planes {0,1} and {2,3}
+    // epilogue of block b: lanes t and t^1 hold digit planes {0,1} and {2,3}; each lane folds its
+    // pair in int32 (|C| <= 128 * 15 * 128 < 2^18, so |C_even + 256 C_odd| < 2^27 is exact) and
+    // one shuffle per row brings the high pair to the owner lane
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-      const int p2 = __shfl_xor_sync(0xffffffffu, c[j][0], 1);
-      const int p3 = __shfl_xor_sync(0xffffffffu, c[j][1], 1);
-      const int q2 = __shfl_xor_sync(0xffffffffu, c[j][2], 1);
-      const int q3 = __shfl_xor_sync(0xffffffffu, c[j][3], 1);
+      const int x0 = c[j][0] + 256 * c[j][1], x1 = c[j][2] + 256 * c[j][3];
+      const int h0 = __shfl_xor_sync(0xffffffffu, x0, 1);
+      const int h1 = __shfl_xor_sync(0xffffffffu, x1, 1);
       const int m = 2 * j + seq_off;
       if (owner && m < MX) {
         const float es = img.escl[m * nb + b], xsb = img.bsum[m * nb + b];
-        float v0 = (float)p3;
-        v0 = fmaf(v0, 256.0f, (float)p2);
-        v0 = fmaf(v0, 256.0f, (float)c[j][1]);
-        v0 = fmaf(v0, 256.0f, (float)c[j][0]);
-        float v1 = (float)q3;
-        v1 = fmaf(v1, 256.0f, (float)q2);
-        v1 = fmaf(v1, 256.0f, (float)c[j][3]);
-        v1 = fmaf(v1, 256.0f, (float)c[j][2]);
+        const float v0 = fmaf((float)h0, 65536.0f, (float)x0);
+        const float v1 = fmaf((float)h1, 65536.0f, (float)x1);
         acc.y[j][0] += fmaf(sc[0] * es, v0, sc[1] * xsb);
         acc.y[j][1] += fmaf(sc[2] * es, v1, sc[3] * xsb);
       }

@@ -232,10 +232,11 @@ def test_prefill_chunk_edges(pkg, bindings, small_model, oracle_lib):
         eng.close()
 
 
-def test_long_prefill_and_split_attention(pkg, bindings, small_model, oracle_lib):
-    """1040 prompt tokens in two chunks (query-tiled causal attention, the second chunk over 33
-    key tiles), then two batched decode rows at positions 1040 and 1041: their attention is split
-    over position ranges and merged (k_attn_combine)."""
+def test_long_prefill_and_split_attention(pkg, bindings, small_model, oracle_lib, monkeypatch):
+    """1040 prompt tokens in two chunks of at most 1024 (query-tiled causal attention, the second
+    chunk over 33 key tiles), then two batched decode rows at positions 1040 and 1041: their
+    attention is split over position ranges and merged (k_attn_combine)."""
+    monkeypatch.setenv("LLAMA_B200_PREFILL_CHUNK", "1024")
     eng = pkg.LlamaEngine(str(small_model), bindings)
     o = oracle_lib.orc_create(str(small_model).encode())
     try:
