@@ -391,9 +391,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         // async proxy, and the copies' completion is only guaranteed visible to them through this
         // thread's own wait on the full barrier (the dequantisers' later hand-off is not enough).
         trace_ev(A, 8, g);
-        bool ok = wait_bar(A, &s_abort, bar_full(S, s), n & 1, 3) && wait_bar(A, &s_abort, bar_afull(S, ba), na & 1, 4);
+        // the three inputs are normally ready long before: test all three at once (independent
+        // non-blocking tests, so their latencies overlap), and take the bounded waits only if one
+        // is still pending
+        bool ok = mbar_test(bar_full(S, s), n & 1) & mbar_test(bar_afull(S, ba), na & 1) &
+                  (mbar_test(bar_dempty(S, bd), (nd - 1) & 1) | (g < kBufsD));
         trace_ev(A, 9, g);
-        ok = ok && (g < kBufsD || wait_bar(A, &s_abort, bar_dempty(S, bd), (nd - 1) & 1, 5));
+        if (!ok)
+          ok = wait_bar(A, &s_abort, bar_full(S, s), n & 1, 3) && wait_bar(A, &s_abort, bar_afull(S, ba), na & 1, 4) &&
+               (g < kBufsD || wait_bar(A, &s_abort, bar_dempty(S, bd), (nd - 1) & 1, 5));
         if (!ok) break;
         trace_ev(A, 1, g);
         tc_fence_after();
