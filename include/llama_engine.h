@@ -244,9 +244,11 @@ int llama_engine_check_schedule(int layers, int dim, int ffn_dim, int vocab_size
  * kernel and of the tensor-core GEMM to wait_ns (0 restores the default of 2 s), and with
  * expire_code != 0 makes the next launches wait on a device word that nothing writes, so that
  * the wait runs out: the persistent kernel's CTA 0 at the start of a launch, the GEMM's MMA
- * issuer before its first block.  The launch then drains and the next waiting call fails with
- * the timeout reported; expire_code = 0 turns that off again and clears the recorded error so
- * the engine can be used again.  Returns 0, or -1 for a NULL handle. */
+ * issuer before its first block; expire_code = 20 instead expires only the prefill attention
+ * kernel (its MMA-issuing thread, after the first K / V tile copies are in flight).  The launch
+ * then drains and the next waiting call fails with the timeout reported; expire_code = 0 turns
+ * that off again and clears the recorded error so the engine can be used again.  Returns 0, or
+ * -1 for a NULL handle. */
 int llama_engine_debug_waits(llama_engine_t engine, unsigned long long wait_ns, int expire_code);
 
 /* Greedy argmax of n device-resident fp32 logits that allocates no memory: writes the first

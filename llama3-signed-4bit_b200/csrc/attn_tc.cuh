@@ -198,10 +198,11 @@ __global__ void __launch_bounds__(128) k_kv_tiles(const float* __restrict__ kc, 
 // q: rotated queries [T][q_dim] (rows of the chunk, positions p0 ..); img: the layer's tile
 // images (k_kv_tiles, keys 0 .. p0 + T - 1); out: [T][q_dim].
 // Grid (kv_heads, ceil(T / 32)), 128 threads, attn::kSmemBytes of dynamic shared memory.
+// expire (test only): thread 0 first waits on a barrier phase that nothing completes.
 __global__ void __launch_bounds__(128) k_attn_prefill_tc5(const float* __restrict__ q, int q_dim,
                                                           const uint8_t* __restrict__ img, int tile_stride, int p0,
                                                           int T, float* __restrict__ out, uint32_t* error,
-                                                          unsigned long long wait_ns) {
+                                                          unsigned long long wait_ns, int expire) {
   using namespace attn;
   extern __shared__ uint8_t attn_smem_raw[];
   __shared__ __align__(8) unsigned long long s_bar[4];  // full[0], full[1], S ready, O_tile ready
@@ -271,6 +272,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc5(const float* __restric
   int n_mma = 0;  // thread 0: MMA groups committed (to bar_s or bar_o)
   uint32_t last_bar = 0, last_parity = 0;
   auto issue_s = [&](int j) {
+    if (s_abort) return;
     if (!attn::wait_bar(bar_full0 + 8 * (j & 1), (uint32_t)(j >> 1) & 1u, error, wait_ns, &s_abort)) return;
     tc::tc_fence_after();
     const uint32_t st = stage(j);
@@ -280,6 +282,9 @@ __global__ void __launch_bounds__(128) k_attn_prefill_tc5(const float* __restric
     last_bar = bar_s;
     last_parity = (uint32_t)j & 1u;
   };
+  // test only: phase 0 of the O_tile barrier completes only after the first P V product, which
+  // is issued after this wait, so the wait runs out (the tile copies are in flight meanwhile)
+  if (expire && tid == 0) attn::wait_bar(bar_o, 0u, error, wait_ns, &s_abort);
   if (tid == 0) issue_s(0);
 
   float o[LE_HEAD_DIM];

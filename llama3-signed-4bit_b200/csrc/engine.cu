@@ -145,6 +145,7 @@ struct TcLayer {
   TcMat qkv, o, gu, d;
 };
 constexpr int kTcMaxSplits = 8;
+constexpr int kExpireAttn = 20;  // llama_engine_debug_waits code that expires only the prefill attention
 constexpr int kAttnMaxSplits = 8;
 constexpr int kScoreRows = 256;  // rows of logits held at once by llama_engine_score_tokens
 
@@ -236,6 +237,7 @@ struct Engine {
   bool tc_dirty = true;        // a batched step ran since tc_err was last read
   unsigned long long tc_wait_ns = kWaitNs;  // bound on the GEMM's waits (test hook)
   int tc_expire = 0;                        // test hook: the GEMM's issuer waits on nothing
+  int attn_expire = 0;                      // test hook: the prefill attention's issuer waits on nothing
   // decode steps of the batched path replayed as CUDA graphs, one per (rows, logits rows,
   // attention splits); the rows' ids, positions and slots are read from t_idx
   struct TcGraph { int n, nlog, splits; bool fold; cudaGraphExec_t exec; };
@@ -943,7 +945,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
                  E->kv_img, E->kv_img_tiles);
       launch_pdl(k_attn_prefill_tc5, dim3(E->kv_heads, (n + attn::kQ - 1) / attn::kQ), dim3(128),
                  (size_t)attn::kSmemBytes, s, E->t_q, dim, E->kv_img, E->kv_img_tiles, prefill_p0, n, E->t_attn,
-                 E->tc_err, E->tc_wait_ns);
+                 E->tc_err, E->tc_wait_ns, E->attn_expire);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
       // without position splits the attention kernel writes the o-proj input image itself
@@ -1048,7 +1050,9 @@ static bool check_status(Engine* E) {
     return false;
   }
   if (tc_read && E->h_err[2] != 0) {
-    E->err = "tensor-core GEMM: a pipeline wait timed out (code " + std::to_string(E->h_err[2]) + ")";
+    E->err = (E->h_err[2] == (uint32_t)kExpireAttn ? "prefill attention (tensor cores): a wait timed out (code "
+                                                    : "tensor-core GEMM: a pipeline wait timed out (code ") +
+             std::to_string(E->h_err[2]) + ")";
     E->tc_dirty = true;  // keep reporting it
     return false;
   }
@@ -1891,7 +1895,8 @@ LE_API int llama_engine_debug_waits(llama_engine_t engine, unsigned long long wa
   E->pargs.wait_ns = ns;
   E->pargs.expire_where = expire_code;
   E->tc_wait_ns = ns;
-  E->tc_expire = expire_code != 0 ? 1 : 0;
+  E->tc_expire = expire_code != 0 && expire_code != kExpireAttn ? 1 : 0;
+  E->attn_expire = expire_code == kExpireAttn ? 1 : 0;
   // captured batched steps hold the old GEMM arguments
   for (auto& g : E->tc_graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);

@@ -1,9 +1,9 @@
 """The error path of the bounded device waits, exercised without a fault.
 
-Every wait in the persistent token-step kernel and in the tensor-core GEMM is bounded in time; on
-timeout the launch records an error word, drains its own copies and returns.  These tests shorten
-the bound to a millisecond and make one launch wait on a device word that nothing writes
-(``llama_engine_debug_waits``), then check that
+Every wait in the persistent token-step kernel, the tensor-core GEMM and the prefill attention is
+bounded in time; on timeout the launch records an error word, drains its own copies and returns.
+These tests shorten the bound to a millisecond and make one launch wait on a device word that
+nothing writes (``llama_engine_debug_waits``), then check that
 
 * the launch returns (no hang) and the next waiting call reports the timeout,
 * after the hook is turned off and the error cleared, the same engine again matches the oracle.
@@ -106,5 +106,35 @@ def test_tensor_core_gemm_wait_expires_and_engine_recovers(pkg, bindings, small_
             assert rel_max_err(eng.get_logits_batch(0), ref_logits[s]) <= LOGIT_RTOL
             assert got == ref_toks[s]
             tok, pos = got, pos + 1
+    finally:
+        eng.close()
+
+
+def test_prefill_attention_wait_expires_and_engine_recovers(pkg, bindings, small_model, oracle_lib):
+    """Expire code 20 makes only the prefill attention kernel's issuing thread wait on a barrier
+    phase that nothing completes (after its first K / V tile copies are issued): the kernel drains
+    its copies, the next waiting call reports the attention timeout, and after clearing it the
+    same engine's prefill matches the oracle again."""
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    try:
+        if eng.batch_path != "tensor-core":
+            pytest.skip("batched path not on the tensor cores: " + bindings.last_error(eng.handle))
+        lib = bindings.lib
+        ids = np.random.default_rng(23).integers(0, eng.vocab_size, 70).astype(np.int32)
+        assert lib.llama_engine_debug_waits(eng.handle, WAIT_NS, 20) == 0
+        eng.prefill([int(t) for t in ids], 0, True)  # queued; the failure shows at the next wait
+        assert lib.llama_engine_sample(eng.handle, ctypes.c_float(0.0), ctypes.c_float(0.9)) == 0
+        msg = bindings.last_error(eng.handle)
+        assert "prefill attention" in msg and "timed out" in msg, msg
+        assert lib.llama_engine_debug_waits(eng.handle, 0, 0) == 0
+        o = oracle_lib.orc_create(str(small_model).encode())
+        try:
+            oracle_lib.orc_prefill(o, fptr(ids), len(ids), 0, 1)
+            ref = np.ctypeslib.as_array(oracle_lib.orc_get_logits(o), shape=(eng.vocab_size,)).copy()
+            eng.prefill([int(t) for t in ids], 0, True)
+            assert rel_max_err(eng.get_logits(), ref) <= LOGIT_RTOL
+            assert eng.sample(0.0, 0.9) == oracle_lib.orc_sample_engine(o, ctypes.c_float(0.0), ctypes.c_float(0.9))
+        finally:
+            oracle_lib.orc_free(o)
     finally:
         eng.close()
