@@ -795,11 +795,18 @@ def main():
                     help="layers of the synthetic model (16 = LLaMA-3.2-1B; fewer only for profiling runs)")
     ap.add_argument("--no-tp2", dest="tp2", action="store_false",
                     help="skip the 2-way tensor-parallel batch-1 measurement of a 2-GPU run")
+    ap.add_argument("--gemm-trace", default=None, metavar="M,N,K",
+                    help="only trace CTA 0's pipeline of one isolated tcgen05 GEMM launch and print it")
     ap.add_argument("--write-model", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.write_model:  # child of the reference arm: write the config-0 model, print its path
         pkg = load_package()
         print(pkg.model_file.cached_model(cache_dir(), pkg.model_file.LLAMA_3_2_1B, seed=0, sigma=0.02))
+        return
+    if args.gemm_trace:  # diagnostics of the batched path's GEMM, not a benchmark line
+        M, N, K = (int(v) for v in args.gemm_trace.split(","))
+        pkg = load_package()
+        print(json.dumps(pkg.trace.capture_gemm(pkg.LlamaEngineBindings().lib, M, N, K)), flush=True)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -159,6 +159,17 @@ __device__ __forceinline__ bool mbar_test(uint32_t a, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase is pending sleeps (up to hint_ns) until
+// the phase completes instead of returning at once, so waiting warps take no issue slots.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t a, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(a), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
   uint32_t ok;
   asm volatile(

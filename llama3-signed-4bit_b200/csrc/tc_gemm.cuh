@@ -71,6 +71,7 @@ constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64
 constexpr int kBufsD = 2;                // accumulator buffers (128 columns: hi | lo tokens)
 constexpr int kTmemCols = 512;
 constexpr int kDCol = kBufsA * 64;
+constexpr uint32_t kSleepNs = 20000;    // suspend hint of a pending wait (the bound is checked between)
 constexpr int kPrefetch = 8;             // records prefetched into L2 this many blocks ahead
 constexpr int kNumBars = 2 * kStages + kBufsA + kBufsD + 2 * kSide + 1;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kSide * kSideBytes + (kNumBars * 8 + 63) / 64 * 64;
@@ -221,7 +222,7 @@ __device__ __forceinline__ bool wait_bar(const Args& A, volatile uint32_t* abort
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = gtimer();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity, kSleepNs)) return true;
     if (*abort_flag) return false;
     if (gtimer() - t0 > A.wait_ns) {
       *abort_flag = 1u;
@@ -236,7 +237,7 @@ __device__ __forceinline__ void wait_bar_drain(const Args& A, volatile uint32_t*
                                                uint32_t parity, uint32_t where) {
   if (mbar_try(bar, parity)) return;
   const unsigned long long t0 = gtimer();
-  while (!mbar_try(bar, parity)) {
+  while (!mbar_try_sleep(bar, parity, kSleepNs)) {
     if (gtimer() - t0 > A.wait_ns) {
       *abort_flag = 1u;
       atomicCAS(A.error, 0u, where);

@@ -114,3 +114,73 @@ def analyse(tr: np.ndarray) -> dict:
         out["critical_path_end_us"] = {k: {int(l): round((t - t0) / 1e3, 2) for l, t in sorted(v.items())}
                                        for k, v in ends.items()}
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# tcgen05 GEMM pipeline trace: CTA 0's globaltimer stamps per K block (kTraceEvents x
+# kTraceBlocks, written by llama_b128_gemm when $LLAMA_B128_GEMM_TRACE names a file).
+# ---------------------------------------------------------------------------------------------
+GEMM_EVENTS = 10
+GEMM_BLOCKS = 256
+# 0 copies issued, 1 MMA inputs ready, 2 dequantiser sees the stage, 3 A codes written,
+# 4 epilogue sees the accumulator, 5 epilogue done, 6 MMAs issued, 7 commit issued,
+# 8 MMA loop top, 9 issuer past its barrier tests
+GEMM_INTERVALS = {
+    "issuer: barrier tests (8 -> 9)": (8, 9, 0),
+    "issuer: tests -> inputs ready (9 -> 1)": (9, 1, 0),
+    "issuer: 8 MMAs issued (1 -> 6)": (1, 6, 0),
+    "issuer: commit (6 -> 7)": (6, 7, 0),
+    "issuer: to next block (7 -> 8 of g+1)": (7, 8, 1),
+    "issuer: block period (8 -> 8 of g+1)": (8, 8, 1),
+    "slack: copies issued -> inputs ready (0 -> 1)": (0, 1, 0),
+    "dequantiser: stage seen -> A codes written (2 -> 3)": (2, 3, 0),
+    "slack: A codes written -> inputs ready (3 -> 1)": (3, 1, 0),
+    "commit -> epilogue sees the accumulator (7 -> 4)": (7, 4, 0),
+    "epilogue per block (4 -> 5)": (4, 5, 0),
+    "slack: epilogue done -> inputs of g+2 ready (5 -> 1 of g+2)": (5, 1, 2),
+}
+
+
+def gemm_pipeline(path) -> dict:
+    """Median ns of each pipeline interval over CTA 0's blocks (the first 8 and the last are
+    left out: pipeline fill and drain)."""
+    t = np.fromfile(path, dtype=np.uint64).astype(np.int64).reshape(GEMM_EVENTS, GEMM_BLOCKS)
+    nb = int((t[7] > 0).sum())
+    sl = slice(8, max(9, min(nb - 2, GEMM_BLOCKS - 2)))
+    out = {"blocks": nb}
+    for name, (a, b, shift) in GEMM_INTERVALS.items():
+        out[name] = float(np.median(np.roll(t[b], -shift)[sl] - t[a][sl]))
+    return out
+
+
+def capture_gemm(lib, M: int, N: int, K: int, seed: int = 3, path: str | None = None) -> dict:
+    """Runs the isolated tcgen05 GEMM (llama_b128_gemm) on seeded synthetic weights at M x N x K
+    twice untraced and once traced, and returns gemm_pipeline() of the traced launch."""
+    import os
+    import tempfile
+
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(seed)
+    nib = torch.randint(0, 256, (N * K // 2,), dtype=torch.uint8, device=dev, generator=g)
+    step = torch.empty(N * K // 128, device=dev).uniform_(1e-3, 2e-2, generator=g)
+    mn = -8.0 * step * torch.empty_like(step).uniform_(0.8, 1.2, generator=g)
+    step16 = step.to(torch.bfloat16).view(torch.int16)
+    mn16 = mn.to(torch.bfloat16).view(torch.int16)
+    x = torch.randn(M, K, device=dev, generator=g)
+    y = torch.empty(M, N, device=dev)
+    path = path or os.path.join(tempfile.gettempdir(), f"gemm_trace_{M}x{N}x{K}.bin")
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for rep in range(3):
+        if rep == 2:
+            os.environ["LLAMA_B128_GEMM_TRACE"] = path
+        try:
+            rc = lib.llama_b128_gemm(ctypes.c_void_p(nib.data_ptr()), ctypes.c_void_p(step16.data_ptr()),
+                                     ctypes.c_void_p(mn16.data_ptr()), N, K, ctypes.c_void_p(x.data_ptr()), M,
+                                     ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(stream))
+        finally:
+            os.environ.pop("LLAMA_B128_GEMM_TRACE", None)
+        if rc != 0:
+            raise RuntimeError(f"llama_b128_gemm failed at {M} x {N} x {K}")
+    return {"M": M, "N": N, "K": K, **gemm_pipeline(path)}

@@ -32,3 +32,24 @@ def test_analyse_phase_breakdown(pkg):
     assert abs(q["layer_max_over_mean"] - round((3.0 / 2.0 + 4.0 / 2.0) / 2, 3)) < 1e-9
     # the last CTA to finish each layer, from the token's start
     assert out["critical_path_end_us"]["qkv"] == {0: 4.3, 1: 15.3}
+
+
+def test_gemm_pipeline_intervals(pkg, tmp_path):
+    tr_mod = pkg.trace
+    E, B = tr_mod.GEMM_EVENTS, tr_mod.GEMM_BLOCKS
+    nb = 40
+    t = np.zeros((E, B), dtype=np.uint64)
+    for g in range(nb):  # a steady pipeline: one block every 700 ns
+        base = 10_000 + 700 * g
+        t[8, g], t[9, g], t[1, g], t[6, g], t[7, g] = base, base + 60, base + 200, base + 520, base + 580
+        t[0, g], t[2, g], t[3, g] = base - 3000, base - 2500, base - 2000
+        t[4, g], t[5, g] = base + 800, base + 1150
+    p = tmp_path / "trace.bin"
+    t.tofile(p)
+    out = tr_mod.gemm_pipeline(p)
+    assert out["blocks"] == nb
+    assert out["issuer: block period (8 -> 8 of g+1)"] == 700
+    assert out["issuer: barrier tests (8 -> 9)"] == 60
+    assert out["issuer: 8 MMAs issued (1 -> 6)"] == 320
+    assert out["epilogue per block (4 -> 5)"] == 350
+    assert out["slack: epilogue done -> inputs of g+2 ready (5 -> 1 of g+2)"] == 200 + 1400 - 1150
