@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
       const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
       const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = (g[k] / (1.0f + expf(-g[k]))) * u[k];
+      for (int k = 0; k < 8; ++k) e[k] = __fdividef(g[k], 1.0f + __expf(-g[k])) * u[k];
     } else {
       float* xp = x + (size_t)t * ldx + i0;
       const float4 a = *reinterpret_cast<const float4*>(xp), b = *reinterpret_cast<const float4*>(xp + 4);
