@@ -232,6 +232,33 @@ def test_prefill_chunk_edges(pkg, bindings, small_model, oracle_lib):
         eng.close()
 
 
+def test_max_context_three_attention_paths(pkg, bindings, small_model):
+    """The whole context (8192 positions = max_seq_len): the last position's logits computed by
+    three independent attention implementations over the same cache contents.  (a) prefill of
+    all 8192 ids in 2048-token chunks (tcgen05 prefill attention, up to 128 key tiles per CTA);
+    (b) prefill of the first 8191, then id 8191 through forward_token (the persistent batch-1
+    kernel's attention); (c) the same, through forward_batch (batched decode attention split
+    over position ranges).  The oracle needs minutes per thousand positions at this length, so
+    the paths are checked against each other: logits within 1e-3, same greedy id."""
+    eng = pkg.LlamaEngine(str(small_model), bindings)
+    try:
+        assert eng.batch_path == "tensor-core" and eng.decode_path == "persistent"
+        n = 8192
+        ids = np.random.default_rng(8192).integers(0, eng.vocab_size, n).astype(np.int32)
+        eng.prefill([int(t) for t in ids], 0, True)
+        la = eng.get_logits()
+        eng.prefill([int(t) for t in ids[:-1]], 0, False)
+        eng.forward_token(int(ids[-1]), n - 1, True)
+        lb = eng.get_logits()
+        eng.forward_batch([int(ids[-1])], [n - 1], [0], True)
+        lc = eng.get_logits_batch(0)
+        assert rel_max_err(lb, la) <= LOGIT_RTOL, rel_max_err(lb, la)
+        assert rel_max_err(lc, la) <= LOGIT_RTOL, rel_max_err(lc, la)
+        assert int(np.argmax(la)) == int(np.argmax(lb)) == int(np.argmax(lc))
+    finally:
+        eng.close()
+
+
 def test_long_prefill_and_split_attention(pkg, bindings, small_model, oracle_lib, monkeypatch):
     """1040 prompt tokens in two chunks of at most 1024 (query-tiled causal attention, the second
     chunk over 33 key tiles), then two batched decode rows at positions 1040 and 1041: their
