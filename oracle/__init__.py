@@ -22,7 +22,7 @@ _F = ctypes.POINTER(ctypes.c_float)
 
 
 def _default_ref_dir() -> str | None:
-    """The reference tree: $LLAMA_REF_DIR, else the checker-building machine's copy if present."""
+    """The reference tree: $LLAMA_REF_DIR, else the building machine's copy if present."""
     env = os.environ.get("LLAMA_REF_DIR")
     if env:
         return env

@@ -1,7 +1,7 @@
 /*
  * ORACLE — test infrastructure only.  Never linked into, loaded by, or called from the product
  * library; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it, and only
- * as the checker.
+ * as the reference results the GPU path is compared with.
  *
  * A plain-C, single-threaded restatement of the reference engine's token loop, following the
  * scalar (non-NEON) code path that the reference compiles to on Linux/x86
