@@ -349,6 +349,20 @@ def run_ours(args, rank, world, local_rank):
                    "kind": "reference" if use_ref else "port",
                    "sample": f"one process, 1 thread: prefill of the 31-id prompt (untimed), 1 warm-up + "
                              f"{args.cpu_tokens} timed greedy decode tokens (forward_token + sample) from position 32"}
+        if world == 1 and not args.no_cpu_baseline and (batched or box):
+            # configs with many sequences: one reference process per host core, one sequence each
+            # (the reference's prefill is the same token loop, so this also bounds its prefill rate)
+            n_proc = max(1, min(host_cores(), 32))
+            agg_steps = 6
+            with mp.get_context("spawn").Pool(n_proc) as pool:
+                times = pool.map(_ref_decode_worker, [(str(model), prompt, 1, agg_steps, False)] * n_proc)
+            cpu_all = {"value": round(n_proc * agg_steps / max(t for t, _ in times), 4), "unit": "tok/s",
+                       "cores": n_proc, "kind": "reference" if all(u for _, u in times) else "port",
+                       "sample": f"{n_proc} concurrent processes (1 thread each), one sequence each from position "
+                                 f"0, 1 warm-up + {agg_steps} timed greedy tokens each; aggregate tok/s"}
+            for obj in (batched, box):
+                if obj:
+                    obj["cpu_baseline"] = cpu_all
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
