@@ -222,7 +222,7 @@ struct Engine {
   float* t_q = nullptr;      // [tc_T][dim] rotated queries
   float* t_attn = nullptr;   // [tc_T][dim]
   float* t_qkv = nullptr;    // [kTcMaxSplits][tc_T][dim + 2 kv_dim] q | k | v before RoPE (split-K planes)
-  float* t_gu = nullptr;     // [tc_T][2 ffn] gate / up rows, 64-row groups interleaved
+  float* t_gu = nullptr;     // [tc_T][ffn] SiLU(gate) * up, from the gate-up GEMM's epilogue
   float* t_part = nullptr;   // [kTcMaxSplits][tc_T][dim] split-K partial sums
   float* t_attn_part = nullptr;  // [tc_T][kv_heads][kAttnMaxSplits][kAttnPart] attention partials
   uint8_t* kv_img = nullptr;     // [kv_heads][kv_img_tiles] prefill K / V tile images (attn::kTileBytes)
@@ -773,8 +773,8 @@ static bool init_tc(Engine* E) {
     off += (size_t)tiles * kb * tc::kRecBytes;
     return m;
   };
-  auto repack = [&](const QMat& W, const TcMat& M, int row0, int G, int o) -> bool {
-    k_tc_repack<<<E->num_sms * 8, 256, 0, E->stream>>>(W, const_cast<uint8_t*>(M.recs), row0, G, o);
+  auto repack = [&](const QMat& W, const TcMat& M, int row0, int G, int o, int stride = 1) -> bool {
+    k_tc_repack<<<E->num_sms * 8, 256, 0, E->stream>>>(W, const_cast<uint8_t*>(M.recs), row0, G, o, stride);
     LE_CK(cudaGetLastError());
     return true;
   };
@@ -789,7 +789,7 @@ static bool init_tc(Engine* E) {
     if (!repack(D.q, Y.qkv, 0, kM, 0) || !repack(D.k, Y.qkv, dim, kM, 0) || !repack(D.v, Y.qkv, dim + kvd, kM, 0))
       return false;
     if (!repack(D.o, Y.o, 0, kM, 0)) return false;
-    if (!repack(D.g, Y.gu, 0, 64, 0) || !repack(D.u, Y.gu, 0, 64, 64)) return false;
+    if (!repack(D.g, Y.gu, 0, 64, 0, 2) || !repack(D.u, Y.gu, 0, 64, 1, 2)) return false;
     if (!repack(D.d, Y.d, 0, kM, 0)) return false;
   }
   E->tc_lm = take(t_lm, kb_d);
@@ -804,7 +804,7 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMalloc(&E->t_q, (size_t)T * dim * 4));
   LE_CK(cudaMalloc(&E->t_attn, (size_t)T * dim * 4));
   LE_CK(cudaMalloc(&E->t_qkv, (size_t)kTcMaxSplits * T * (dim + 2 * kvd) * 4));
-  LE_CK(cudaMalloc(&E->t_gu, (size_t)T * 2 * ffn * 4));
+  LE_CK(cudaMalloc(&E->t_gu, (size_t)T * ffn * 4));
   LE_CK(cudaMalloc(&E->t_part, (size_t)kTcMaxSplits * T * dim * 4));
   LE_CK(cudaMalloc(&E->t_attn_part, (size_t)T * E->kv_heads * kAttnMaxSplits * kAttnPart * 4));
   E->kv_img_tiles = (E->max_seq + attn::kKeys - 1) / attn::kKeys;
@@ -931,7 +931,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     const DevLayer& D = E->L[l];
     float* kc = E->kcache + l * layer_stride;
     float* vc = E->vcache + l * layer_stride;
-    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, 0, dim,
+    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, dim,
                E->img_d);
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
@@ -957,19 +957,21 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
                    E->t_attn);
     }
     if (prefill_p0 >= 0 || attn_splits > 1)
-      launch_pdl(k_tc_stage, dim3(n, dim / 2048), dim3(256), 0, s, E->t_attn, dim, nullptr, 0, 0, nullptr, 0, dim,
+      launch_pdl(k_tc_stage, dim3(n, dim / 2048), dim3(256), 0, s, E->t_attn, dim, nullptr, 0, 0, nullptr, dim,
                  E->img_d);
     const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
-    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, so, part_stride, D.post_norm, 0, dim,
+    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, so, part_stride, D.post_norm, dim,
                E->img_d);
-    tc_launch(E, Y.gu, E->img_d, n, 1, rows(E->t_gu, 2 * ffn, 2 * ffn, 0));
-    launch_pdl(k_tc_stage, dim3(n, ffn / 2048), dim3(256), 0, s, E->t_gu, 2 * ffn, nullptr, 0, 0, nullptr, 1, ffn,
+    Args Agu = rows(E->t_gu, ffn, ffn, 0);
+    Agu.swiglu = 1;
+    tc_launch(E, Y.gu, E->img_d, n, 1, Agu);
+    launch_pdl(k_tc_stage, dim3(n, ffn / 2048), dim3(256), 0, s, E->t_gu, ffn, nullptr, 0, 0, nullptr, ffn,
                E->img_f);
     d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), rows(E->t_part, dim, dim, part_stride));
   }
   if (nlog > 0) {
     launch_pdl(k_tc_stage, dim3(nlog), dim3(256), 0, s, E->t_x + (size_t)lrow0 * dim, dim,
-               E->t_part + (size_t)lrow0 * dim, d_splits, part_stride, E->final_norm, 0, dim, E->img_d);
+               E->t_part + (size_t)lrow0 * dim, d_splits, part_stride, E->final_norm, dim, E->img_d);
     tc_launch(E, E->tc_lm, E->img_d, nlog, 1, rows(lg_out, (int)E->vocab, (int)E->vocab, 0));
     if (!logits_out) {
       launch_pdl(k_argmax_rows_batch, dim3(E->tc_am_parts, nlog), dim3(256), 0, s, E->logits, (int)E->vocab,
@@ -2201,8 +2203,8 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     cudaMemsetAsync(img, 0, img_bytes, s);
     cudaMemsetAsync(err, 0, 16, s);
     QMat W{nibbles, step_bf16, min_bf16, N, K};
-    k_tc_repack<<<sms * 8, 256, 0, s>>>(W, recs, 0, kM, 0);
-    k_tc_stage<<<dim3(M, K / 2048), 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, 0, K, img);
+    k_tc_repack<<<sms * 8, 256, 0, s>>>(W, recs, 0, kM, 0, 1);
+    k_tc_stage<<<dim3(M, K / 2048), 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, K, img);
     Args A{};
     A.recs = recs;
     A.img = img;

@@ -89,6 +89,7 @@ struct Args {
   unsigned long long* trace;  // optional: CTA 0's pipeline events, [kTraceEvents][kTraceBlocks]
   unsigned long long wait_ns;  // bound on every wait
   int expire;            // test only: nonzero makes the MMA issuer wait on a barrier nothing completes
+  int swiglu;            // gate-up tiles (gate / up rows interleaved): store SiLU(gate) * up per ffn row
 };
 
 // Pipeline trace (diagnostics): globaltimer stamps of CTA 0 for its first kTraceBlocks blocks.
@@ -527,11 +528,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       if (lane == 0) mbar_arrive_n(bar_sempty(S, j), 1);
       if (warp == 11) trace_ev(A, 5, g);
       if (c.kb + 1 == c.U.kb1) {  // unit complete: store its rows
-        const int n = c.U.tile * kM + r;
+        int n = c.U.tile * kM + r;
+        bool store = true;
+        if (A.swiglu) {  // rows r (gate, r even) and r + 1 (up) are ffn row tile * 64 + r / 2
+#pragma unroll
+          for (int i = 0; i < kHalf; ++i) {
+            const float up = __shfl_xor_sync(0xffffffffu, acc[i], 1);
+            acc[i] = __fdividef(acc[i], 1.0f + __expf(-acc[i])) * up;
+          }
+          n = c.U.tile * (kM / 2) + (r >> 1);
+          store = (r & 1) == 0;
+        }
         const int tok0 = c.U.tt * kTok + kHalf * h;
         const int nt = min(kHalf, A.T - tok0);
         float* o = A.out + (size_t)c.U.split * A.split_stride + (size_t)tok0 * A.ldo + n;
-        if (n < A.N) {
+        if (store && n < A.N) {
 #pragma unroll
           for (int i = 0; i < kHalf; ++i) {
             if (i < nt) *o = acc[i];
@@ -555,17 +566,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
 
 // ---------------------------------------------------------------------------------------------
 // Weight record builder: rows [0, N) of W go to tile rows dest(n) = row0 + (n / G) * 128 + off +
-// n % G of a record arena with kb_total = W.K / 128 blocks per tile (G = 128, off = 0 for plain
-// and concatenated matrices; G = 64, off = 0 / 64 for the gate / up halves of gate-up tiles).
+// stride * (n % G) of a record arena with kb_total = W.K / 128 blocks per tile (G = 128,
+// stride = 1, off = 0 for plain and concatenated matrices; G = 64, stride = 2, off = 0 / 1 for the
+// gate / up rows of gate-up tiles, so gate row f and up row f are tile rows 2 (f % 64) and
+// 2 (f % 64) + 1: adjacent lanes of one epilogue warp).
 // ---------------------------------------------------------------------------------------------
-__global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G, int off) {
+__global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G, int off, int stride) {
   const int kbt = W.K >> 7;
   const size_t total = (size_t)W.N * kbt * 4;  // one thread per 16-byte nibble chunk
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int c = (int)(i & 3);
     const size_t nb = i >> 2;
     const int n = (int)(nb / kbt), kb = (int)(nb % kbt);
-    const int dr = row0 + (n / G) * kM + off + n % G;
+    const int dr = row0 + (n / G) * kM + off + stride * (n % G);
     const int tile = dr / kM, rr = dr % kM;
     uint8_t* rec = recs + ((size_t)tile * kbt + kb) * kRecBytes;
     const uint4 src = *reinterpret_cast<const uint4*>(W.nib + (size_t)n * (W.K >> 1) + kb * 64 + c * 16);
@@ -583,15 +596,14 @@ __global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G,
 // block sums of compute_x_block_sums, src/llama_engine.cpp:496-521).  The input row is
 //   * x[t] (+ sum_s part[s][t], the split-K partials of the previous projection, folded into the
 //     residual x, which is written back: x += proj, :1024-1025 and :1033-1034), rms-normalised
-//     with gamma when given (rms_norm, :87-115); or
-//   * with gateup != 0: silu(g) * u (:362-491, silu(v) = v / (1 + exp(-v))) from a gate/up GEMM
-//     output row whose 128-column tiles hold 64 gate rows then the 64 matching up rows.
+//     with gamma when given (rms_norm, :87-115); or x[t] as it is (the attention output, or the
+//     SwiGLU activations silu(g) * u, :362-491, that the gate-up GEMM's epilogue wrote).
 // K is a multiple of 2048; a thread handles runs of 8 consecutive elements.  Without gamma the
 // grid is (tokens, K / 2048), one 2048-wide run per CTA; with gamma (tokens, 1).
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx, const float* __restrict__ part,
                                                   int nsplit, size_t split_stride, const float* __restrict__ gamma,
-                                                  int gateup, int K, uint8_t* __restrict__ img) {
+                                                  int K, uint8_t* __restrict__ img) {
   grid_dep_begin();
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -607,15 +619,7 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
     if (j < j0 || j >= j1) continue;
     const int i0 = j * 2048 + threadIdx.x * 8;
     float e[8];
-    if (gateup) {
-      const float* gp = x + (size_t)t * ldx + (i0 >> 6) * 128 + (i0 & 63);
-      const float4 g0 = *reinterpret_cast<const float4*>(gp), g1 = *reinterpret_cast<const float4*>(gp + 4);
-      const float4 u0 = *reinterpret_cast<const float4*>(gp + 64), u1 = *reinterpret_cast<const float4*>(gp + 68);
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = __fdividef(g[k], 1.0f + __expf(-g[k])) * u[k];
-    } else {
+    {
       float* xp = x + (size_t)t * ldx + i0;
       const float4 a = *reinterpret_cast<const float4*>(xp), b = *reinterpret_cast<const float4*>(xp + 4);
       e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w; e[4] = b.x; e[5] = b.y; e[6] = b.z; e[7] = b.w;
