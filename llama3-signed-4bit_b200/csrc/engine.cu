@@ -833,7 +833,15 @@ static bool init_tc(Engine* E) {
 // Number of K splits for a GEMM whose tiles x token tiles alone would leave SMs idle.
 static int tc_splits(const Engine* E, const TcMat& W, int tok_tiles) {
   const int base = W.tiles * tok_tiles;
-  if (base >= E->num_sms) return 1;
+  if (base >= E->num_sms) {
+    // enough units for every SM: split K in two only for long K (the down projection), where the
+    // fuller last wave outweighs the extra partial plane (units per wave-slot: busy fraction)
+    auto busy = [&](int s) {
+      const int u = base * s, waves = (u + E->num_sms - 1) / E->num_sms;
+      return (double)u / (double)(waves * E->num_sms);
+    };
+    return (W.kb >= 32 && busy(2) > busy(1) + 0.05) ? 2 : 1;
+  }
   int s = std::min(kTcMaxSplits, E->num_sms / base);
   s = std::min(s, std::max(1, W.kb / 2));
   return std::max(1, s);
