@@ -932,6 +932,9 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     A.split_stride = split_stride;
     return A;
   };
+  // staging with every split-K plane's loads at once for steps of up to one row per SM (decode
+  // batches, where the step is latency-bound), three at a time for larger steps (occupancy)
+  auto stage_fn = n <= E->num_sms ? k_tc_stage<true> : k_tc_stage<false>;
   k_embed_batch<<<n, 256, 0, s>>>(E->lm_head, tok, E->t_x, dim);
   int d_splits = 0;
   for (uint32_t l = 0; l < E->layers; ++l) {
@@ -939,7 +942,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     const DevLayer& D = E->L[l];
     float* kc = E->kcache + l * layer_stride;
     float* vc = E->vcache + l * layer_stride;
-    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, dim,
+    launch_pdl(stage_fn, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, dim,
                E->img_d);
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
@@ -965,20 +968,20 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
                    E->t_attn);
     }
     if (prefill_p0 >= 0 || attn_splits > 1)
-      launch_pdl(k_tc_stage, dim3(n, dim / 2048), dim3(256), 0, s, E->t_attn, dim, nullptr, 0, 0, nullptr, dim,
+      launch_pdl(stage_fn, dim3(n, dim / 2048), dim3(256), 0, s, E->t_attn, dim, nullptr, 0, 0, nullptr, dim,
                  E->img_d);
     const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
-    launch_pdl(k_tc_stage, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, so, part_stride, D.post_norm, dim,
+    launch_pdl(stage_fn, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, so, part_stride, D.post_norm, dim,
                E->img_d);
     Args Agu = rows(E->t_gu, ffn, ffn, 0);
     Agu.swiglu = 1;
     tc_launch(E, Y.gu, E->img_d, n, 1, Agu);
-    launch_pdl(k_tc_stage, dim3(n, ffn / 2048), dim3(256), 0, s, E->t_gu, ffn, nullptr, 0, 0, nullptr, ffn,
+    launch_pdl(stage_fn, dim3(n, ffn / 2048), dim3(256), 0, s, E->t_gu, ffn, nullptr, 0, 0, nullptr, ffn,
                E->img_f);
     d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), rows(E->t_part, dim, dim, part_stride));
   }
   if (nlog > 0) {
-    launch_pdl(k_tc_stage, dim3(nlog), dim3(256), 0, s, E->t_x + (size_t)lrow0 * dim, dim,
+    launch_pdl(stage_fn, dim3(nlog), dim3(256), 0, s, E->t_x + (size_t)lrow0 * dim, dim,
                E->t_part + (size_t)lrow0 * dim, d_splits, part_stride, E->final_norm, dim, E->img_d);
     tc_launch(E, E->tc_lm, E->img_d, nlog, 1, rows(lg_out, (int)E->vocab, (int)E->vocab, 0));
     if (!logits_out) {
@@ -2212,7 +2215,7 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     cudaMemsetAsync(err, 0, 16, s);
     QMat W{nibbles, step_bf16, min_bf16, N, K};
     k_tc_repack<<<sms * 8, 256, 0, s>>>(W, recs, 0, kM, 0, 1);
-    k_tc_stage<<<dim3(M, K / 2048), 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, K, img);
+    k_tc_stage<false><<<dim3(M, K / 2048), 256, 0, s>>>(const_cast<float*>(x), K, nullptr, 0, 0, nullptr, K, img);
     Args A{};
     A.recs = recs;
     A.img = img;

@@ -601,6 +601,9 @@ __global__ void k_tc_repack(QMat W, uint8_t* __restrict__ recs, int row0, int G,
 // K is a multiple of 2048; a thread handles runs of 8 consecutive elements.  Without gamma the
 // grid is (tokens, K / 2048), one 2048-wide run per CTA; with gamma (tokens, 1).
 // ---------------------------------------------------------------------------------------------
+// kAllPlanes: all split-K planes' loads in flight at once (one round trip; more registers, so for
+// steps of few rows, where latency matters more than occupancy), else three at a time.
+template <bool kAllPlanes>
 __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx, const float* __restrict__ part,
                                                   int nsplit, size_t split_stride, const float* __restrict__ gamma,
                                                   int K, uint8_t* __restrict__ img) {
@@ -630,9 +633,27 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
           const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
           s8[0] = p0.x; s8[1] = p0.y; s8[2] = p0.z; s8[3] = p0.w; s8[4] = p1.x; s8[5] = p1.y; s8[6] = p1.z; s8[7] = p1.w;
         }
-        // planes in order, three planes' loads in flight at a time
+        // planes in order
         int sp = 1;
-        for (; sp + 2 < nsplit; sp += 3) {
+        if (kAllPlanes && nsplit <= 8) {
+          float4 q[7][2];
+#pragma unroll
+          for (int j = 0; j < 7; ++j) {
+            if (1 + j < nsplit) {
+              q[j][0] = *reinterpret_cast<const float4*>(pp + (1 + j) * split_stride);
+              q[j][1] = *reinterpret_cast<const float4*>(pp + (1 + j) * split_stride + 4);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 7; ++j) {
+            if (1 + j < nsplit) {
+              s8[0] += q[j][0].x; s8[1] += q[j][0].y; s8[2] += q[j][0].z; s8[3] += q[j][0].w;
+              s8[4] += q[j][1].x; s8[5] += q[j][1].y; s8[6] += q[j][1].z; s8[7] += q[j][1].w;
+            }
+          }
+          sp = nsplit;
+        }
+        for (; sp + 2 < nsplit; sp += 3) {  // three planes' loads in flight at a time
           float4 q[3][2];
 #pragma unroll
           for (int j = 0; j < 3; ++j) {
