@@ -145,6 +145,15 @@ struct TcLayer {
   TcMat qkv, o, gu, d;
 };
 constexpr int kTcMaxSplits = 8;
+constexpr int kTcPairRows = 1024;  // steps of at least this many rows run two-tile GEMM units
+// Two-tile GEMM units for large steps, on unless $LLAMA_B200_TC_PAIR is "0" (read once).
+static bool tc_pair_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LLAMA_B200_TC_PAIR");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
 constexpr int kExpireAttn = 20;  // llama_engine_debug_waits code that expires only the prefill attention
 constexpr int kAttnMaxSplits = 8;
 constexpr int kScoreRows = 256;  // rows of logits held at once by llama_engine_score_tokens
@@ -816,12 +825,14 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaMalloc(&E->t_am, (size_t)T * E->tc_am_parts * sizeof(ArgmaxPart)));
   LE_CK(cudaMalloc(&E->tc_err, 16));
   LE_CK(cudaMemsetAsync(E->tc_err, 0, 16, E->stream));
-  LE_CK(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  LE_CK(cudaFuncSetAttribute(k_tc_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<1>::kSmemBytes));
+  LE_CK(cudaFuncSetAttribute(k_tc_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<2>::kSmemBytes));
   LE_CK(cudaFuncSetAttribute(k_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
   LE_CK(cudaFuncSetAttribute(k_attn_prefill_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
-  int per_sm = 0;
-  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm, tc::kThreads, kSmemBytes));
-  if (per_sm < 1) {
+  int per_sm = 0, per_sm2 = 0;
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm<1>, tc::kThreads, Geo<1>::kSmemBytes));
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm2, k_tc_gemm<2>, tc::kThreads, Geo<2>::kSmemBytes));
+  if (std::min(per_sm, per_sm2) < 1) {
     E->err = "tensor-core GEMM declined: 0 resident CTAs per SM";
     return true;
   }
@@ -865,13 +876,19 @@ static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
-// Launches one tensor-core GEMM over T token rows of `img`; returns the number of K splits used.
+// Launches one tensor-core GEMM over T token rows of `img`; returns the number of K splits used
+// (splits < 0: chosen for the shape).  Steps of at least kTcPairRows rows run units of two token
+// tiles (the issuer's per-block cost is then shared by 128 tokens); smaller steps keep one-tile
+// units, whose count fills more SMs.
 static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int splits, tc::Args A) {
+  const int P = (T >= kTcPairRows && tc_pair_enabled()) ? 2 : 1;
   A.recs = W.recs;
   A.img = img;
   A.tiles = W.tiles;
   A.kb_total = W.kb;
-  A.tok_tiles = (T + tc::kTok - 1) / tc::kTok;
+  A.img_tiles = (T + tc::kTok - 1) / tc::kTok;
+  A.tok_tiles = (A.img_tiles + P - 1) / P;
+  if (splits < 0) splits = tc_splits(E, W, A.tok_tiles);
   A.T = T;
   A.kb_split = (W.kb + splits - 1) / splits;
   A.splits = (W.kb + A.kb_split - 1) / A.kb_split;
@@ -879,7 +896,12 @@ static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int s
   A.wait_ns = E->tc_wait_ns;
   A.expire = E->tc_expire;
   const int units = A.tiles * A.tok_tiles * A.splits;
-  launch_pdl(tc::k_tc_gemm, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::kSmemBytes, E->stream, A);
+  if (P == 2)
+    launch_pdl(tc::k_tc_gemm<2>, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::Geo<2>::kSmemBytes,
+               E->stream, A);
+  else
+    launch_pdl(tc::k_tc_gemm<1>, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::Geo<1>::kSmemBytes,
+               E->stream, A);
   return A.splits;
 }
 
@@ -921,7 +943,6 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
   const int32_t* tok = E->t_idx;
   const int32_t* pos = E->t_idx + n;
   const int32_t* slot = E->t_idx + 2 * n;
-  const int tok_tiles = (n + kTok - 1) / kTok;
   const int attn_splits = attn_splits_for(max_pos);
   cudaStream_t s = E->stream;
   auto rows = [&](float* out, int ldo, int N, size_t split_stride) {
@@ -945,7 +966,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     launch_pdl(stage_fn, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, d_splits, part_stride, D.in_norm, dim,
                E->img_d);
     const size_t qkv_stride = (size_t)E->tc_T * (dim + 2 * kvd);
-    const int sq = tc_launch(E, Y.qkv, E->img_d, n, tc_splits(E, Y.qkv, tok_tiles),
+    const int sq = tc_launch(E, Y.qkv, E->img_d, n, -1,
                              rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
     if (prefill_p0 >= 0 || !fold)
       launch_pdl(k_rope_append, dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), dim3(256), 0, s, E->t_qkv, sq, qkv_stride,
@@ -970,7 +991,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     if (prefill_p0 >= 0 || attn_splits > 1)
       launch_pdl(stage_fn, dim3(n, dim / 2048), dim3(256), 0, s, E->t_attn, dim, nullptr, 0, 0, nullptr, dim,
                  E->img_d);
-    const int so = tc_launch(E, Y.o, E->img_d, n, tc_splits(E, Y.o, tok_tiles), rows(E->t_part, dim, dim, part_stride));
+    const int so = tc_launch(E, Y.o, E->img_d, n, -1, rows(E->t_part, dim, dim, part_stride));
     launch_pdl(stage_fn, dim3(n), dim3(256), 0, s, E->t_x, dim, E->t_part, so, part_stride, D.post_norm, dim,
                E->img_d);
     Args Agu = rows(E->t_gu, ffn, ffn, 0);
@@ -978,7 +999,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     tc_launch(E, Y.gu, E->img_d, n, 1, Agu);
     launch_pdl(stage_fn, dim3(n, ffn / 2048), dim3(256), 0, s, E->t_gu, ffn, nullptr, 0, 0, nullptr, ffn,
                E->img_f);
-    d_splits = tc_launch(E, Y.d, E->img_f, n, tc_splits(E, Y.d, tok_tiles), rows(E->t_part, dim, dim, part_stride));
+    d_splits = tc_launch(E, Y.d, E->img_f, n, -1, rows(E->t_part, dim, dim, part_stride));
   }
   if (nlog > 0) {
     launch_pdl(stage_fn, dim3(nlog), dim3(256), 0, s, E->t_x + (size_t)lrow0 * dim, dim,
@@ -2208,8 +2229,13 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
   if (cudaMalloc(&recs, rec_bytes) == cudaSuccess && cudaMalloc(&img, img_bytes) == cudaSuccess &&
       cudaMalloc(&err, 16) == cudaSuccess) {
     static bool attr = false;
-    if (!attr) attr = cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) ==
-                      cudaSuccess;
+    if (!attr)
+      attr = cudaFuncSetAttribute(k_tc_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<1>::kSmemBytes) ==
+                 cudaSuccess &&
+             cudaFuncSetAttribute(k_tc_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<2>::kSmemBytes) ==
+                 cudaSuccess;
+    // units of two token tiles from kTcPairRows rows, as in the engine's steps
+    const int P = (M >= kTcPairRows && tc_pair_enabled()) ? 2 : 1;
     cudaMemsetAsync(recs, 0, rec_bytes, s);
     cudaMemsetAsync(img, 0, img_bytes, s);
     cudaMemsetAsync(err, 0, 16, s);
@@ -2221,7 +2247,8 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     A.img = img;
     A.tiles = tiles;
     A.kb_total = kb;
-    A.tok_tiles = tok_tiles;
+    A.img_tiles = tok_tiles;
+    A.tok_tiles = (tok_tiles + P - 1) / P;
     A.splits = 1;
     A.kb_split = kb;
     A.T = M;
@@ -2238,7 +2265,11 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
       cudaMemsetAsync(trace, 0, trace_bytes, s);
       A.trace = trace;
     }
-    k_tc_gemm<<<std::min(tiles * tok_tiles, sms), tc::kThreads, kSmemBytes, s>>>(A);
+    const int grid = std::min(tiles * A.tok_tiles, sms);
+    if (P == 2)
+      k_tc_gemm<2><<<grid, tc::kThreads, Geo<2>::kSmemBytes, s>>>(A);
+    else
+      k_tc_gemm<1><<<grid, tc::kThreads, Geo<1>::kSmemBytes, s>>>(A);
     if (trace) {
       std::vector<unsigned long long> h(trace_bytes / 8);
       if (cudaMemcpyAsync(h.data(), trace, trace_bytes, cudaMemcpyDeviceToHost, s) == cudaSuccess &&

@@ -58,28 +58,53 @@ constexpr int kNibBytes = kM * 64;       // nibbles of one (tile, K block)
 constexpr int kRecBytes = kNibBytes + kM * 4;
 constexpr int kAtom = kTok * 128;        // one 64-wide K slice of 64 token rows (bf16, swizzled)
 constexpr int kImgBytes = 4 * kAtom + kTok * 4;  // activation image of one (token tile, K block)
-constexpr int kOffXs = 4 * kAtom;        // stage: hi0 | lo0 | hi1 | lo1 | xs | record
-constexpr int kOffRec = kImgBytes;
-constexpr int kStageTx = kImgBytes + kRecBytes;
-constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
-constexpr int kStages = 5;
-constexpr int kSide = 8;                 // side ring: per block the rows' scales and the block sums
-constexpr int kSideBytes = kM * 4 + kTok * 4;
+constexpr int kOffXs = 4 * kAtom;        // image: hi0 | lo0 | hi1 | lo1 | xs
 constexpr int kWarps = 19;               // 0 producer, 1 MMA issuer, 2 idle, 3-10 dequantisers, 11-18 epilogue
 constexpr int kThreads = 32 * kWarps;
 constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64 columns each)
-constexpr int kBufsD = 2;                // accumulator buffers (128 columns: hi | lo tokens)
+constexpr int kBufsD = 2;                // accumulator buffers (128 columns)
 constexpr int kTmemCols = 512;
 constexpr int kDCol = kBufsA * 64;
 constexpr uint32_t kSleepNs = 20000;    // suspend hint of a pending wait (the bound is checked between)
 constexpr int kPrefetch = 8;             // records prefetched into L2 this many blocks ahead
-constexpr int kNumBars = 2 * kStages + kBufsA + kBufsD + 2 * kSide + 1;
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kSide * kSideBytes + (kNumBars * 8 + 63) / 64 * 64;
+
+// Shared-memory geometry for work units of P 64-token tiles.
+//   P = 1 (decode-sized steps): a stage is one tile's activation image as stored (hi0 | lo0 |
+//   hi1 | lo1 | xs), then the weight record; 5 stages, 8 side slots.  The MMA's B operand for a
+//   16-wide K step is the tile's hi rows stacked on its lo rows (N = 128): accumulator columns
+//   t and 64 + t hold token t's x_hi and x_lo products.
+//   P = 2 (prefill-sized steps): a stage holds two tiles' images regrouped so that each 64-wide
+//   K slice of hi (or lo) parts is one 128-row B operand: hi atoms [K 0..63: tile 0 | tile 1]
+//   [K 64..127: tile 0 | tile 1], the lo atoms likewise, the two tiles' block sums, then the
+//   record; two MMAs per 16-wide K step (x_hi, then x_lo, N = 128 tokens) accumulate into one
+//   column per token, so the issuer's per-block bookkeeping serves twice the tokens.  3 stages
+//   and 3 side slots are what fit.
+template <int P>
+struct Geo {
+  static constexpr int kUnitTok = P * kTok;                   // tokens per unit
+  static constexpr int kOffLo = P == 1 ? kAtom : 4 * kAtom;   // first lo atom of a stage
+  static constexpr int kOffXs = P == 1 ? 4 * kAtom : 8 * kAtom;
+  static constexpr int kOffRec = kOffXs + kUnitTok * 4;
+  static constexpr int kStageTx = kOffRec + kRecBytes;
+  static constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
+  static constexpr int kStages = P == 1 ? 5 : 3;
+  static constexpr int kSide = P == 1 ? 8 : 3;  // side ring: per block the rows' scales and block sums
+  static constexpr int kSideBytes = kM * 4 + kUnitTok * 4;
+  static constexpr int kNumBars = 2 * kStages + kBufsA + kBufsD + 2 * kSide + 1;
+  // 1024 bytes of slack to align the dynamic base (the swizzled operands need 1024-byte atoms)
+  static constexpr int kSmemBytes =
+      1024 + kStages * kStageBytes + kSide * kSideBytes + (kNumBars * 8 + 63) / 64 * 64;
+};
+static_assert(Geo<1>::kOffRec == kImgBytes, "a one-tile stage starts with the image as stored");
+// dynamic plus the kernel's 1 KB of static shared memory, within the 232448 bytes a CTA may opt into
+static_assert(Geo<1>::kSmemBytes + 1024 <= 232448 && Geo<2>::kSmemBytes + 1024 <= 232448,
+              "stages must fit one CTA's shared memory");
 
 struct Args {
   const uint8_t* recs;   // [tiles][kb_total][kRecBytes]
-  const uint8_t* img;    // [tok_tiles][kb_total][kImgBytes]
-  int tiles, kb_total, tok_tiles, splits, kb_split;
+  const uint8_t* img;    // [img_tiles][kb_total][kImgBytes]
+  int tiles, kb_total, tok_tiles, splits, kb_split;  // tok_tiles: token groups (P tiles each)
+  int img_tiles;         // 64-token tiles held by img (a unit's second tile may lie past them)
   int T;                 // valid tokens
   int N;                 // valid output rows
   float* out;            // out[split * split_stride + t * ldo + n]
@@ -192,29 +217,44 @@ __device__ __forceinline__ uint32_t nib_pair_bf16(uint32_t w, uint32_t w4) {
   return r;
 }
 
+template <int P>
 struct Shared {
   uint32_t base;   // 1024-aligned shared address of stage 0
   uint32_t side;   // side ring
   uint32_t bar;    // barriers
 };
-// barrier index layout: full[S] done[S] afull[BA] dempty[BD] sfull[8] sempty[8] final.
+// barrier index layout: full[S] done[S] afull[BA] dempty[BD] sfull[side] sempty[side] final.
 // done[g % S] completes when the MMAs of block g have: the stage, the A buffer of block g and
 // its accumulator are then free or ready (one tcgen05.commit serves all three).
-__device__ __forceinline__ uint32_t bar_full(const Shared& S, int s) { return S.bar + 8 * s; }
-__device__ __forceinline__ uint32_t bar_done(const Shared& S, int s) { return S.bar + 8 * (kStages + s); }
-__device__ __forceinline__ uint32_t bar_afull(const Shared& S, int b) { return S.bar + 8 * (2 * kStages + b); }
-__device__ __forceinline__ uint32_t bar_dempty(const Shared& S, int b) {
-  return S.bar + 8 * (2 * kStages + kBufsA + b);
+template <int P>
+__device__ __forceinline__ uint32_t bar_full(const Shared<P>& S, int s) { return S.bar + 8 * s; }
+template <int P>
+__device__ __forceinline__ uint32_t bar_done(const Shared<P>& S, int s) {
+  return S.bar + 8 * (Geo<P>::kStages + s);
 }
-__device__ __forceinline__ uint32_t bar_sfull(const Shared& S, int j) {
-  return S.bar + 8 * (2 * kStages + kBufsA + kBufsD + j);
+template <int P>
+__device__ __forceinline__ uint32_t bar_afull(const Shared<P>& S, int b) {
+  return S.bar + 8 * (2 * Geo<P>::kStages + b);
 }
-__device__ __forceinline__ uint32_t bar_sempty(const Shared& S, int j) {
-  return S.bar + 8 * (2 * kStages + kBufsA + kBufsD + kSide + j);
+template <int P>
+__device__ __forceinline__ uint32_t bar_dempty(const Shared<P>& S, int b) {
+  return S.bar + 8 * (2 * Geo<P>::kStages + kBufsA + b);
+}
+template <int P>
+__device__ __forceinline__ uint32_t bar_sfull(const Shared<P>& S, int j) {
+  return S.bar + 8 * (2 * Geo<P>::kStages + kBufsA + kBufsD + j);
+}
+template <int P>
+__device__ __forceinline__ uint32_t bar_sempty(const Shared<P>& S, int j) {
+  return S.bar + 8 * (2 * Geo<P>::kStages + kBufsA + kBufsD + Geo<P>::kSide + j);
 }
 // Parity of the completion of done[] that belongs to block g.
-__device__ __forceinline__ uint32_t done_parity(int g) { return (uint32_t)(g / kStages) & 1u; }
-__device__ __forceinline__ uint32_t bar_final(const Shared& S) { return S.bar + 8 * (kNumBars - 1); }
+template <int P>
+__device__ __forceinline__ uint32_t done_parity(const Shared<P>&, int g) {
+  return (uint32_t)(g / Geo<P>::kStages) & 1u;
+}
+template <int P>
+__device__ __forceinline__ uint32_t bar_final(const Shared<P>& S) { return S.bar + 8 * (Geo<P>::kNumBars - 1); }
 
 // Bounded wait on an mbarrier phase.  Returns false when the launch has failed (here or in
 // another role); the first timeout records `where`.
@@ -300,26 +340,28 @@ __device__ __forceinline__ int cta_blocks(const Args& A, int n_units) {
 // 3..10 = dequantisers, 11..18 = epilogue.  A warp may only touch tensor-memory lanes 32 * (warp % 4) .. +31, so each group of
 // four covers the 128 rows once; the two dequantiser groups take alternate blocks, the two
 // epilogue groups the two halves of the token tile.
+template <int P>
 __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
+  using Gm = Geo<P>;
   extern __shared__ __align__(1024) uint8_t tc_smem[];
   __shared__ uint32_t s_tmem;
   __shared__ volatile uint32_t s_abort;
-  Shared S;
+  Shared<P> S;
   S.base = (smem_u32(tc_smem) + 1023u) & ~1023u;
-  S.side = S.base + kStages * kStageBytes;
-  S.bar = S.side + kSide * kSideBytes;
+  S.side = S.base + Gm::kStages * Gm::kStageBytes;
+  S.bar = S.side + Gm::kSide * Gm::kSideBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = A.tiles * A.tok_tiles * A.splits;
 
   if (threadIdx.x == 0) {
     s_abort = 0u;
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < Gm::kStages; ++s) {
       mbar_init(bar_full(S, s), 1);
       mbar_init(bar_done(S, s), 1);
     }
     for (int b = 0; b < kBufsA; ++b) mbar_init(bar_afull(S, b), 4);
     for (int b = 0; b < kBufsD; ++b) mbar_init(bar_dempty(S, b), 8);
-    for (int j = 0; j < kSide; ++j) {
+    for (int j = 0; j < Gm::kSide; ++j) {
       mbar_init(bar_sfull(S, j), 4);
       mbar_init(bar_sempty(S, j), 8);
     }
@@ -350,13 +392,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       grid_dep_wait();  // the weight records are constant; the activation image is not
       int g = 0;
       for (; c.valid(n_units) && !s_abort; c.next(A, n_units), ++g) {
-        const int s = g % kStages;
-        if (g >= kStages && !wait_bar(A, &s_abort, bar_done(S, s), done_parity(g - kStages), 1)) break;
-        const uint32_t st = S.base + s * kStageBytes;
+        const int s = g % Gm::kStages;
+        if (g >= Gm::kStages && !wait_bar(A, &s_abort, bar_done(S, s), done_parity(S, g - Gm::kStages), 1)) break;
+        const uint32_t st = S.base + s * Gm::kStageBytes;
         const uint32_t fb = bar_full(S, s);
-        mbar_expect_tx(fb, kStageTx);
-        bulk_g2s(st, A.img + ((size_t)c.U.tt * A.kb_total + c.kb) * kImgBytes, kImgBytes, fb);
-        bulk_g2s(st + kOffRec, A.recs + ((size_t)c.U.tile * A.kb_total + c.kb) * kRecBytes, kRecBytes, fb);
+        mbar_expect_tx(fb, Gm::kStageTx);
+        if (P == 1) {
+          bulk_g2s(st, A.img + ((size_t)c.U.tt * A.kb_total + c.kb) * kImgBytes, kImgBytes, fb);
+        } else {
+          // the group's two tiles, atoms regrouped so that each K slice's hi (lo) parts of both
+          // tiles form one 128-row B operand; a second tile past the image (an odd tile count)
+          // repeats the first, whose rows the epilogue then does not store
+          const int t0 = 2 * c.U.tt, t1 = min(t0 + 1, A.img_tiles - 1);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const uint8_t* im = A.img + ((size_t)(t ? t1 : t0) * A.kb_total + c.kb) * kImgBytes;
+#pragma unroll
+            for (int kh = 0; kh < 2; ++kh) {
+              bulk_g2s(st + (2 * kh + t) * kAtom, im + 2 * kh * kAtom, kAtom, fb);
+              bulk_g2s(st + Gm::kOffLo + (2 * kh + t) * kAtom, im + (2 * kh + 1) * kAtom, kAtom, fb);
+            }
+            bulk_g2s(st + Gm::kOffXs + t * kTok * 4, im + kOffXs, kTok * 4, fb);
+          }
+        }
+        bulk_g2s(st + Gm::kOffRec, A.recs + ((size_t)c.U.tile * A.kb_total + c.kb) * kRecBytes, kRecBytes, fb);
         trace_ev(A, 0, g);
         if (ahead.valid(n_units)) {
           prefetch_l2(A.recs + ((size_t)ahead.U.tile * A.kb_total + ahead.kb) * kRecBytes, kRecBytes);
@@ -365,9 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       }
       // drain: every issued stage must have landed before the CTA may exit
       const int issued = g;
-      for (int s = 0; s < kStages && s < issued; ++s) {
-        const int last = issued - 1 - ((issued - 1 - s) % kStages);  // last fill of stage s
-        wait_bar_drain(A, &s_abort, bar_full(S, s), (last / kStages) & 1, 2);
+      for (int s = 0; s < Gm::kStages && s < issued; ++s) {
+        const int last = issued - 1 - ((issued - 1 - s) % Gm::kStages);  // last fill of stage s
+        wait_bar_drain(A, &s_abort, bar_full(S, s), (last / Gm::kStages) & 1, 2);
       }
     }
   } else if (warp == 1) {
@@ -375,11 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     if (lane == 0) {
       // ---------------- MMA issuer (one thread issues every MMA of the CTA) ----------------
       // Issuing from two threads that take alternate blocks was measured to corrupt an occasional
-      // block, so a single thread issues all MMAs.  One MMA (N = 128) per 16-wide K step: B rows
-      // 0..63 are the tokens' hi parts, rows 64..127 their lo parts (the adjacent atoms), so D
-      // columns 0..63 and 64..127 accumulate q . x_hi and q . x_lo.  The loop is kept short: it
-      // runs on a sub-partition shared with busy dequant and epilogue warps.
-      const uint32_t idesc = idesc_bf16(2 * kTok);
+      // block, so a single thread issues all MMAs.  P = 1: one MMA (N = 128) per 16-wide K step,
+      // B rows 0..63 the tokens' hi parts and rows 64..127 their lo parts (the adjacent atoms),
+      // so D columns 0..63 and 64..127 accumulate q . x_hi and q . x_lo.  P = 2: two MMAs
+      // (N = 128 tokens) per K step, B = the 128 tokens' hi parts, then their lo parts, both into
+      // D column t.  The loop is kept short: it runs on a sub-partition shared with busy dequant
+      // and epilogue warps.
+      const uint32_t idesc = idesc_bf16(128);
       const int nblk = cta_blocks(A, n_units);
       const uint32_t desc_hi = (uint32_t)(sw128_desc(0) >> 32);
       const uint32_t desc_lo0 = (uint32_t)sw128_desc(S.base);
@@ -387,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       // this wait runs out and the launch takes its error path
       if (A.expire) wait_bar(A, &s_abort, bar_final(S), 0, 13);
       for (int g = 0; g < nblk; ++g) {
-        const int s = g % kStages, n = g / kStages;
+        const int s = g % Gm::kStages, n = g / Gm::kStages;
         const int ba = g % kBufsA, na = g / kBufsA, bd = g % kBufsD, nd = g / kBufsD;
         // The issuer waits for the stage's bulk copies itself: the MMAs read the stage through the
         // async proxy, and the copies' completion is only guaranteed visible to them through this
@@ -405,13 +466,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         if (!ok) break;
         trace_ev(A, 1, g);
         tc_fence_after();
-        const uint32_t dl = desc_lo0 + (uint32_t)(s * (kStageBytes >> 4));
-        const uint32_t d = tmem + kDCol + bd * 2 * kTok;
+        const uint32_t dl = desc_lo0 + (uint32_t)(s * (Gm::kStageBytes >> 4));
+        const uint32_t d = tmem + kDCol + bd * 128;
         const uint32_t a_t = tmem + ba * 64;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
+          // K slice k >> 2's hi rows start 2 atoms further on, a 16-wide step is 32 bytes of a row
           const uint32_t kl = dl + (uint32_t)((((k >> 2) * 2 * kAtom) + (k & 3) * 32) >> 4);
           tc_mma_ts(d, a_t + 8 * k, ((uint64_t)desc_hi << 32) | kl, idesc, k > 0);
+          if (P == 2)
+            tc_mma_ts(d, a_t + 8 * k, ((uint64_t)desc_hi << 32) | (kl + (uint32_t)(Gm::kOffLo >> 4)), idesc, 1u);
         }
         trace_ev(A, 6, g);
         tc_commit(bar_done(S, s));
@@ -433,18 +497,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int sw = (r >> 1) & 3;
     const int nblk = cta_blocks(A, n_units);
+    // A[b] is free once the MMAs of block g - kBufsA have completed.  The wait is on block
+    // g - kFreeA: commits complete in issue order, so its completion implies that of g - kBufsA,
+    // and the next phase of its done barrier is block g's own (kFreeA <= kStages), which cannot
+    // complete before this warp has written A.  With fewer stages than A buffers, block
+    // g - kBufsA's barrier would alias: the other set's block g - 1 reuses it and can complete
+    // it again before this wait starts.
+    constexpr int kFreeA = Gm::kStages < kBufsA ? Gm::kStages : kBufsA;
     for (int g = h; g < nblk; g += 2) {
-      const int s = g % kStages, n = g / kStages, b = g % kBufsA;
-      const int j = g % kSide, nj = g / kSide;
-      // A[b] is free once the MMAs of block g - kBufsA have completed; side slot j once the
-      // epilogue has read block g - kSide
+      const int s = g % Gm::kStages, n = g / Gm::kStages, b = g % kBufsA;
+      const int j = g % Gm::kSide, nj = g / Gm::kSide;
+      // side slot j is free once the epilogue has read block g - kSide
       if (!warp_wait(A, &s_abort, bar_full(S, s), n & 1, 8) ||
-          (g >= kBufsA && !warp_wait(A, &s_abort, bar_done(S, (g - kBufsA) % kStages), done_parity(g - kBufsA), 10)) ||
-          (g >= kSide && !warp_wait(A, &s_abort, bar_sempty(S, j), (nj - 1) & 1, 11)))
+          (g >= kFreeA &&
+           !warp_wait(A, &s_abort, bar_done(S, (g - kFreeA) % Gm::kStages), done_parity(S, g - kFreeA), 10)) ||
+          (g >= Gm::kSide && !warp_wait(A, &s_abort, bar_sempty(S, j), (nj - 1) & 1, 11)))
         break;
       if (warp == 3 || warp == 7) trace_ev(A, 2, g);
-      const uint32_t st = S.base + s * kStageBytes;
-      const uint32_t rec = st + kOffRec + 64 * r;
+      const uint32_t st = S.base + s * Gm::kStageBytes;
+      const uint32_t rec = st + Gm::kOffRec + 64 * r;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const uint4 c0 = lds128(rec + (uint32_t)(((2 * half) ^ sw) << 4));
@@ -461,14 +532,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         }
         tmem_st32(tmem + lane_base + b * 64 + 32 * half, v);
       }
-      // scales of this row and (one warp) the 64 block sums into side slot j
-      const uint32_t sd = S.side + j * kSideBytes;
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sd + 4 * r), "r"(lds32(st + kOffRec + kNibBytes + 4 * r))
+      // scales of this row and (one warp) the unit's block sums into side slot j
+      const uint32_t sd = S.side + j * Gm::kSideBytes;
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sd + 4 * r), "r"(lds32(st + Gm::kOffRec + kNibBytes + 4 * r))
                    : "memory");
       if (q == 0) {
-        const uint2 x2 = lds64(st + kOffXs + 8 * lane);
-        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(sd + kM * 4 + 8 * lane), "r"(x2.x), "r"(x2.y)
-                     : "memory");
+        if (P == 1) {
+          const uint2 x2 = lds64(st + Gm::kOffXs + 8 * lane);
+          asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(sd + kM * 4 + 8 * lane), "r"(x2.x), "r"(x2.y)
+                       : "memory");
+        } else {
+          const uint4 x4 = lds128(st + Gm::kOffXs + 16 * lane);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(sd + kM * 4 + 16 * lane), "r"(x4.x),
+                       "r"(x4.y), "r"(x4.z), "r"(x4.w)
+                       : "memory");
+        }
       }
       tmem_wait_st();
       tc_fence_before();
@@ -481,31 +559,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     }
   } else {
     // ---------------- epilogue: per-block scales in fp32, unit results ----------------
-    // warp (q, h): rows 32q .. 32q+31, tokens 32h .. 32h+31 of the token tile
+    // warp (q, h): rows 32q .. 32q+31, the unit's tokens kHalf h .. kHalf h + kHalf - 1
     const int q = warp & 3, h = (warp - 11) >> 2;
     const int r = 32 * q + lane;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    constexpr int kHalf = kTok / 2;
+    constexpr int kHalf = Gm::kUnitTok / 2;
     float acc[kHalf];
 #pragma unroll
     for (int i = 0; i < kHalf; ++i) acc[i] = 0.0f;
     Cursor c;
     c.start(A, n_units);
     for (int g = 0; c.valid(n_units); c.next(A, n_units), ++g) {
-      const int b = g % kBufsD, j = g % kSide, nj = g / kSide;
-      if (!warp_wait(A, &s_abort, bar_done(S, g % kStages), done_parity(g), 7) ||
+      const int b = g % kBufsD, j = g % Gm::kSide, nj = g / Gm::kSide;
+      if (!warp_wait(A, &s_abort, bar_done(S, g % Gm::kStages), done_parity(S, g), 7) ||
           !warp_wait(A, &s_abort, bar_sfull(S, j), nj & 1, 12))
         break;
       if (warp == 11) trace_ev(A, 4, g);
       tc_fence_after();
-      const uint32_t sd = S.side + j * kSideBytes;
+      const uint32_t sd = S.side + j * Gm::kSideBytes;
       const uint32_t sc = lds32(sd + 4 * r);
       const float step = bf16_bits_to_f32(sc & 0xFFFFu), mn = bf16_bits_to_f32(sc >> 16);
 #pragma unroll
       for (int cc = 0; cc < kHalf / 16; ++cc) {
+        // P = 1: token i's x_hi and x_lo products in columns i and 64 + i; P = 2: their sum in i
         uint32_t dv[16], dw[16];
-        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kHalf * h + 16 * cc, dv);
-        tmem_ld16(tmem + lane_base + kDCol + b * 2 * kTok + kTok + kHalf * h + 16 * cc, dw);
+        const uint32_t dcol = tmem + lane_base + kDCol + b * 128 + kHalf * h + 16 * cc;
+        tmem_ld16(dcol, dv);
+        if (P == 1) tmem_ld16(dcol + kTok, dw);
         tmem_wait_ld();
         if (cc == kHalf / 16 - 1) {
           tc_fence_before();
@@ -520,7 +600,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             float& a = acc[16 * cc + i + jj];
-            a = fmaf(step, __uint_as_float(dv[i + jj]) + __uint_as_float(dw[i + jj]), fmaf(mn, xs[jj], a));
+            const float dq = P == 1 ? __uint_as_float(dv[i + jj]) + __uint_as_float(dw[i + jj])
+                                    : __uint_as_float(dv[i + jj]);
+            a = fmaf(step, dq, fmaf(mn, xs[jj], a));
           }
         }
       }
@@ -539,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
           n = c.U.tile * (kM / 2) + (r >> 1);
           store = (r & 1) == 0;
         }
-        const int tok0 = c.U.tt * kTok + kHalf * h;
+        const int tok0 = c.U.tt * Gm::kUnitTok + kHalf * h;
         const int nt = min(kHalf, A.T - tok0);
         float* o = A.out + (size_t)c.U.split * A.split_stride + (size_t)tok0 * A.ldo + n;
         if (store && n < A.N) {

@@ -74,7 +74,10 @@ def _abs_scale(pkg, step, mn, N, K, X):
 
 @pytest.mark.parametrize("K,N,M", [(2048, 2048, 1), (2048, 2048, 64), (2048, 320, 17), (8192, 2048, 64),
                                    (2048, 512, 100), (8192, 384, 130), (2048, 128256, 64),
-                                   (2048, 8192, 1024)])  # a prefill chunk through the gate/up shape
+                                   (2048, 8192, 1024),  # a prefill chunk through the gate/up shape
+                                   # two-tile units: an odd tile count (the last unit's second tile
+                                   # repeats its first) and ragged rows over a long K
+                                   (2048, 2048, 1050), (8192, 384, 1100)])
 def test_tc_gemm_vs_oracle(pkg, bindings, oracle_lib, torch_cuda, K, N, M):
     torch = torch_cuda
     nib, step, mn = pkg.model_file.gen_matrix(N, K, seed=300 + K + N, tensor=3, uniform_codes=True)
