@@ -12,6 +12,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -213,7 +214,8 @@ struct Engine {
   uint32_t* d_recs = nullptr;
   float* d_norms = nullptr;  // [2*layers + 1][dim] contiguous copy of the norm weights
   unsigned long long* d_tagged = nullptr;  // x | qkv | attn | act as (value, phase tag) words
-  PCtrl* d_ctrl = nullptr;
+  uint8_t* ctrl_block = nullptr;  // PCtrl, then am_result [max_batch]
+  PCtrl* d_ctrl = nullptr;        // the start of ctrl_block (persistent kernel only)
   uint32_t* h_err = nullptr;  // pinned mirror of PCtrl::error / err_where
   unsigned long long* d_trace = nullptr;  // optional phase trace of the persistent kernel
   PArgs pargs{};
@@ -700,7 +702,7 @@ static bool init_persistent(Engine* E) {
   const size_t n_tagged = (size_t)E->dim + (E->dim + 2 * E->kv_dim) + E->dim + E->ffn;
   LE_CK(cudaMalloc(&E->d_tagged, n_tagged * sizeof(unsigned long long)));
   LE_CK(cudaMemset(E->d_tagged, 0, n_tagged * sizeof(unsigned long long)));  // tag 0 is never valid
-  LE_CK(cudaMalloc(&E->d_ctrl, sizeof(PCtrl)));
+  E->d_ctrl = reinterpret_cast<PCtrl*>(E->ctrl_block);  // am_result follows it (greedy())
   LE_CK(cudaMemset(E->d_ctrl, 0, sizeof(PCtrl)));
   PArgs& A = E->pargs;
   A.arena = E->rec_arena;
@@ -713,7 +715,7 @@ static bool init_persistent(Engine* E) {
   A.act = A.attn + E->dim;
   A.logits = E->logits;
   A.kcache = E->kcache; A.vcache = E->vcache;
-  A.ctrl = E->d_ctrl; A.prm = E->d_params;
+  A.ctrl = E->d_ctrl;
   A.token_log = E->token_log; A.am_result = E->am_result;
   A.lm_rec_base = (unsigned long long)lm_base * kRecBytes;
   A.wait_ns = kWaitNs;
@@ -721,6 +723,7 @@ static bool init_persistent(Engine* E) {
   A.heads = (int)E->heads; A.kv_heads = (int)E->kv_heads; A.max_seq = E->max_seq;
   A.n_lm_ctas = n_lm_ctas;
   A.n_tokens = 1; A.do_logits = 1;
+  A.token0 = 0; A.pos0 = 0;
   A.expire_where = 0;
   E->p_grid = G;
   LE_CK(cudaStreamSynchronize(E->stream));
@@ -728,11 +731,14 @@ static bool init_persistent(Engine* E) {
   return true;
 }
 
-// One cooperative launch of n_tokens steps on slot 0 (parameters already queued).
-static bool launch_persistent(Engine* E, int n_tokens, bool logits) {
+// One cooperative launch of n_tokens steps on slot 0 from (token, pos); the token and position
+// are kernel arguments, so a step needs no parameter copy.
+static bool launch_persistent(Engine* E, int n_tokens, bool logits, int32_t token, int32_t pos) {
   PArgs A = E->pargs;
   A.n_tokens = n_tokens;
   A.do_logits = logits ? 1 : 0;
+  A.token0 = token;
+  A.pos0 = pos;
   void* args[] = {&A};
   const void* fn = A.trace ? (const void*)k_decode_persistent<true> : (const void*)k_decode_persistent<false>;
   LE_CK(cudaLaunchCooperativeKernel(fn, dim3(E->p_grid), dim3(kPThreads), args,
@@ -1225,8 +1231,11 @@ static bool init_device(Engine* E, const uint8_t* base, const ParsedFile& P) {
   LE_CK(cudaMalloc(&E->red, 2048 * 4));
   LE_CK(cudaMalloc(&E->d_misc, 16 * 4));
   LE_CK(cudaMalloc(&E->part, B * E->lm_grid * sizeof(ArgmaxPart)));
-  LE_CK(cudaMalloc(&E->am_result, B * 4));
-  LE_CK(cudaMemsetAsync(E->am_result, 0, B * 4, E->stream));
+  // the persistent kernel's control words and the greedy results in one allocation, am_result
+  // right after PCtrl: greedy() reads the error words and am_result[0] with one copy
+  LE_CK(cudaMalloc(&E->ctrl_block, sizeof(PCtrl) + B * 4));
+  LE_CK(cudaMemsetAsync(E->ctrl_block, 0, sizeof(PCtrl) + B * 4, E->stream));
+  E->am_result = reinterpret_cast<int32_t*>(E->ctrl_block + sizeof(PCtrl));
   LE_CK(cudaMalloc(&E->token_log, (size_t)LE_MAX_SEQ_LEN * 4));
   LE_CK(cudaMalloc(&E->d_params, B * sizeof(StepParams)));
   LE_CK(cudaMemsetAsync(E->d_params, 0, B * sizeof(StepParams), E->stream));
@@ -1259,7 +1268,7 @@ static void destroy(Engine* E) {
   for (auto& g : E->tc_graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
   if (E->g_gen) cudaGraphExecDestroy(E->g_gen);
   for (auto& ev : E->ring_ev) if (ev) cudaEventDestroy(ev);
-  void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged, E->d_ctrl};
+  void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged};
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
   void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_qkv, E->t_gu, E->t_part,
@@ -1269,7 +1278,7 @@ static void destroy(Engine* E) {
   if (E->h_idx) cudaFreeHost(E->h_idx);
   if (E->idx_ev) cudaEventDestroy(E->idx_ev);
   void* dev_ptrs[] = {E->arena, E->rope_cos, E->rope_sin, E->kcache, E->vcache, E->x, E->qkv, E->attn,
-                      E->act, E->logits, E->emb, E->red, E->d_misc, E->part, E->am_result, E->token_log, E->d_params};
+                      E->act, E->logits, E->emb, E->red, E->d_misc, E->part, E->ctrl_block, E->token_log, E->d_params};
   for (void* p : dev_ptrs) if (p) cudaFree(p);
   if (E->h_ring) cudaFreeHost(E->h_ring);
   if (E->h_logits) cudaFreeHost(E->h_logits);
@@ -1559,13 +1568,16 @@ static bool queue_params(Engine* E, int32_t token, int32_t pos) {
 static bool forward_token(Engine* E, int32_t token, size_t pos, bool logits) {
   if (pos >= (size_t)E->max_seq) return true;  // silent no-op, src/llama_engine.cpp:936
   if (token < 0 || token >= (int32_t)E->vocab) token = 0;  // :937
-  if (!queue_params(E, token, (int32_t)pos)) return false;
-  if (E->tp_world > 1) {
-    LE_CK(cudaGraphLaunch(E->tp_g[logits ? 1 : 0], E->stream));
-  } else if (E->persist) {
-    if (!launch_persistent(E, 1, logits)) return false;
+  if (E->persist) {
+    E->last_pos = (int32_t)pos;
+    if (!launch_persistent(E, 1, logits, token, (int32_t)pos)) return false;
   } else {
-    LE_CK(cudaGraphLaunch(E->g_fwd[logits ? 1 : 0], E->stream));
+    if (!queue_params(E, token, (int32_t)pos)) return false;
+    if (E->tp_world > 1) {
+      LE_CK(cudaGraphLaunch(E->tp_g[logits ? 1 : 0], E->stream));
+    } else {
+      LE_CK(cudaGraphLaunch(E->g_fwd[logits ? 1 : 0], E->stream));
+    }
   }
   if (logits) {
     E->logits_on_host_fresh = false;
@@ -1582,6 +1594,18 @@ static bool greedy(Engine* E, int32_t* out) {
     k_argmax_finish<<<1, 1024, 0, E->stream>>>(E->part, parts, E->am_result, E->d_params, E->token_log, 0);
     LE_CK(cudaGetLastError());
     E->argmax_valid = true;
+  }
+  if (E->persist && !(E->tc && E->tc_dirty)) {
+    // one copy for the persistent kernel's error words and am_result[0], which follows PCtrl
+    constexpr size_t off = offsetof(PCtrl, error), bytes = sizeof(PCtrl) + 4 - off;
+    static_assert(bytes % 4 == 0 && offsetof(PCtrl, err_where) == off + 4, "PCtrl layout");
+    LE_CK(cudaMemcpyAsync(E->h_small, E->ctrl_block + off, bytes, cudaMemcpyDeviceToHost, E->stream));
+    LE_CK(cudaStreamSynchronize(E->stream));
+    E->h_err[0] = (uint32_t)E->h_small[0];
+    E->h_err[1] = (uint32_t)E->h_small[1];
+    if (!check_status(E)) return false;
+    *out = E->h_small[bytes / 4 - 1];
+    return true;
   }
   LE_CK(cudaMemcpyAsync(E->h_small, E->am_result, 4, cudaMemcpyDeviceToHost, E->stream));
   if (!enqueue_status(E)) return false;
@@ -1772,7 +1796,7 @@ LE_API int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_tok
     for (int32_t i = 0; i < n_steps; ++i)
       if (cudaGraphLaunch(E->tp_g[2], E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
   } else if (E->persist) {
-    if (!launch_persistent(E, n_steps, true)) return -1;
+    if (!launch_persistent(E, n_steps, true, first_token, (int32_t)start_pos)) return -1;
   } else {
     for (int32_t i = 0; i < n_steps; ++i)
       if (cudaGraphLaunch(E->g_gen, E->stream) != cudaSuccess) { E->err = "graph launch failed"; return -1; }
@@ -2001,7 +2025,7 @@ LE_API int llama_engine_profile_phase(llama_engine_t engine, const char* phase, 
   cudaEventRecord(a, E->stream);
   for (int i = 0; i < iters; ++i) {
     if (step) {
-      if (E->persist) launch_persistent(E, 1, true);
+      if (E->persist) launch_persistent(E, 1, true, 0, std::min<int32_t>(E->last_pos, E->max_seq - 1));
       else cudaGraphLaunch(E->g_fwd[1], E->stream);
     }
     else enqueue_phase(E, B, ph, (uint32_t)(i % E->layers), E->stream);

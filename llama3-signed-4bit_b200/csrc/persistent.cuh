@@ -113,7 +113,6 @@ struct PArgs {
   float* kcache;    // slot 0: [layers][max_seq][kv_dim]
   float* vcache;
   PCtrl* ctrl;
-  const StepParams* prm;
   int32_t* token_log;
   int32_t* am_result;
   unsigned long long lm_rec_base;  // record offset of lm_head tile 0 (embedding lookup)
@@ -121,6 +120,7 @@ struct PArgs {
   int layers, dim, ffn, vocab, heads, kv_heads, max_seq;
   int n_lm_ctas;
   int n_tokens, do_logits;
+  int token0, pos0;  // the first step's token id and position (later steps feed back the greedy id)
   int expire_where;  // test only: nonzero makes CTA 0 wait on PCtrl::never with this code
   unsigned long long* trace;  // optional: per CTA kTraceCap (time, tag) pairs, first token only
 };
@@ -828,8 +828,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
   S.bsum = reinterpret_cast<float*>(image + 32768);
   S.escl = S.bsum + 64;
   S.red = S.escl + 64;
-  int token = A.prm->token;
-  const int pos0 = A.prm->pos;
+  int token = A.token0;
+  const int pos0 = A.pos0;
   const int L = A.layers;
   int ntr = 0;
 
