@@ -146,8 +146,8 @@ struct TcLayer {
   TcMat qkv, o, gu, d;
 };
 constexpr int kTcMaxSplits = 8;
-constexpr int kTcPairRows = 1024;  // steps of at least this many rows run two-tile GEMM units
-// Two-tile GEMM units for large steps, on unless $LLAMA_B200_TC_PAIR is "0" (read once).
+// Two-tile GEMM units where they are estimated faster (tc_plan), on unless $LLAMA_B200_TC_PAIR is
+// "0" (read once).
 static bool tc_pair_enabled() {
   static const bool on = [] {
     const char* v = getenv("LLAMA_B200_TC_PAIR");
@@ -847,21 +847,52 @@ static bool init_tc(Engine* E) {
   return true;
 }
 
-// Number of K splits for a GEMM whose tiles x token tiles alone would leave SMs idle.
-static int tc_splits(const Engine* E, const TcMat& W, int tok_tiles) {
-  const int base = W.tiles * tok_tiles;
-  if (base >= E->num_sms) {
+// Number of K splits for a GEMM whose tiles x token groups alone would leave SMs idle.
+static int tc_splits(int num_sms, int tiles, int kb, int tok_groups) {
+  const int base = tiles * tok_groups;
+  if (base >= num_sms) {
     // enough units for every SM: split K in two only for long K (the down projection), where the
     // fuller last wave outweighs the extra partial plane (units per wave-slot: busy fraction)
     auto busy = [&](int s) {
-      const int u = base * s, waves = (u + E->num_sms - 1) / E->num_sms;
-      return (double)u / (double)(waves * E->num_sms);
+      const int u = base * s, waves = (u + num_sms - 1) / num_sms;
+      return (double)u / (double)(waves * num_sms);
     };
-    return (W.kb >= 32 && busy(2) > busy(1) + 0.05) ? 2 : 1;
+    return (kb >= 32 && busy(2) > busy(1) + 0.05) ? 2 : 1;
   }
-  int s = std::min(kTcMaxSplits, E->num_sms / base);
-  s = std::min(s, std::max(1, W.kb / 2));
+  int s = std::min(kTcMaxSplits, num_sms / base);
+  s = std::min(s, std::max(1, kb / 2));
   return std::max(1, s);
+}
+
+// Unit form and K splits of one tensor-core GEMM launch: P = 1 (64-token units) or 2 (128-token
+// units over two image tiles), whichever gives the shorter estimate = K blocks of the busiest CTA
+// x the form's block period (768 and 1056 ns, measured by the per-block pipeline trace at 64 and
+// 128 tokens).  Two-tile units halve the issuer's cost per token but also the unit count, so small
+// steps keep one-tile units; one image tile cannot pair.  splits_req > 0 fixes the splits.
+struct TcPlan {
+  int P = 1, groups = 1, splits = 1, kb_split = 1;
+};
+static TcPlan tc_plan(int num_sms, int tiles, int kb, int img_tiles, int splits_req) {
+  static constexpr double kBlockNs[3] = {0.0, 768.0, 1056.0};
+  TcPlan best;
+  double best_ns = 0.0;
+  for (int P = 1; P <= 2; ++P) {
+    if (P == 2 && (img_tiles < 2 || !tc_pair_enabled())) continue;
+    TcPlan c;
+    c.P = P;
+    c.groups = (img_tiles + P - 1) / P;
+    const int want = splits_req > 0 ? splits_req : tc_splits(num_sms, tiles, kb, c.groups);
+    c.kb_split = (kb + want - 1) / want;
+    c.splits = (kb + c.kb_split - 1) / c.kb_split;
+    const long long units = (long long)tiles * c.groups * c.splits;
+    const long long grid = std::min<long long>(units, num_sms);
+    const double ns = (double)((units + grid - 1) / grid) * c.kb_split * kBlockNs[P];
+    if (P == 1 || ns < best_ns) {
+      best = c;
+      best_ns = ns;
+    }
+  }
+  return best;
 }
 
 // Launch with programmatic stream serialisation: the kernel may be scheduled while the previous
@@ -883,21 +914,19 @@ static void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 // Launches one tensor-core GEMM over T token rows of `img`; returns the number of K splits used
-// (splits < 0: chosen for the shape).  Steps of at least kTcPairRows rows run units of two token
-// tiles (the issuer's per-block cost is then shared by 128 tokens); smaller steps keep one-tile
-// units, whose count fills more SMs.
+// (splits < 0: chosen for the shape; the unit form is chosen by tc_plan).
 static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int splits, tc::Args A) {
-  const int P = (T >= kTcPairRows && tc_pair_enabled()) ? 2 : 1;
   A.recs = W.recs;
   A.img = img;
   A.tiles = W.tiles;
   A.kb_total = W.kb;
   A.img_tiles = (T + tc::kTok - 1) / tc::kTok;
-  A.tok_tiles = (A.img_tiles + P - 1) / P;
-  if (splits < 0) splits = tc_splits(E, W, A.tok_tiles);
+  const TcPlan pl = tc_plan(E->num_sms, W.tiles, W.kb, A.img_tiles, splits);
+  const int P = pl.P;
+  A.tok_tiles = pl.groups;
   A.T = T;
-  A.kb_split = (W.kb + splits - 1) / splits;
-  A.splits = (W.kb + A.kb_split - 1) / A.kb_split;
+  A.kb_split = pl.kb_split;
+  A.splits = pl.splits;
   A.error = E->tc_err;
   A.wait_ns = E->tc_wait_ns;
   A.expire = E->tc_expire;
@@ -2258,8 +2287,9 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
                  cudaSuccess &&
              cudaFuncSetAttribute(k_tc_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<2>::kSmemBytes) ==
                  cudaSuccess;
-    // units of two token tiles from kTcPairRows rows, as in the engine's steps
-    const int P = (M >= kTcPairRows && tc_pair_enabled()) ? 2 : 1;
+    // the unit form the engine's steps would take for this shape (no K splits here)
+    const TcPlan pl = tc_plan(sms, tiles, kb, tok_tiles, 1);
+    const int P = pl.P;
     cudaMemsetAsync(recs, 0, rec_bytes, s);
     cudaMemsetAsync(img, 0, img_bytes, s);
     cudaMemsetAsync(err, 0, 16, s);
@@ -2272,7 +2302,7 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     A.tiles = tiles;
     A.kb_total = kb;
     A.img_tiles = tok_tiles;
-    A.tok_tiles = (tok_tiles + P - 1) / P;
+    A.tok_tiles = pl.groups;
     A.splits = 1;
     A.kb_split = kb;
     A.T = M;

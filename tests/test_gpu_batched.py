@@ -77,7 +77,7 @@ def _abs_scale(pkg, step, mn, N, K, X):
                                    (2048, 8192, 1024),  # a prefill chunk through the gate/up shape
                                    # two-tile units: an odd tile count (the last unit's second tile
                                    # repeats its first) and ragged rows over a long K
-                                   (2048, 2048, 1050), (8192, 384, 1100)])
+                                   (2048, 2048, 1050), (8192, 2048, 1100)])
 def test_tc_gemm_vs_oracle(pkg, bindings, oracle_lib, torch_cuda, K, N, M):
     torch = torch_cuda
     nib, step, mn = pkg.model_file.gen_matrix(N, K, seed=300 + K + N, tensor=3, uniform_codes=True)
