@@ -836,8 +836,8 @@ static bool init_tc(Engine* E) {
   LE_CK(cudaFuncSetAttribute(k_attn_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
   LE_CK(cudaFuncSetAttribute(k_attn_prefill_tc5, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes));
   int per_sm = 0, per_sm2 = 0;
-  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm<1>, tc::kThreads, Geo<1>::kSmemBytes));
-  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm2, k_tc_gemm<2>, tc::kThreads, Geo<2>::kSmemBytes));
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_tc_gemm<1>, Geo<1>::kThreads, Geo<1>::kSmemBytes));
+  LE_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm2, k_tc_gemm<2>, Geo<2>::kThreads, Geo<2>::kSmemBytes));
   if (std::min(per_sm, per_sm2) < 1) {
     E->err = "tensor-core GEMM declined: 0 resident CTAs per SM";
     return true;
@@ -932,10 +932,10 @@ static int tc_launch(Engine* E, const TcMat& W, const uint8_t* img, int T, int s
   A.expire = E->tc_expire;
   const int units = A.tiles * A.tok_tiles * A.splits;
   if (P == 2)
-    launch_pdl(tc::k_tc_gemm<2>, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::Geo<2>::kSmemBytes,
+    launch_pdl(tc::k_tc_gemm<2>, dim3(std::min(units, E->num_sms)), dim3(tc::Geo<2>::kThreads), tc::Geo<2>::kSmemBytes,
                E->stream, A);
   else
-    launch_pdl(tc::k_tc_gemm<1>, dim3(std::min(units, E->num_sms)), dim3(tc::kThreads), tc::Geo<1>::kSmemBytes,
+    launch_pdl(tc::k_tc_gemm<1>, dim3(std::min(units, E->num_sms)), dim3(tc::Geo<1>::kThreads), tc::Geo<1>::kSmemBytes,
                E->stream, A);
   return A.splits;
 }
@@ -2321,9 +2321,9 @@ LE_API int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, co
     }
     const int grid = std::min(tiles * A.tok_tiles, sms);
     if (P == 2)
-      k_tc_gemm<2><<<grid, tc::kThreads, Geo<2>::kSmemBytes, s>>>(A);
+      k_tc_gemm<2><<<grid, Geo<2>::kThreads, Geo<2>::kSmemBytes, s>>>(A);
     else
-      k_tc_gemm<1><<<grid, tc::kThreads, Geo<1>::kSmemBytes, s>>>(A);
+      k_tc_gemm<1><<<grid, Geo<1>::kThreads, Geo<1>::kSmemBytes, s>>>(A);
     if (trace) {
       std::vector<unsigned long long> h(trace_bytes / 8);
       if (cudaMemcpyAsync(h.data(), trace, trace_bytes, cudaMemcpyDeviceToHost, s) == cudaSuccess &&

@@ -12,7 +12,8 @@
 //     in the UMMA K-major 128-byte-swizzled layout, plus the tokens' block sums) and the tile's
 //     weight record (nibbles + scales) with two 1-D bulk copies into a 5-stage shared-memory
 //     ring, and prefetches the records of later blocks into L2;
-//   * warps 3..10 (dequantisers, two sets taking alternate blocks, thread = weight row) turn
+//   * warps 3..10 (dequantisers, two sets taking alternate blocks, thread = weight row; one set
+//     for two-tile units) turn
 //     each record's nibbles into bf16 codes q (exact: 0..15), write them into tensor memory
 //     (tcgen05.st) as the MMA's A operand, and pass the block's scales and block sums to the
 //     epilogue through a small side ring;
@@ -59,8 +60,6 @@ constexpr int kRecBytes = kNibBytes + kM * 4;
 constexpr int kAtom = kTok * 128;        // one 64-wide K slice of 64 token rows (bf16, swizzled)
 constexpr int kImgBytes = 4 * kAtom + kTok * 4;  // activation image of one (token tile, K block)
 constexpr int kOffXs = 4 * kAtom;        // image: hi0 | lo0 | hi1 | lo1 | xs
-constexpr int kWarps = 19;               // 0 producer, 1 MMA issuer, 2 idle, 3-10 dequantisers, 11-18 epilogue
-constexpr int kThreads = 32 * kWarps;
 constexpr int kBufsA = 4;                // tensor-memory buffers of A codes (64 columns each)
 constexpr int kBufsD = 2;                // accumulator buffers (128 columns)
 constexpr int kTmemCols = 512;
@@ -89,6 +88,15 @@ struct Geo {
   static constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
   static constexpr int kStages = P == 1 ? 5 : 3;
   static constexpr int kSide = P == 1 ? 8 : 3;  // side ring: per block the rows' scales and block sums
+  // Warps: 0 producer, 1 MMA issuer, 2 idle, then kDqSets sets of 4 dequantisers, then 8 epilogue
+  // warps.  One set converts a block in ~0.5 us: two sets taking alternate blocks keep up with the
+  // 0.77 us block period of one-tile units; one set suffices for the 1.06 us period of two-tile
+  // units, which then run 15 warps (128 registers a thread instead of 96: no spilled accumulators,
+  // and fewer warps beside the MMA issuer on its sub-partition).
+  static constexpr int kDqSets = P == 1 ? 2 : 1;
+  static constexpr int kEpiWarp0 = 3 + 4 * kDqSets;
+  static constexpr int kWarps = kEpiWarp0 + 8;
+  static constexpr int kThreads = 32 * kWarps;
   static constexpr int kSideBytes = kM * 4 + kUnitTok * 4;
   static constexpr int kNumBars = 2 * kStages + kBufsA + kBufsD + 2 * kSide + 1;
   // 1024 bytes of slack to align the dynamic base (the swizzled operands need 1024-byte atoms)
@@ -337,11 +345,12 @@ __device__ __forceinline__ int cta_blocks(const Args& A, int n_units) {
 
 // Warp roles: 0 = bulk-copy producer (one lane), 1 = tensor-memory owner and MMA issuer (one
 // lane), 2 = none (keeps the dequantiser and epilogue groups aligned to the lane quadrants),
-// 3..10 = dequantisers, 11..18 = epilogue.  A warp may only touch tensor-memory lanes 32 * (warp % 4) .. +31, so each group of
-// four covers the 128 rows once; the two dequantiser groups take alternate blocks, the two
-// epilogue groups the two halves of the token tile.
+// 3 .. kEpiWarp0 - 1 = dequantisers (one or two sets of four), the next 8 = epilogue.  A warp may
+// only touch tensor-memory lanes 32 * (warp % 4) .. +31, so each group of four covers the 128
+// rows once; two dequantiser sets take alternate blocks, the two epilogue groups the two halves
+// of the unit's tokens.
 template <int P>
-__global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
+__global__ void __launch_bounds__(Geo<P>::kThreads, 1) k_tc_gemm(Args A) {
   using Gm = Geo<P>;
   extern __shared__ __align__(1024) uint8_t tc_smem[];
   __shared__ uint32_t s_tmem;
@@ -487,12 +496,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     }
   } else if (warp == 2) {
     // no role
-  } else if (warp < 11) {
+  } else if (warp < Gm::kEpiWarp0) {
     // ---------------- dequantisers: nibbles -> bf16 codes in tensor memory ----------------
-    // two sets of four warps take alternate blocks (set h: blocks g with g % 2 == h), so one
-    // set's waits and tensor-memory store latency overlap the other's work; warp (q, h) converts
-    // rows 32q .. 32q+31 of its blocks
+    // with two sets of four warps, set h takes blocks g with g % 2 == h, so one set's waits and
+    // tensor-memory store latency overlap the other's work; warp (q, h) converts rows
+    // 32q .. 32q+31 of its blocks
     const int q = warp & 3, h = (warp - 3) >> 2;
+    const bool trace_warp = ((warp - 3) & 3) == 0;
     const int r = 32 * q + lane;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int sw = (r >> 1) & 3;
@@ -504,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
     // g - kBufsA's barrier would alias: the other set's block g - 1 reuses it and can complete
     // it again before this wait starts.
     constexpr int kFreeA = Gm::kStages < kBufsA ? Gm::kStages : kBufsA;
-    for (int g = h; g < nblk; g += 2) {
+    for (int g = h; g < nblk; g += Gm::kDqSets) {
       const int s = g % Gm::kStages, n = g / Gm::kStages, b = g % kBufsA;
       const int j = g % Gm::kSide, nj = g / Gm::kSide;
       // side slot j is free once the epilogue has read block g - kSide
@@ -513,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
            !warp_wait(A, &s_abort, bar_done(S, (g - kFreeA) % Gm::kStages), done_parity(S, g - kFreeA), 10)) ||
           (g >= Gm::kSide && !warp_wait(A, &s_abort, bar_sempty(S, j), (nj - 1) & 1, 11)))
         break;
-      if (warp == 3 || warp == 7) trace_ev(A, 2, g);
+      if (trace_warp) trace_ev(A, 2, g);
       const uint32_t st = S.base + s * Gm::kStageBytes;
       const uint32_t rec = st + Gm::kOffRec + 64 * r;
 #pragma unroll
@@ -555,12 +565,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
         mbar_arrive_n(bar_afull(S, b), 1);
         mbar_arrive_n(bar_sfull(S, j), 1);
       }
-      if (warp == 3 || warp == 7) trace_ev(A, 3, g);
+      if (trace_warp) trace_ev(A, 3, g);
     }
   } else {
     // ---------------- epilogue: per-block scales in fp32, unit results ----------------
     // warp (q, h): rows 32q .. 32q+31, the unit's tokens kHalf h .. kHalf h + kHalf - 1
-    const int q = warp & 3, h = (warp - 11) >> 2;
+    const int q = warp & 3, h = (warp - Gm::kEpiWarp0) >> 2;
     const int r = 32 * q + lane;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     constexpr int kHalf = Gm::kUnitTok / 2;
@@ -574,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       if (!warp_wait(A, &s_abort, bar_done(S, g % Gm::kStages), done_parity(S, g), 7) ||
           !warp_wait(A, &s_abort, bar_sfull(S, j), nj & 1, 12))
         break;
-      if (warp == 11) trace_ev(A, 4, g);
+      if (warp == Gm::kEpiWarp0) trace_ev(A, 4, g);
       tc_fence_after();
       const uint32_t sd = S.side + j * Gm::kSideBytes;
       const uint32_t sc = lds32(sd + 4 * r);
@@ -608,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_gemm(Args A) {
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_n(bar_sempty(S, j), 1);
-      if (warp == 11) trace_ev(A, 5, g);
+      if (warp == Gm::kEpiWarp0) trace_ev(A, 5, g);
       if (c.kb + 1 == c.U.kb1) {  // unit complete: store its rows
         int n = c.U.tile * kM + r;
         bool store = true;
