@@ -1004,7 +1004,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
     const int sq = tc_launch(E, Y.qkv, E->img_d, n, -1,
                              rows(E->t_qkv, dim + 2 * kvd, dim + 2 * kvd, qkv_stride));
     if (prefill_p0 >= 0 || !fold)
-      launch_pdl(k_rope_append, dim3(n, ((dim + kvd) / 2 + kvd + 255) / 256), dim3(256), 0, s, E->t_qkv, sq, qkv_stride,
+      launch_pdl(k_rope_append, dim3(n), dim3(256), 0, s, E->t_qkv, sq, qkv_stride,
                  dim, kvd, pos, slot, E->rope_cos, E->rope_sin, E->t_q, kc, vc, slot_stride);
     if (prefill_p0 >= 0) {
       const int p_last = prefill_p0 + n - 1;

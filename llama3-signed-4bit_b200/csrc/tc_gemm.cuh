@@ -819,8 +819,9 @@ __global__ void __launch_bounds__(256) k_tc_stage(float* __restrict__ x, int ldx
 // ---------------------------------------------------------------------------------------------
 // RoPE and KV append for token row t of a q | k | v GEMM output (src/llama_engine.cpp:953-956,
 // apply_rope :120-151 with the host-built table), summing its nsplit split-K planes first:
-// rotated q to q_out[t], rotated k and v into the cache row (slot[t], pos[t]).  Grid (tokens,
-// ceil((q_dim + kv_dim) / 2 + kv_dim) / 256)), one item per thread.
+// rotated q to q_out[t], rotated k and v into the cache row (slot[t], pos[t]).  One CTA of 256
+// threads per token row; a thread rotates kRopePer pairs at a time with all their loads issued
+// before any store, then copies v elements.
 // ---------------------------------------------------------------------------------------------
 // Sum of the nsplit planes in plane order; four loads in flight at a time.
 __device__ __forceinline__ float sum_planes(const float* p, int nsplit, size_t stride) {
@@ -836,6 +837,7 @@ __device__ __forceinline__ float sum_planes(const float* p, int nsplit, size_t s
   for (; s < nsplit; ++s) v += p[s * stride];
   return v;
 }
+constexpr int kRopePer = 5;  // (q_dim + kv_dim) / 2 = 1280 pairs per 2048 of dim: 5 per thread
 __global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ qkv, int nsplit, size_t split_stride,
                                                      int q_dim, int kv_dim, const int32_t* __restrict__ pos,
                                                      const int32_t* __restrict__ slot, const float* __restrict__ rope_cos,
@@ -847,29 +849,48 @@ __global__ void __launch_bounds__(256) k_rope_append(const float* __restrict__ q
   const float* row = qkv + (size_t)t * (q_dim + 2 * kv_dim);
   const size_t cache = (size_t)slot[t] * slot_stride + (size_t)p * kv_dim;
   const int npairs = (q_dim + kv_dim) / 2;  // rotated pairs (i, i + 32) of the q and k heads
-  // items 0 .. npairs-1 rotate a pair, npairs .. npairs+kv_dim-1 copy a v element; the CTAs of
-  // blockIdx.y split them
-  const int j = blockIdx.y * blockDim.x + threadIdx.x;
-  if (j >= npairs) {
-    const int e = j - npairs;
-    if (e < kv_dim) vc[cache + e] = sum_planes(row + q_dim + kv_dim + e, nsplit, split_stride);
-    return;
-  }
-  {
-    const int head = j >> 5, i = j & 31;
-    const int base = head * LE_HEAD_DIM + i;  // q heads first, then k heads (row offset q_dim)
-    const float c = rope_cos[p * 32 + i], s = rope_sin[p * 32 + i];
-    const float r0 = sum_planes(row + base, nsplit, split_stride);
-    const float r1 = sum_planes(row + base + 32, nsplit, split_stride);
-    const float o0 = __fsub_rn(__fmul_rn(r0, c), __fmul_rn(r1, s));
-    const float o1 = __fadd_rn(__fmul_rn(r0, s), __fmul_rn(r1, c));
-    if (base < q_dim) {
-      q_out[(size_t)t * q_dim + base] = o0;
-      q_out[(size_t)t * q_dim + base + 32] = o1;
-    } else {
-      kc[cache + base - q_dim] = o0;
-      kc[cache + base - q_dim + 32] = o1;
+  for (int j0 = threadIdx.x; j0 < npairs; j0 += kRopePer * 256) {
+    float r0[kRopePer], r1[kRopePer], c[kRopePer], sn[kRopePer];
+#pragma unroll
+    for (int k = 0; k < kRopePer; ++k) {
+      const int j = j0 + 256 * k;
+      if (j < npairs) {
+        const int i = j & 31, base = (j >> 5) * LE_HEAD_DIM + i;  // q heads first, then k heads
+        if (nsplit == 1) {
+          r0[k] = row[base];
+          r1[k] = row[base + 32];
+        } else {
+          r0[k] = sum_planes(row + base, nsplit, split_stride);
+          r1[k] = sum_planes(row + base + 32, nsplit, split_stride);
+        }
+        c[k] = rope_cos[p * 32 + i];
+        sn[k] = rope_sin[p * 32 + i];
+      }
     }
+#pragma unroll
+    for (int k = 0; k < kRopePer; ++k) {
+      const int j = j0 + 256 * k;
+      if (j < npairs) {
+        const int base = (j >> 5) * LE_HEAD_DIM + (j & 31);
+        const float o0 = __fsub_rn(__fmul_rn(r0[k], c[k]), __fmul_rn(r1[k], sn[k]));
+        const float o1 = __fadd_rn(__fmul_rn(r0[k], sn[k]), __fmul_rn(r1[k], c[k]));
+        if (base < q_dim) {
+          q_out[(size_t)t * q_dim + base] = o0;
+          q_out[(size_t)t * q_dim + base + 32] = o1;
+        } else {
+          kc[cache + base - q_dim] = o0;
+          kc[cache + base - q_dim + 32] = o1;
+        }
+      }
+    }
+  }
+  const float* vrow = row + q_dim + kv_dim;
+  for (int e0 = threadIdx.x; e0 < kv_dim; e0 += 2 * 256) {
+    const int e1 = e0 + 256;
+    const float v0 = sum_planes(vrow + e0, nsplit, split_stride);
+    const float v1 = e1 < kv_dim ? sum_planes(vrow + e1, nsplit, split_stride) : 0.0f;
+    vc[cache + e0] = v0;
+    if (e1 < kv_dim) vc[cache + e1] = v1;
   }
 }
 
