@@ -241,11 +241,12 @@ int llama_engine_check_schedule(int layers, int dim, int ffn_dim, int vocab_size
                                 int grid, char* err, int err_len);
 
 /* Test hook for the bounded device waits: sets the time bound of every wait of the persistent
- * kernel and of the tensor-core GEMM to wait_ns (0 restores the default of 2 s), and with
- * expire_code != 0 makes the next launches wait on a device word that nothing writes, so that
- * the wait runs out: the persistent kernel's CTA 0 at the start of a launch, the GEMM's MMA
- * issuer before its first block; expire_code = 20 instead expires only the prefill attention
- * kernel (its MMA-issuing thread, after the first K / V tile copies are in flight).  The launch
+ * kernel, the tensor-core GEMM and the prefill attention to wait_ns (0 restores the default of
+ * 2 s), and with expire_code != 0 makes the next launches wait on a device word that nothing
+ * writes, so that the wait runs out: the persistent kernel's CTA 0 at the start of a launch, the
+ * GEMM's MMA issuer before its first block; expire_code = 20 instead expires only the prefill
+ * attention kernel (its MMA-issuing thread, after the first K / V tile copies are in flight),
+ * and the GEMMs then keep the default bound, so that only the attention's wait runs out.  The launch
  * then drains and the next waiting call fails with the timeout reported; expire_code = 0 turns
  * that off again and clears the recorded error so the engine can be used again.  Returns 0, or
  * -1 for a NULL handle. */

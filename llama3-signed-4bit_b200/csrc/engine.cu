@@ -249,6 +249,7 @@ struct Engine {
   unsigned long long tc_wait_ns = kWaitNs;  // bound on the GEMM's waits (test hook)
   int tc_expire = 0;                        // test hook: the GEMM's issuer waits on nothing
   int attn_expire = 0;                      // test hook: the prefill attention's issuer waits on nothing
+  unsigned long long attn_wait_ns = kWaitNs;  // bound on the prefill attention's waits (test hook)
   // decode steps of the batched path replayed as CUDA graphs, one per (rows, logits rows,
   // attention splits); the rows' ids, positions and slots are read from t_idx
   struct TcGraph { int n, nlog, splits; bool fold; cudaGraphExec_t exec; };
@@ -1012,7 +1013,7 @@ static bool tc_step(Engine* E, int n, int lrow0, int nlog, int max_pos, int pref
                  E->kv_img, E->kv_img_tiles);
       launch_pdl(k_attn_prefill_tc5, dim3(E->kv_heads, (n + attn::kQ - 1) / attn::kQ), dim3(128),
                  (size_t)attn::kSmemBytes, s, E->t_q, dim, E->kv_img, E->kv_img_tiles, prefill_p0, n, E->t_attn,
-                 E->tc_err, E->tc_wait_ns, E->attn_expire);
+                 E->tc_err, E->attn_wait_ns, E->attn_expire);
     } else {
       // decode rows: RoPE and the KV append run inside the attention kernel
       // without position splits the attention kernel writes the o-proj input image itself
@@ -1981,7 +1982,11 @@ LE_API int llama_engine_debug_waits(llama_engine_t engine, unsigned long long wa
   const unsigned long long ns = wait_ns ? wait_ns : kWaitNs;
   E->pargs.wait_ns = ns;
   E->pargs.expire_where = expire_code;
-  E->tc_wait_ns = ns;
+  // expiring only the attention keeps the default bound on the GEMMs: with programmatic launches
+  // the next GEMM may already wait for the stalled attention's output, and its bounded waits
+  // would otherwise run out in the same millisecond and race the attention's error code
+  E->tc_wait_ns = expire_code == kExpireAttn ? kWaitNs : ns;
+  E->attn_wait_ns = ns;
   E->tc_expire = expire_code != 0 && expire_code != kExpireAttn ? 1 : 0;
   E->attn_expire = expire_code == kExpireAttn ? 1 : 0;
   // captured batched steps hold the old GEMM arguments
