@@ -4,16 +4,17 @@
 //
 //   y[t][n] = sum_b ( min[n][b] * xs[t][b]  +  step[n][b] * sum_{k in b} q[n][k] * x[t][k] )
 //
-// One CTA (19 warps, one per SM, persistent over work units) computes a tile of 128 weight rows
-// for up to 64 tokens over a range of 128-wide K blocks, as a pipeline over K blocks:
+// One CTA (one per SM, persistent over work units) computes a tile of 128 weight rows for a unit
+// of 64 tokens (or 128: two-tile units, Geo<2>) over a range of 128-wide K blocks, as a pipeline
+// over K blocks (described here for 64-token units; Geo<P> gives the two-tile differences):
 //
 //   * warp 0 (one lane) streams, per K block, the activation image of the token tile (the 64
 //     token rows as bf16 hi and lo parts, x = hi + lo, hi = bf16(x), lo = bf16(x - hi), already
 //     in the UMMA K-major 128-byte-swizzled layout, plus the tokens' block sums) and the tile's
 //     weight record (nibbles + scales) with two 1-D bulk copies into a 5-stage shared-memory
 //     ring, and prefetches the records of later blocks into L2;
-//   * warps 3..10 (dequantisers, two sets taking alternate blocks, thread = weight row; one set
-//     for two-tile units) turn
+//   * warps 3..10 (dequantisers, two sets taking alternate blocks, thread = weight row; one set,
+//     warps 3..6, for two-tile units) turn
 //     each record's nibbles into bf16 codes q (exact: 0..15), write them into tensor memory
 //     (tcgen05.st) as the MMA's A operand, and pass the block's scales and block sums to the
 //     epilogue through a small side ring;
@@ -22,7 +23,8 @@
 //     an fp32 accumulator D in tensor memory (one per K block): D[t] = sum_k q . x_hi[t],
 //     D[64 + t] = sum_k q . x_lo[t]; the MMAs' completion frees the stage, the A buffer and
 //     signals the accumulator;
-//   * warps 11..18 (epilogue, thread = weight row, 32 tokens each) read D back (tcgen05.ld) and
+//   * warps 11..18 (epilogue, thread = weight row, 32 tokens each; warps 7..14 with 64 tokens
+//     each in two-tile units) read D back (tcgen05.ld) and
 //     apply the block's scales in fp32: acc[t] += min * xs[t] + step * (D[t] + D[64 + t]) (the
 //     reference's factored form); at the end of a unit they store the rows (split-K partials,
 //     projections or logits).
