@@ -12,6 +12,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstddef>
 #include <cmath>
 #include <cstdio>
@@ -202,6 +203,10 @@ struct Engine {
   int32_t* h_small = nullptr; // pinned scratch [LE_MAX_SEQ_LEN]
   bool logits_on_host_fresh = false;   // slot-0 host mirror matches device
   bool argmax_valid = false;           // am_result[0] holds greedy of current device logits
+  bool argmax_persist = false;         // ... from the newest persistent launch (also in h_done)
+  uint32_t* h_done = nullptr;          // mapped pinned words the persistent kernel's last CTA writes
+  uint32_t persist_seq = 0;            // persistent launches so far
+  uint32_t persist_seq_logits = 0;     // the newest one with logits
   bool have_logits = false;
 
   // persistent token-step kernel (LLaMA-3.2-1B geometry: dim 2048, ffn 8192)
@@ -705,6 +710,15 @@ static bool init_persistent(Engine* E) {
   LE_CK(cudaMemset(E->d_tagged, 0, n_tagged * sizeof(unsigned long long)));  // tag 0 is never valid
   E->d_ctrl = reinterpret_cast<PCtrl*>(E->ctrl_block);  // am_result follows it (greedy())
   LE_CK(cudaMemset(E->d_ctrl, 0, sizeof(PCtrl)));
+  // mapped completion words (greedy()); without them sample() reads the result with a copy
+  uint32_t* d_done = nullptr;
+  if (cudaHostAlloc(&E->h_done, 64, cudaHostAllocMapped) == cudaSuccess) {
+    std::memset(E->h_done, 0, 64);
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&d_done), E->h_done, 0) != cudaSuccess) d_done = nullptr;
+  } else {
+    E->h_done = nullptr;
+  }
+  cudaGetLastError();  // a failed mapping only disables the fast path
   PArgs& A = E->pargs;
   A.arena = E->rec_arena;
   A.sched = E->d_sched; A.segs = E->d_segs; A.items = E->d_items; A.recs = E->d_recs;
@@ -725,11 +739,19 @@ static bool init_persistent(Engine* E) {
   A.n_lm_ctas = n_lm_ctas;
   A.n_tokens = 1; A.do_logits = 1;
   A.token0 = 0; A.pos0 = 0;
+  A.host_done = d_done; A.seq = 0;
   A.expire_where = 0;
   E->p_grid = G;
   LE_CK(cudaStreamSynchronize(E->stream));
   E->persist = true;
   return true;
+}
+
+// Every change of the greedy-result state goes through here: `persist` says that am_result[0]
+// (and the mapped h_done words) hold the greedy id of the newest persistent launch.
+static void set_argmax(Engine* E, bool valid, bool persist = false) {
+  E->argmax_valid = valid;
+  E->argmax_persist = valid && persist;
 }
 
 // One cooperative launch of n_tokens steps on slot 0 from (token, pos); the token and position
@@ -740,6 +762,8 @@ static bool launch_persistent(Engine* E, int n_tokens, bool logits, int32_t toke
   A.do_logits = logits ? 1 : 0;
   A.token0 = token;
   A.pos0 = pos;
+  A.seq = ++E->persist_seq;
+  if (logits) E->persist_seq_logits = A.seq;
   void* args[] = {&A};
   const void* fn = A.trace ? (const void*)k_decode_persistent<true> : (const void*)k_decode_persistent<false>;
   LE_CK(cudaLaunchCooperativeKernel(fn, dim3(E->p_grid), dim3(kPThreads), args,
@@ -1301,6 +1325,7 @@ static void destroy(Engine* E) {
   void* pdev[] = {E->d_trace, E->rec_arena, E->d_sched, E->d_segs, E->d_items, E->d_recs, (void*)E->d_norms, E->d_tagged};
   for (void* p : pdev) if (p) cudaFree(p);
   if (E->h_err) cudaFreeHost(E->h_err);
+  if (E->h_done) cudaFreeHost(E->h_done);
   void* tdev[] = {E->tc_arena, E->img_d, E->img_f, E->t_x, E->t_q, E->t_attn, E->t_qkv, E->t_gu, E->t_part,
                   E->t_idx, E->t_am, E->tc_err, E->t_attn_part, E->kv_img, E->sc_logits, E->sc_target, E->sc_lp,
                   E->sc_greedy};
@@ -1611,19 +1636,57 @@ static bool forward_token(Engine* E, int32_t token, size_t pos, bool logits) {
   }
   if (logits) {
     E->logits_on_host_fresh = false;
-    E->argmax_valid = true;
+    set_argmax(E, true, E->persist);
     E->have_logits = true;
   }
   return true;
 }
 
+// Waits for the newest persistent launch through the mapped completion words (the kernel's last
+// CTA writes them as it finishes) instead of a device-to-host copy and a stream wait.  Returns
+// false when that cannot be used (the stream drained without the words: the slow path reads the
+// result instead) and sets *failed on a CUDA error.
+static bool wait_done_words(Engine* E, bool* failed) {
+  volatile uint32_t* hd = E->h_done;
+  const uint32_t want = E->persist_seq;
+  for (uint32_t i = 1;; ++i) {
+    if (hd[3] == want) break;
+    if ((i & 255) == 0) {  // now and then: has the stream drained, or failed?
+      const cudaError_t q = cudaStreamQuery(E->stream);
+      if (q == cudaSuccess) {
+        if (hd[3] == want) break;
+        return false;
+      }
+      if (q != cudaErrorNotReady) {
+        E->err = cudaGetErrorString(q);
+        *failed = true;
+        return false;
+      }
+    }
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);  // the words before seq
+  return true;
+}
+
 static bool greedy(Engine* E, int32_t* out) {
+  if (E->argmax_valid && E->argmax_persist && E->h_done && E->persist_seq_logits == E->persist_seq &&
+      !(E->tc && E->tc_dirty)) {
+    bool failed = false;
+    if (wait_done_words(E, &failed)) {
+      E->h_err[0] = E->h_done[0];
+      E->h_err[1] = E->h_done[1];
+      if (!check_status(E)) return false;
+      *out = (int32_t)E->h_done[2];
+      return true;
+    }
+    if (failed) return false;
+  }
   if (!E->argmax_valid) {
     const int parts = std::min<int>(E->num_sms * 2, (E->vocab + kThreads - 1) / kThreads);
     k_argmax_rows<<<parts, kThreads, 0, E->stream>>>(E->logits, E->vocab, E->part);
     k_argmax_finish<<<1, 1024, 0, E->stream>>>(E->part, parts, E->am_result, E->d_params, E->token_log, 0);
     LE_CK(cudaGetLastError());
-    E->argmax_valid = true;
+    set_argmax(E, true);
   }
   if (E->persist && !(E->tc && E->tc_dirty)) {
     // one copy for the persistent kernel's error words and am_result[0], which follows PCtrl
@@ -1739,7 +1802,7 @@ LE_API int llama_engine_prefill(llama_engine_t engine, const int32_t* token_ids,
     if (!tc_prefill(E, token_ids, n, start_pos, last)) return -1;
     if (last) {
       E->logits_on_host_fresh = false;
-      E->argmax_valid = true;
+      set_argmax(E, true);
       E->have_logits = true;
     }
     return 0;
@@ -1837,7 +1900,7 @@ LE_API int llama_engine_generate_greedy(llama_engine_t engine, int32_t first_tok
   if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
   if (!persistent_ok(E)) return -1;
   E->logits_on_host_fresh = false;
-  E->argmax_valid = true;
+  set_argmax(E, true);
   E->have_logits = true;
   return 0;
 }
@@ -1879,7 +1942,7 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
     if (!tc_step_graph(E, n, compute_logits ? n : 0, *std::max_element(positions, positions + n), distinct))
       return -1;
     E->logits_on_host_fresh = false;
-    if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
+    if (compute_logits) { set_argmax(E, true); E->have_logits = true; }
     return 0;
   }
   std::vector<StepParams> hp(n);
@@ -1894,7 +1957,7 @@ LE_API int llama_engine_forward_batch(llama_engine_t engine, const int32_t* toke
   cudaError_t ce = cudaStreamSynchronize(E->stream);  // hp goes out of scope
   if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
   E->logits_on_host_fresh = false;
-  if (compute_logits) { E->argmax_valid = true; E->have_logits = true; }
+  if (compute_logits) { set_argmax(E, true); E->have_logits = true; }
   return 0;
 }
 
@@ -2073,7 +2136,7 @@ LE_API int llama_engine_profile_phase(llama_engine_t engine, const char* phase, 
   if (ce != cudaSuccess) { E->err = cudaGetErrorString(ce); return -1; }
   *avg_ms = ms / (float)iters;
   E->logits_on_host_fresh = false;
-  E->argmax_valid = false;
+  set_argmax(E, false);
   return 0;
 }
 
@@ -2163,7 +2226,7 @@ LE_API int llama_engine_score_tokens(llama_engine_t engine, const int32_t* token
   }
   if (!persistent_ok(E)) return -1;
   E->logits_on_host_fresh = false;
-  E->argmax_valid = false;
+  set_argmax(E, false);
   E->have_logits = true;
   return 0;
 }

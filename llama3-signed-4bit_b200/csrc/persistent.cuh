@@ -121,6 +121,10 @@ struct PArgs {
   int n_lm_ctas;
   int n_tokens, do_logits;
   int token0, pos0;  // the first step's token id and position (later steps feed back the greedy id)
+  // optional mapped host words, written by the last CTA to finish: error, err_where, greedy id
+  // (with logits), then `seq` (after a system-scope fence) so that the host can wait on it
+  uint32_t* host_done;
+  uint32_t seq;
   int expire_where;  // test only: nonzero makes CTA 0 wait on PCtrl::never with this code
   unsigned long long* trace;  // optional: per CTA kTraceCap (time, tag) pairs, first token only
 };
@@ -1053,6 +1057,14 @@ __global__ void __launch_bounds__(kPThreads, 1) k_decode_persistent(const __grid
       A.ctrl->lm_seq = lm_seq + (A.do_logits ? (uint32_t)A.n_tokens : 0u);
       A.ctrl->done_ctas = 0;
       __threadfence();
+      if (A.host_done) {
+        volatile uint32_t* hd = A.host_done;
+        hd[0] = *reinterpret_cast<volatile uint32_t*>(&A.ctrl->error);
+        hd[1] = *reinterpret_cast<volatile uint32_t*>(&A.ctrl->err_where);
+        hd[2] = (uint32_t)*reinterpret_cast<volatile int32_t*>(A.am_result);
+        __threadfence_system();
+        hd[3] = A.seq;
+      }
     }
   }
 }
