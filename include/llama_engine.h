@@ -154,6 +154,15 @@ int llama_b128_gemv(const uint8_t* nibbles, const uint16_t* step_bf16, const uin
 int llama_b128_gemm(const uint8_t* nibbles, const uint16_t* step_bf16, const uint16_t* min_bf16,
                     int N, int K, const float* x, int M, float* y, void* stream);
 
+/* Host-side planner of the tensor-core GEMM's work units (no device work; extension with no
+ * counterpart in the reference, which has no tensor-core path): for a GEMM of `tiles` 128-row
+ * weight tiles, `kb` 128-wide K blocks and `img_tiles` 64-token activation tiles on `num_sms` SMs,
+ * writes out[0] = unit form (1: 64-token units, 2: 128-token units over two tiles), out[1] =
+ * token groups (units along the tokens), out[2] = K splits, out[3] = K blocks per split.
+ * splits_req > 0 fixes the splits (the gate-up and lm_head GEMMs use 1).  The batched steps and
+ * llama_b128_gemm launch what this returns.  Returns 0, or -1 for arguments out of range. */
+int llama_b128_gemm_plan(int num_sms, int tiles, int kb, int img_tiles, int splits_req, int32_t* out);
+
 /* Log-likelihood of a token run, for scoring consumers such as the reference's lm-eval adapter
  * (tests/lm_eval_adapter.py:111-229, which calls forward_token + get_logits per token and forms
  * log_softmax on the host).  Runs tokens[0..n) through slot 0 at positions start_pos.. (in

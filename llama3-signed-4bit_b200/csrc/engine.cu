@@ -2037,6 +2037,16 @@ LE_API int llama_engine_check_schedule(int layers, int dim, int ffn_dim, int voc
   return ok ? 0 : -1;
 }
 
+LE_API int llama_b128_gemm_plan(int num_sms, int tiles, int kb, int img_tiles, int splits_req, int32_t* out) {
+  if (!out || num_sms < 1 || num_sms > 4096 || tiles < 1 || kb < 1 || img_tiles < 1 || splits_req > kb) return -1;
+  const TcPlan pl = tc_plan(num_sms, tiles, kb, img_tiles, splits_req);
+  out[0] = pl.P;
+  out[1] = pl.groups;
+  out[2] = pl.splits;
+  out[3] = pl.kb_split;
+  return 0;
+}
+
 LE_API int llama_engine_debug_waits(llama_engine_t engine, unsigned long long wait_ns, int expire_code) {
   if (!engine) return -1;
   Engine* E = H(engine);

@@ -95,6 +95,8 @@ class LlamaEngineBindings:
         lib.llama_b128_gemv.restype = ctypes.c_int
         lib.llama_b128_gemm.argtypes = [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P]
         lib.llama_b128_gemm.restype = ctypes.c_int
+        lib.llama_b128_gemm_plan.argtypes = [ctypes.c_int] * 5 + [_I32P]
+        lib.llama_b128_gemm_plan.restype = ctypes.c_int
         lib.llama_b128_argmax_noalloc.argtypes = [_P, ctypes.c_int, _P, _P]
         lib.llama_b128_argmax_noalloc.restype = ctypes.c_int
         lib.llama_engine_set_rope_scaling.argtypes = [_P, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int]

@@ -112,3 +112,57 @@ def test_persistent_schedule_rejects_bad_geometry(bindings):
     assert bindings.lib.llama_engine_check_schedule(16, 4096, 8192, 128256, 32, 8, 148, err, 256) == -1
     assert err.value
     assert bindings.lib.llama_engine_check_schedule(16, 2048, 8192, 128256, 32, 8, 0, None, 0) == -1
+
+
+def _plan(bindings, sms, tiles, kb, img_tiles, splits_req):
+    out = (ctypes.c_int32 * 4)()
+    assert bindings.lib.llama_b128_gemm_plan(sms, tiles, kb, img_tiles, splits_req, out) == 0
+    return tuple(out)
+
+
+# LLaMA-3.2-1B batched-path matrices: (128-row tiles, K blocks, fixed splits or -1)
+_MATS = {"qkv": (24, 16, -1), "o": (16, 16, -1), "gate_up": (128, 16, 1), "down": (16, 64, -1),
+         "lm_head": (1002, 16, 1)}
+
+
+@pytest.mark.parametrize("rows", [1, 64, 128, 192, 256, 512, 1024, 2048])
+@pytest.mark.parametrize("mat", sorted(_MATS))
+def test_gemm_plan_covers_the_work(bindings, rows, mat):
+    """Whatever form the planner picks, its units cover every token tile and every K block once."""
+    tiles, kb, req = _MATS[mat]
+    img = (rows + 63) // 64
+    p, groups, splits, kbs = _plan(bindings, 148, tiles, kb, img, req)
+    assert p in (1, 2) and (p == 1 or img >= 2)
+    assert groups == (img + p - 1) // p
+    assert splits * kbs >= kb and (splits - 1) * kbs < kb
+    if req > 0:
+        assert splits == req
+
+
+def test_gemm_plan_choices(bindings):
+    """The forms the engine's steps take: one image tile cannot pair (batch-64 decode); prefill
+    chunks and box-scale steps pair tiles; 192 rows keep one-tile q|k|v units (the estimate is
+    slightly shorter)."""
+    P = lambda mat, rows: _plan(bindings, 148, *_MATS[mat][:2], (rows + 63) // 64, _MATS[mat][2])
+    for mat in _MATS:
+        assert P(mat, 64)[0] == 1
+        assert P(mat, 2048) == (2, 16, 1, _MATS[mat][1])
+    assert P("qkv", 64) == (1, 1, 6, 3)
+    assert P("qkv", 256) == (2, 2, 3, 6)
+    assert P("down", 256) == (2, 2, 4, 16)
+    assert P("qkv", 192)[0] == 1
+    # the isolated GEMM's test shapes (splits fixed at 1)
+    assert _plan(bindings, 148, 64, 16, 16, 1)[0] == 2    # 1024 x 8192 x 2048
+    assert _plan(bindings, 148, 16, 16, 17, 1)[:2] == (2, 9)  # 1050 rows: odd tile count
+    assert _plan(bindings, 148, 16, 64, 18, 1)[0] == 2    # 1100 x 2048 x 8192
+    assert _plan(bindings, 148, 3, 64, 3, 1)[0] == 1      # 130 x 384 x 8192
+
+
+def test_gemm_plan_rejects_bad_args(bindings):
+    out = (ctypes.c_int32 * 4)()
+    lib = bindings.lib
+    assert lib.llama_b128_gemm_plan(0, 16, 16, 1, -1, out) == -1
+    assert lib.llama_b128_gemm_plan(148, 0, 16, 1, -1, out) == -1
+    assert lib.llama_b128_gemm_plan(148, 16, 16, 0, -1, out) == -1
+    assert lib.llama_b128_gemm_plan(148, 16, 16, 1, 17, out) == -1
+    assert lib.llama_b128_gemm_plan(148, 16, 16, 1, -1, None) == -1
