@@ -128,7 +128,7 @@ GEMM_BLOCKS = 256
 GEMM_INTERVALS = {
     "issuer: barrier tests (8 -> 9)": (8, 9, 0),
     "issuer: tests -> inputs ready (9 -> 1)": (9, 1, 0),
-    "issuer: 8 MMAs issued (1 -> 6)": (1, 6, 0),
+    "issuer: the block's MMAs issued (1 -> 6)": (1, 6, 0),  # 8 (64-token units) or 16 (128-token)
     "issuer: commit (6 -> 7)": (6, 7, 0),
     "issuer: to next block (7 -> 8 of g+1)": (7, 8, 1),
     "issuer: block period (8 -> 8 of g+1)": (8, 8, 1),

@@ -50,6 +50,6 @@ def test_gemm_pipeline_intervals(pkg, tmp_path):
     assert out["blocks"] == nb
     assert out["issuer: block period (8 -> 8 of g+1)"] == 700
     assert out["issuer: barrier tests (8 -> 9)"] == 60
-    assert out["issuer: 8 MMAs issued (1 -> 6)"] == 320
+    assert out["issuer: the block's MMAs issued (1 -> 6)"] == 320
     assert out["epilogue per block (4 -> 5)"] == 350
     assert out["slack: epilogue done -> inputs of g+2 ready (5 -> 1 of g+2)"] == 200 + 1400 - 1150
